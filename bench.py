@@ -1,0 +1,342 @@
+"""T3 decode benchmark.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (configs[0], the metric's batch-1 configuration): T3 Turbo GPT-2
+Medium (24 layers, d 1024, 16 heads, FFN 4096, V 6563), random-init weights
+quantized to Q4_0 (speech_head Q4_0 too, as convert --quant q4_0), batch 1,
+no CFG, a 150-position prompt (1 speaker row + 62 cond speech tokens + 86
+text ids + start token), temperature 0.8, top_k 1000, top_p 0.95,
+repetition penalty 1.2, std::mt19937 seed 0.  One bench step = one decode
+step (one speech token per stream): embedding, 24 layers, head, sampler.
+K defaults to 256 (the config's decode length).  Under torchrun every rank
+decodes its own utterance on its own GPU (independent utterances, no
+collective: weak scaling); the job time is the max over ranks.
+
+value: speech tokens/s with everything resident on the device (t3b_decode,
+timed with CUDA events on the context's stream).  e2e: the same decode driven
+through the per-step drop-in API (t3b_step -> logits to host -> t3b_sample
+with host logits -> token to host), i.e. chatterbox.cpp's eval_step +
+sample_next_token_ex call pattern, host copies included.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_TEXT = 86
+PARAMS = dict(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2)
+METRIC = "T3 speech tokens/s (batch-1 Q4_0 decode, % HBM roofline)"
+UNIT = "speech tokens/s"
+
+
+def algorithmic_bytes_per_step(hp, L_mean, weight_bytes):
+    """Bytes one decode step must move: every weight byte once plus the f16
+    K and V of L positions for every layer (98 304 B per position for T3),
+    plus the step's own K/V write and the logits."""
+    kv = 2 * hp["n_layer"] * hp["n_embd"] * 2
+    return weight_bytes + kv * (L_mean + 1) + hp["n_speech_vocab"] * 4
+
+
+def model_weight_bytes(t):
+    n = 0
+    for name, (ty, arr) in t.items():
+        if name in ("chatterbox/text_emb", "chatterbox/cond_spkr/w", "chatterbox/cond_spkr/b",
+                    "chatterbox/builtin/speaker_emb", "chatterbox/builtin/cond_prompt_speech_tokens",
+                    "model/wpe", "chatterbox/speech_emb"):
+            continue
+        n += np.asarray(arr).nbytes
+    # one speech_emb row (f16) and one wpe row (f32) per step
+    return n + 1024 * 2 + 1024 * 4
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.p = None
+        return self
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_reference(args, hp, t, text, label_impl):
+    """The reference's CPU path for this workload: chatterbox.cpp cannot be
+    built here (ggml absent), so the oracle's restatement of ggml's CPU
+    arithmetic (oracle/t3_oracle.cpp, ggml-like mode) runs the same
+    batch-1 decode on all host cores.  Bounded sample: as many decode steps
+    as fit in ~12 s (at least 4), after an untimed prefill."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    m = oracle.Model(hp, t, max_ctx=150 + max(args.steps, 64) + 8, gemv_mode=1, gelu_f16=1, kv_f16=0)
+    P, lg = m.prompt(text)
+    words = oracle.mt19937_words(0, 0, 2 * (args.steps + 2))
+    hist = []
+    tok, _ = oracle.sample(lg, PARAMS, words[0], words[1])
+    hist.append(tok)
+    n, t0 = 0, time.perf_counter()
+    budget = float(os.environ.get("T3B_CPU_SECONDS", "12"))
+    while n < args.steps:
+        lg = m.step(P + n, tok)
+        tok, _ = oracle.sample(lg, PARAMS, words[2 * n + 2], words[2 * n + 3], hist=np.array(hist, np.int32))
+        hist.append(tok)
+        n += 1
+        if n >= 4 and time.perf_counter() - t0 > budget:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} decode steps of the batch-1 Q4_0 workload after a 150-position prefill "
+                      f"(oracle restatement of ggml's CPU path, OpenMP x{cores}); {dt:.2f} s"}
+
+
+def make_model(pkg, seed=0):
+    hp = dict(pkg.t3_gguf.T3_TURBO)
+    hp, t = pkg.t3_gguf.random_t3(hp, quant="q4_0", seed=seed)
+    return hp, t
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    hp, t = make_model(pkg)
+    text = np.random.default_rng(0).integers(0, 50257, PROMPT_TEXT).astype(np.int32)
+    cb = cpu_reference(args, hp, t, text, "reference")
+    line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x q8_0 (int dot, f32 accumulate)",
+            "data": "synthetic (random-init T3 Q4_0 weights, seeded prompt)", "impl": "reference",
+            "config": config_block(args), "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(args):
+    return {"workload": "configs[0]: T3 Turbo batch-1 Q4_0 decode, 150-position prompt, "
+                        f"{args.steps} decode steps per rank, temp 0.8 / top_k 1000 / top_p 0.95 / penalty 1.2, "
+                        "mt19937 seed 0",
+            "model": "T3 Turbo GPT-2 Medium 24x1024, 16 heads, FFN 4096, V 6563 (random init)",
+            "global_batch": args.gpus, "seq_len": 150 + args.steps, "parallelism": f"replicas x{args.gpus}",
+            "l2": "inputs larger than L2 (175 MB of weights streamed per step)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(args.warmup, 3)
+
+    ws, rank, local = dist_env()
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    hp, t = make_model(pkg, seed=0)
+    wbytes = model_weight_bytes(t)
+    text = np.random.default_rng(rank).integers(0, 50257, PROMPT_TEXT).astype(np.int32)
+    m = pkg.T3Model(hp, t, device=local)
+    K, W = args.steps, args.warmup
+    m.alloc_streams(1, 150 + max(K, W) + 8)
+    params = pkg.SampleParams.make(**PARAMS)
+
+    # warm-up: a W-step utterance
+    m.prefill(0, text)
+    m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
+    m.decode([params], W, ignore_stop=True)
+    # timed: K decode steps from the prompt end (positions 151 .. 150+K)
+    P, _ = m.prefill(0, text)
+    m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        toks = m.decode([params], K, ignore_stop=True)[0]
+        dev_ms = m.last_device_ms()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t_dev = torch.tensor([dev_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t_dev, op=dist.ReduceOp.MAX)
+    ms = float(t_dev.item())
+    value = ws * K / (ms / 1000.0)
+    ms_per_step = ms / K
+
+    # e2e through the per-step drop-in API (host copies every step)
+    m.prefill(0, text)
+    m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
+    m.set_history(0, np.zeros(0, np.int32))
+    V = hp["n_speech_vocab"]
+    e2e_steps = min(K, 64)
+    tok = int(m.sample([params])[0])
+    host_logits = np.zeros((1, 1, V), np.float32)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        host_logits = m.step([tok])                         # eval_step: token H2D, logits D2H
+        tok = int(m.sample([params], logits=host_logits)[0])  # sample_next_token_ex on host logits
+    e2e_s = time.perf_counter() - t0
+    t_e2e = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    e2e = {"value": ws * e2e_steps / float(t_e2e.item()), "unit": UNIT,
+           "h2d_bytes_per_step": 4 + 4 + V * 4 + 24 + 4, "d2h_bytes_per_step": V * 4 + 4,
+           "steps": e2e_steps, "path": "t3b_step(host token) -> logits D2H -> t3b_sample(host logits) -> token D2H"}
+
+    # roofline of the dominant kernel: the decode step itself is the unit
+    # that streams every weight once; plus the GEMV alone (op-level)
+    peak, peak_kind = peaks()
+    L_mean = P + (K + 1) / 2.0
+    step_bytes = algorithmic_bytes_per_step(hp, L_mean, wbytes)
+    achieved = step_bytes / (ms_per_step / 1000.0) / 1e9
+    gemv = gemv_roofline(pkg, torch, peak)
+
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_0 x q8_0 (int dot, f32 accumulate)",
+            "data": "synthetic (random-init T3 Q4_0 weights, seeded prompt)",
+            "config": config_block(args),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "decode step (graph of embed + 24 layers + head + sampler)",
+                         "bytes_per_step": step_bytes, "mean_L": L_mean},
+            "gemv_roofline": gemv,
+            "e2e": e2e, "clocks": clk.summary(),
+            "gpu_launches": K * (1 + hp["n_layer"] * 9 + 2 + 2) + 1,
+            "tokens_head": [int(x) for x in toks[:8]]}
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference(args, hp, t, text, "port")
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def gemv_roofline(pkg, torch, peak):
+    """Average device time of the FC GEMV (1024 -> 4096, Q4_0, M = 1) through
+    t3b_op_gemv, CUDA events on the launching stream, weights > L2 by cycling
+    48 distinct weight copies (113 MB)."""
+    import ctypes as C
+    import gguf
+    L = pkg.lib()
+    K, N, copies = 1024, 4096, 48
+    w = (np.random.default_rng(1).standard_normal((N, K)) * 0.02).astype(np.float32)
+    q = np.ascontiguousarray(gguf.quants.quantize(w, gguf.GGMLQuantizationType.Q4_0))
+    rb = L.t3b_op_row_bytes(2, K)
+    wd = torch.empty((copies, N * rb), dtype=torch.uint8, device="cuda")
+    pkg.check(L.t3b_op_repack(2, q.ctypes.data, N, K, C.c_void_p(wd[0].data_ptr())))
+    wd[1:] = wd[0]
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    s = torch.cuda.current_stream()
+    sp = C.c_void_p(s.cuda_stream)
+    for i in range(8):
+        pkg.check(L.t3b_op_gemv(2, C.c_void_p(wd[i].data_ptr()), N, K, C.c_void_p(x.data_ptr()), 1, None, None, 1e-5,
+                                None, None, 0, C.c_void_p(y.data_ptr()), sp))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = copies * 4
+    e0.record(s)
+    for i in range(reps):
+        pkg.check(L.t3b_op_gemv(2, C.c_void_p(wd[i % copies].data_ptr()), N, K, C.c_void_p(x.data_ptr()), 1, None,
+                                None, 1e-5, None, None, 0, C.c_void_p(y.data_ptr()), sp))
+    e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    byts = N * rb + K * 4 + N * 4
+    ach = byts / (us * 1e-6) / 1e9
+    return {"kernel": "prep_act + gemv_q_kernel<Q4_0> (1024x4096, M=1)", "us_per_launch": us,
+            "bytes": byts, "achieved": ach, "peak": peak, "frac": ach / peak}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

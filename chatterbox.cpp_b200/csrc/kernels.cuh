@@ -1,0 +1,813 @@
+// kernels.cuh — multi-kernel T3 step: activation prep, dequant GEMV with
+// fused epilogues, decode attention, embeddings, fused sampler.
+//
+// Weight row layouts in HBM (written by t3b_op_repack / t3b_create from the
+// GGUF blocks, which are 18 B (Q4_0) / 34 B (Q8_0) and so never 16-byte
+// aligned):
+//   Q4_0: [K/2 bytes: block b's 16 nibble bytes at 16*b][K/32 f16 scales]
+//   Q8_0: [K bytes: block b's 32 int8 at 32*b]           [K/32 f16 scales]
+//   F16 : [K halves]
+// Every row is a multiple of 16 bytes, so a warp streams a row with 128-bit
+// loads and each lane owns whole 32-element blocks.
+#pragma once
+
+#include "common.cuh"
+#include "t3_expf.h"
+#include "../../include/t3b200.h"
+
+// ---------------------------------------------------------------------------
+// GEMV epilogue
+// ---------------------------------------------------------------------------
+enum { EPI_BIAS = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_QKV = 3 };
+
+struct GemvEpi {
+    int kind;
+    float * y; int ldy;
+    const float * bias;
+    const float * res; int ldres;
+    // EPI_QKV: append K/V (columns D..3D) to the f16 caches.  Cache row
+    // layout: [layer][K,V][head][max_ctx][64].
+    __half * kv; size_t row_elems; size_t layer_off; size_t v_off;
+    const int * row_of;  // activation row -> cache row
+    const int * pos;     // activation row -> position
+    const int * y_row;   // nullable: activation row -> output row of y
+    int max_ctx; int D;
+    unsigned * err;
+};
+
+__device__ __forceinline__ void epi_store(const GemvEpi & e, int m, int n, float acc) {
+    float v = e.bias ? __fadd_rn(acc, e.bias[n]) : acc;
+    if (e.kind == EPI_GELU) v = gelu_ggml(v);
+    else if (e.kind == EPI_RESID) v = __fadd_rn(v, e.res[(size_t) m * e.ldres + n]);
+    e.y[(size_t) (e.y_row ? e.y_row[m] : m) * e.ldy + n] = v;
+    if (e.kind == EPI_QKV && n >= e.D) {
+        const int which = n >= 2 * e.D ? 1 : 0;
+        const int rem = n - e.D - which * e.D;
+        const int h = rem >> 6, d = rem & 63;
+        const int p = e.pos[m];
+        if (p < 0 || p >= e.max_ctx) { atomicOr(e.err, T3B_DEVERR_POS); return; }
+        __half * base = e.kv + (size_t) e.row_of[m] * e.row_elems + e.layer_off + (which ? e.v_off : 0);
+        base[((size_t) h * e.max_ctx + p) * T3B_HD + d] = __float2half_rn(v);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Activation prep: optional LayerNorm, then Q8_0 re-quantisation (for
+// Q4_0/Q8_0 weights) or f16 rounding (for F16 weights) — what ggml's CPU
+// backend does to src1 before a quantised / f16 mul_mat.
+// One CTA of 256 threads per row; dynamic smem = K floats.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double block_sum_d(double v, double * red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    double r = lane < nw ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
+
+__global__ __launch_bounds__(256) void prep_act_kernel(
+        const float * __restrict__ x, int ldx, int K, const float * __restrict__ g,
+        const float * __restrict__ b, float eps, int qmode,
+        int8_t * __restrict__ xq, float * __restrict__ xd, int * __restrict__ xs,
+        __half * __restrict__ xh) {
+    extern __shared__ float row[];
+    __shared__ double redd[32];
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const float * xr = x + (size_t) m * ldx;
+    for (int i = tid; i < K; i += blockDim.x) row[i] = xr[i];
+    __syncthreads();
+    if (g) {
+        double s = 0.0;
+        for (int i = tid; i < K; i += blockDim.x) s += (double) row[i];
+        s = block_sum_d(s, redd);
+        const float mean = (float) (s / K);
+        double s2 = 0.0;
+        for (int i = tid; i < K; i += blockDim.x) {
+            const float v = __fsub_rn(row[i], mean);
+            s2 += (double) __fmul_rn(v, v);
+        }
+        s2 = block_sum_d(s2, redd);
+        const float var = (float) (s2 / K);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        for (int i = tid; i < K; i += blockDim.x) {
+            const float v = __fsub_rn(row[i], mean);
+            row[i] = __fadd_rn(__fmul_rn(__fmul_rn(v, scale), g[i]), b[i]);
+        }
+        __syncthreads();
+    }
+    if (qmode == 1) {
+        const int lane = tid & 31, w = tid >> 5, nw = blockDim.x >> 5;
+        for (int blk = w; blk < K / 32; blk += nw) {
+            const float v = row[blk * 32 + lane];
+            const float amax = warp_max(fabsf(v));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q = (int) roundf(__fmul_rn(v, id));
+            xq[(size_t) m * K + blk * 32 + lane] = (int8_t) q;
+            const int s = warp_sum_i(q);
+            if (lane == 0) {
+                xd[(size_t) m * (K / 32) + blk] = __half2float(__float2half_rn(d));
+                xs[(size_t) m * (K / 32) + blk] = s;
+            }
+        }
+    } else {
+        for (int i = tid; i < K; i += blockDim.x) xh[(size_t) m * K + i] = __float2half_rn(row[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Quantised GEMV (Q4_0 / Q8_0 weights x Q8_0 activations), integer dot per
+// 32-block with dp4a, float accumulation of sumi * d_w * d_x per block.
+// CTA = 8 warps; warp w owns RPW consecutive output rows; lanes stride the
+// K/32 blocks.  grid = (ceil(N / (8*RPW)), ceil(M / MT)).
+// dynamic smem: MT*K int8 + MT*(K/32)*(4+4).
+// ---------------------------------------------------------------------------
+template <int WT, int MT, int RPW>
+__global__ __launch_bounds__(256) void gemv_q_kernel(
+        const uint8_t * __restrict__ W, int N, int K, int rb,
+        const int8_t * __restrict__ xq, const float * __restrict__ xd, const int * __restrict__ xs,
+        int M, GemvEpi e) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int nb = K / 32;
+    int8_t * sq = (int8_t *) sm;
+    float * sd = (float *) (sm + MT * K);
+    int * ss = (int *) (sd + MT * nb);
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
+    const int tid = threadIdx.x;
+    for (int i = tid; i < mt * K / 16; i += blockDim.x)
+        ((uint4 *) sq)[i] = ((const uint4 *) (xq + (size_t) m0 * K))[i];
+    for (int i = tid; i < mt * nb; i += blockDim.x) {
+        sd[i] = xd[(size_t) m0 * nb + i];
+        ss[i] = xs[(size_t) m0 * nb + i];
+    }
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5;
+    const int row0 = (blockIdx.x * 8 + warp) * RPW;
+    float acc[RPW][MT];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[i][m] = 0.0f;
+
+    for (int b = lane; b < nb; b += 32) {
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            const int r = row0 + i;
+            if (r >= N) continue;
+            const uint8_t * wr = W + (size_t) r * rb;
+            if (WT == T3B_Q4_0) {
+                const uint4 qv = __ldg((const uint4 *) (wr + b * 16));
+                const float dw = __half2float(__ldg((const __half *) (wr + K / 2 + b * 2)));
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m >= mt) break;
+                    const int * xv = (const int *) (sq + m * K + b * 32);
+                    int si = 0;
+                    si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), xv[0], si);
+                    si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), xv[4], si);
+                    si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), xv[1], si);
+                    si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), xv[5], si);
+                    si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), xv[2], si);
+                    si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), xv[6], si);
+                    si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), xv[3], si);
+                    si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), xv[7], si);
+                    si -= 8 * ss[m * nb + b];
+                    acc[i][m] = __fadd_rn(acc[i][m], __fmul_rn(__fmul_rn((float) si, dw), sd[m * nb + b]));
+                }
+            } else {
+                const uint4 q0 = __ldg((const uint4 *) (wr + b * 32));
+                const uint4 q1 = __ldg((const uint4 *) (wr + b * 32 + 16));
+                const float dw = __half2float(__ldg((const __half *) (wr + K + b * 2)));
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m >= mt) break;
+                    const int * xv = (const int *) (sq + m * K + b * 32);
+                    int si = 0;
+                    si = __dp4a((int) q0.x, xv[0], si);
+                    si = __dp4a((int) q0.y, xv[1], si);
+                    si = __dp4a((int) q0.z, xv[2], si);
+                    si = __dp4a((int) q0.w, xv[3], si);
+                    si = __dp4a((int) q1.x, xv[4], si);
+                    si = __dp4a((int) q1.y, xv[5], si);
+                    si = __dp4a((int) q1.z, xv[6], si);
+                    si = __dp4a((int) q1.w, xv[7], si);
+                    acc[i][m] = __fadd_rn(acc[i][m], __fmul_rn(__fmul_rn((float) si, dw), sd[m * nb + b]));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int r = row0 + i;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float v = warp_sum(acc[i][m]);
+            if (lane == 0 && r < N && m < mt) epi_store(e, m0 + m, r, v);
+        }
+    }
+}
+
+// F16 weights x f16-rounded activations, f32 accumulation (each f16*f16
+// product is exact in f32).  Lanes stride 8-element chunks.
+template <int MT, int RPW>
+__global__ __launch_bounds__(256) void gemv_f16_kernel(
+        const __half * __restrict__ W, int N, int K, const __half * __restrict__ xh, int M, GemvEpi e) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __half * sx = (__half *) sm;
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
+    const int tid = threadIdx.x;
+    for (int i = tid; i < mt * K / 8; i += blockDim.x)
+        ((uint4 *) sx)[i] = ((const uint4 *) (xh + (size_t) m0 * K))[i];
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5;
+    const int row0 = (blockIdx.x * 8 + warp) * RPW;
+    float acc[RPW][MT];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[i][m] = 0.0f;
+    for (int c = lane; c < K / 8; c += 32) {
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            const int r = row0 + i;
+            if (r >= N) continue;
+            const uint4 wv = __ldg((const uint4 *) (W + (size_t) r * K + c * 8));
+            const __half2 * wp = (const __half2 *) &wv;
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m >= mt) break;
+                const uint4 xv = *(const uint4 *) (sx + m * K + c * 8);
+                const __half2 * xp = (const __half2 *) &xv;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 wf = __half22float2(wp[j]), xf = __half22float2(xp[j]);
+                    acc[i][m] = fmaf(wf.x, xf.x, acc[i][m]);
+                    acc[i][m] = fmaf(wf.y, xf.y, acc[i][m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int r = row0 + i;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float v = warp_sum(acc[i][m]);
+            if (lane == 0 && r < N && m < mt) epi_store(e, m0 + m, r, v);
+        }
+    }
+}
+
+// Plain f32 matvec for the speaker projection (cond_spkr: K = 256).
+__global__ void matvec_f32_kernel(const float * __restrict__ W, int N, int K, const float * __restrict__ x,
+                                  const float * __restrict__ b, float * __restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= N) return;
+    float acc = 0.0f;
+    for (int k = lane; k < K; k += 32) acc = fmaf(W[(size_t) r * K + k], x[k], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) y[r] = b ? __fadd_rn(acc, b[r]) : acc;
+}
+
+// ---------------------------------------------------------------------------
+// Embeddings
+// ---------------------------------------------------------------------------
+// Decode: x[row] = speech_emb[tok[slot(row)]] + wpe[pos[row]]
+// (build_step_graph, main.cpp:625-627).
+__global__ void embed_step_kernel(const __half * __restrict__ semb, const float * __restrict__ wpe,
+                                  const int * __restrict__ tok, const int * __restrict__ row_slot,
+                                  const int * __restrict__ pos, int D, int V, int n_pos,
+                                  float * __restrict__ x, unsigned * err) {
+    const int row = blockIdx.x;
+    const int t = tok[row_slot[row]];
+    const int p = pos[row];
+    if (t < 0 || t >= V || p < 0 || p >= n_pos) {
+        if (threadIdx.x == 0) atomicOr(err, (t < 0 || t >= V) ? T3B_DEVERR_TOKEN : T3B_DEVERR_POS);
+        return;
+    }
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        x[(size_t) row * D + i] = __fadd_rn(__half2float(semb[(size_t) t * D + i]), wpe[(size_t) p * D + i]);
+}
+
+// Prompt rows (build_prompt_graph, main.cpp:588-616): kind 0 = speaker
+// projection row (spk), 1 = speech_emb[id], 2 = text_emb[id], 3 = zeros
+// (text row of the CFG unconditional prompt); plus wpe[pos0 + r].
+__global__ void embed_prompt_kernel(const __half * __restrict__ semb, const __half * __restrict__ temb,
+                                    const float * __restrict__ wpe, const float * __restrict__ spk,
+                                    const int * __restrict__ kind, const int * __restrict__ id, int pos0,
+                                    int D, float * __restrict__ x) {
+    const int r = blockIdx.x;
+    const int k = kind[r], t = id[r];
+    const float * wp = wpe + (size_t) (pos0 + r) * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float v;
+        if (k == 0) v = spk[i];
+        else if (k == 1) v = __half2float(semb[(size_t) t * D + i]);
+        else if (k == 2) v = __half2float(temb[(size_t) t * D + i]);
+        else v = 0.0f;
+        x[(size_t) r * D + i] = __fadd_rn(v, wp[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention over per-row f16 caches (ggml_flash_attn_ext, N query
+// rows, no mask: each row attends its own positions 0..len-1).
+// grid = (n_head, M, s_max), 128 threads, one key per thread per CTA; the
+// last CTA of a (row, head) merges the split partials (m, l, o[64]).
+// ---------------------------------------------------------------------------
+struct AttnArgs {
+    const float * q; int ldq;
+    const __half * kv; size_t row_elems; size_t layer_off; size_t v_off;
+    const int * row_of;      // nullable: row m uses cache row m
+    const int * len; int len_add;
+    int max_ctx, n_head;
+    float * out; int ldo;
+    float * part; unsigned * cnt; int s_max;
+    unsigned * err;
+};
+
+__global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a) {
+    __shared__ float qs[T3B_HD];
+    __shared__ float ps[T3B_ATTN_CHUNK];
+    __shared__ float red[32];
+    __shared__ float oacc[2][T3B_HD];
+    __shared__ int last;
+    const int h = blockIdx.x, m = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
+    const int L = a.len[m] + a.len_add;
+    if (L <= 0 || L > a.max_ctx) {
+        if (tid == 0 && sp == 0) atomicOr(a.err, T3B_DEVERR_POS);
+        return;
+    }
+    const int ns = (L + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;
+    if (sp >= ns) return;
+    if (tid < T3B_HD) qs[tid] = a.q[(size_t) m * a.ldq + h * T3B_HD + tid];
+    __syncthreads();
+    const int crow = a.row_of ? a.row_of[m] : m;
+    const __half * kb = a.kv + (size_t) crow * a.row_elems + a.layer_off + (size_t) h * a.max_ctx * T3B_HD;
+    const __half * vb = kb + a.v_off;
+    const int j0 = sp * T3B_ATTN_CHUNK;
+    const int nk = min(T3B_ATTN_CHUNK, L - j0);
+    float sc = -INFINITY;
+    if (tid < nk) {
+        const uint4 * kp = (const uint4 *) (kb + (size_t) (j0 + tid) * T3B_HD);
+        float dot = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 u = kp[c];
+            const __half2 * hp = (const __half2 *) &u;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 f = __half22float2(hp[t]);
+                dot = fmaf(qs[c * 8 + 2 * t], f.x, dot);
+                dot = fmaf(qs[c * 8 + 2 * t + 1], f.y, dot);
+            }
+        }
+        sc = dot * 0.125f;
+    }
+    const float mx = block_max(sc, red);
+    const float p = tid < nk ? expf(sc - mx) : 0.0f;
+    ps[tid] = p;
+    const float l = block_sum(p, red);
+    __syncthreads();
+    {
+        const int d = tid & (T3B_HD - 1), half = tid >> 6;
+        float o = 0.0f;
+        for (int t = half; t < nk; t += 2) o = fmaf(ps[t], __half2float(vb[(size_t) (j0 + t) * T3B_HD + d]), o);
+        oacc[half][d] = o;
+    }
+    __syncthreads();
+    if (ns == 1) {
+        if (tid < T3B_HD) a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = (oacc[0][tid] + oacc[1][tid]) / l;
+        return;
+    }
+    float * P = a.part + (((size_t) m * a.n_head + h) * a.s_max + sp) * (T3B_HD + 2);
+    if (tid < T3B_HD) P[2 + tid] = oacc[0][tid] + oacc[1][tid];
+    if (tid == 0) { P[0] = mx; P[1] = l; }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(&a.cnt[(size_t) m * a.n_head + h], 1u);
+        last = (prev == (unsigned) (ns - 1));
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid < T3B_HD) {
+        const float * P0 = a.part + ((size_t) m * a.n_head + h) * a.s_max * (T3B_HD + 2);
+        float gm = -INFINITY;
+        for (int s = 0; s < ns; ++s) gm = fmaxf(gm, __ldcg(P0 + (size_t) s * (T3B_HD + 2)));
+        float lt = 0.0f, ot = 0.0f;
+        for (int s = 0; s < ns; ++s) {
+            const float * Ps = P0 + (size_t) s * (T3B_HD + 2);
+            const float w = expf(__ldcg(Ps) - gm);
+            lt = fmaf(__ldcg(Ps + 1), w, lt);
+            ot = fmaf(__ldcg(Ps + 2 + tid), w, ot);
+        }
+        a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = ot / lt;
+    }
+    if (tid == 0) a.cnt[(size_t) m * a.n_head + h] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Fused sampler
+// ---------------------------------------------------------------------------
+struct ExpFix { const unsigned long long * tab; int bits; int max_probe; };
+
+// exp with the host libm's rounding: t3_expf_core + fix-up table lookup.
+__device__ __forceinline__ float t3_expf_dev(float x, const ExpFix & f) {
+    const float y = t3_expf_core(x);
+    const uint32_t key = __float_as_uint(x);
+    const uint32_t mask = (1u << f.bits) - 1u;
+    uint32_t h = t3_expf_hash(key, f.bits);
+    for (int i = 0; i < f.max_probe; ++i) {
+        const unsigned long long e = __ldg(f.tab + ((h + (uint32_t) i) & mask));
+        const uint32_t k = (uint32_t) (e >> 32);
+        if (k == key) return __uint_as_float((uint32_t) e);
+        if (k == 0u) break;
+    }
+    return y;
+}
+
+// float -> 32-bit key whose ascending order is the float's DEScending order.
+__device__ __forceinline__ uint32_t desc_key(float x) {
+    const uint32_t u = __float_as_uint(x);
+    const uint32_t asc = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ~asc;
+}
+__device__ __forceinline__ float desc_key_inv(uint32_t k) {
+    const uint32_t asc = ~k;
+    const uint32_t u = (asc & 0x80000000u) ? (asc & 0x7fffffffu) : ~asc;
+    return __uint_as_float(u);
+}
+
+// std::mt19937 regeneration (libstdc++ _M_gen_rand), block-parallel in the
+// three dependency phases of the recurrence.  All threads must call it.
+__device__ void mt_twist(uint32_t * x) {
+    const uint32_t UP = 0x80000000u, LO = 0x7fffffffu, A = 0x9908b0dfu;
+    const int t = threadIdx.x;
+    uint32_t nv = 0;
+    // k in [0, 227): x[k+397] not yet rewritten
+    if (t < 227) { const uint32_t y = (x[t] & UP) | (x[t + 1] & LO); nv = x[t + 397] ^ (y >> 1) ^ ((y & 1u) ? A : 0u); }
+    __syncthreads();
+    if (t < 227) x[t] = nv;
+    __syncthreads();
+    // k in [227, 454): x[k-227] from the first phase
+    if (t < 227) { const int k = 227 + t; const uint32_t y = (x[k] & UP) | (x[k + 1] & LO); nv = x[k - 227] ^ (y >> 1) ^ ((y & 1u) ? A : 0u); }
+    __syncthreads();
+    if (t < 227) x[227 + t] = nv;
+    __syncthreads();
+    // k in [454, 623): x[k-227] from the second phase
+    if (t < 169) { const int k = 454 + t; const uint32_t y = (x[k] & UP) | (x[k + 1] & LO); nv = x[k - 227] ^ (y >> 1) ^ ((y & 1u) ? A : 0u); }
+    __syncthreads();
+    if (t < 169) x[454 + t] = nv;
+    __syncthreads();
+    if (t == 0) { const uint32_t y = (x[623] & UP) | (x[0] & LO); x[623] = x[396] ^ (y >> 1) ^ ((y & 1u) ? A : 0u); }
+    __syncthreads();
+}
+__device__ __forceinline__ uint32_t mt_temper(uint32_t z) {
+    z ^= (z >> 11);
+    z ^= (z << 7) & 0x9d2c5680u;
+    z ^= (z << 15) & 0xefc60000u;
+    z ^= (z >> 18);
+    return z;
+}
+
+__device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c[0]), lo0 = 0xD2511F53u * c[0];
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]), lo1 = 0xCD9E8D57u * c[2];
+        const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+        c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+        k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+    }
+}
+
+struct SampArgs {
+    const float * cond; long long cond_stride;
+    const float * uncond; long long uncond_stride;   // nullable
+    int V;
+    const int * slot_of;                              // nullable: slot = row
+    int * hist; int hist_stride; int * hist_len; int hist_append;
+    const t3b_sample_params * params; int params_per_row;
+    const int * rng_mode;                             // per slot; nullable = Philox
+    uint32_t * mt;                                    // [slot][625]
+    const unsigned long long * ph_seed; unsigned long long * ph_ctr;
+    int * tok_out;                                    // [row]
+    int * step_tok;                                   // nullable: [slot] next-step token
+    int * done; int stop_token;                       // nullable
+    ExpFix fx;
+};
+
+#define T3B_SAMPLER_THREADS 1024
+#define T3B_SAMPLER_VMAX 8192
+// dynamic smem: s[VMAX] f32 | keys[VMAX] u64 | e[VMAX] f32
+#define T3B_SAMPLER_SMEM (T3B_SAMPLER_VMAX * (4 + 8 + 4))
+
+__global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArgs a) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    float * s = (float *) smraw;
+    unsigned long long * keys = (unsigned long long *) (smraw + T3B_SAMPLER_VMAX * 4);
+    float * e = (float *) (smraw + T3B_SAMPLER_VMAX * 12);
+    int * lst = (int *) keys;   // index list, reused after the sort
+    __shared__ float redf[32];
+    __shared__ int redi[32];
+    __shared__ int hist256[256];
+    __shared__ unsigned seen[T3B_SAMPLER_VMAX / 32];
+    __shared__ int shi[8];
+    __shared__ float shf[4];
+    __shared__ uint32_t mtx[625];
+
+    const int r = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
+    const int slot = a.slot_of ? a.slot_of[r] : r;
+    if (a.done && a.done[slot]) return;
+    const t3b_sample_params P = a.params[a.params_per_row ? r : 0];
+    const int V = a.V;
+    const float * cond = a.cond + (long long) slot * a.cond_stride;
+    const float * unc = a.uncond ? a.uncond + (long long) slot * a.uncond_stride : nullptr;
+
+    // (0) CFG mix, (1) temperature  (main.cpp:735-738)
+    const bool cfg = unc != nullptr && P.cfg_weight != 0.0f;
+    const bool use_t = P.temp > 0.0f && P.temp != 1.0f;
+    const float inv_t = use_t ? __fdiv_rn(1.0f, P.temp) : 1.0f;
+    for (int i = tid; i < V; i += nth) {
+        float v = cond[i];
+        if (cfg) v = __fadd_rn(v, __fmul_rn(P.cfg_weight, __fsub_rn(v, unc[i])));
+        if (use_t) v = __fmul_rn(v, inv_t);
+        s[i] = v;
+    }
+    __syncthreads();
+
+    // (1b) min-p: drop exp(s - max) < min_p
+    if (P.min_p > 0.0f) {
+        float lm = -INFINITY;
+        for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
+        const float mx = block_max(lm, redf);
+        for (int i = tid; i < V; i += nth)
+            if (s[i] != -INFINITY && t3_expf_dev(__fsub_rn(s[i], mx), a.fx) < P.min_p) s[i] = -INFINITY;
+        __syncthreads();
+    }
+
+    // (2) top-k (main.cpp:740-748): radix-select the value at descending
+    // rank k, then keep s > thr (thr nudged by 1e-10f if fewer than k).
+    if (P.top_k > 0 && P.top_k < V) {
+        uint32_t prefix = 0u, maskb = 0u;
+        int rank = P.top_k;
+        for (int pass = 0; pass < 4; ++pass) {
+            const int shift = 24 - 8 * pass;
+            for (int i = tid; i < 256; i += nth) hist256[i] = 0;
+            __syncthreads();
+            for (int i = tid; i < V; i += nth) {
+                const uint32_t k = desc_key(s[i]);
+                if ((k & maskb) == prefix) atomicAdd(&hist256[(k >> shift) & 255u], 1);
+            }
+            __syncthreads();
+            if (tid < 32) {
+                int c[8], tot = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { c[j] = hist256[tid * 8 + j]; tot += c[j]; }
+                int incl = tot;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (tid >= o) incl += n;
+                }
+                const int excl = incl - tot;
+                if (excl <= rank && rank < incl) {
+                    int run = excl;
+                    for (int j = 0; j < 8; ++j) {
+                        if (rank < run + c[j]) { shi[0] = tid * 8 + j; shi[1] = run; break; }
+                        run += c[j];
+                    }
+                }
+            }
+            __syncthreads();
+            rank -= shi[1];
+            prefix |= ((uint32_t) shi[0]) << shift;
+            maskb |= 255u << shift;
+            __syncthreads();
+        }
+        float thr = desc_key_inv(prefix);
+        int above = 0;
+        for (int i = tid; i < V; i += nth) above += s[i] > thr ? 1 : 0;
+        above = block_sum_i(above, redi);
+        if (above < P.top_k) thr = __fsub_rn(thr, 1e-10f);
+        for (int i = tid; i < V; i += nth) if (s[i] <= thr) s[i] = -INFINITY;
+        __syncthreads();
+    }
+
+    // (3) top-p (main.cpp:750-772): survivors sorted by score descending
+    // (ties by ascending index), sequential float sums in that order.
+    if (P.top_p < 1.0f) {
+        if (tid == 0) shi[2] = 0;
+        __syncthreads();
+        for (int i = tid; i < V; i += nth)
+            if (s[i] != -INFINITY) {
+                const int p = atomicAdd(&shi[2], 1);
+                keys[p] = ((unsigned long long) desc_key(s[i]) << 32) | (unsigned) i;
+            }
+        __syncthreads();
+        const int c = shi[2];
+        if (c > 0) {
+            int n2 = 1;
+            while (n2 < c) n2 <<= 1;
+            for (int i = c + tid; i < n2; i += nth) keys[i] = ~0ull;
+            __syncthreads();
+            for (int k = 2; k <= n2; k <<= 1)
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    for (int i = tid; i < n2; i += nth) {
+                        const int ixj = i ^ j;
+                        if (ixj > i) {
+                            const unsigned long long x0 = keys[i], x1 = keys[ixj];
+                            const bool up = (i & k) == 0;
+                            if ((x0 > x1) == up) { keys[i] = x1; keys[ixj] = x0; }
+                        }
+                    }
+                    __syncthreads();
+                }
+            const float mx = s[(int) (keys[0] & 0xffffffffu)];
+            for (int j = tid; j < c; j += nth) e[j] = t3_expf_dev(__fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx), a.fx);
+            __syncthreads();
+            if (tid == 0) {
+                float ps = 0.0f;
+                for (int j = 0; j < c; ++j) ps = __fadd_rn(ps, e[j]);
+                shf[0] = ps;
+            }
+            __syncthreads();
+            const float psum = shf[0];
+            for (int j = tid; j < c; j += nth) e[j] = __fdiv_rn(e[j], psum);
+            __syncthreads();
+            if (tid == 0) {
+                float cum = 0.0f;
+                int cut = c;
+                for (int j = 0; j < c; ++j) {
+                    cum = __fadd_rn(cum, e[j]);
+                    if (cum >= P.top_p) { cut = j + 1; break; }
+                }
+                shi[3] = cut;
+            }
+            __syncthreads();
+            for (int j = shi[3] + tid; j < c; j += nth) s[(int) (keys[j] & 0xffffffffu)] = -INFINITY;
+            __syncthreads();
+        }
+    }
+
+    // (4) repetition penalty over distinct history ids (main.cpp:774-781)
+    const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
+    const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
+    if (P.repeat_penalty != 1.0f && hl > 0) {
+        for (int i = tid; i < (V + 31) / 32; i += nth) seen[i] = 0u;
+        __syncthreads();
+        for (int j = tid; j < hl; j += nth) {
+            const int t = hist[j];
+            if (t < 0 || t >= V) continue;
+            const unsigned bit = 1u << (t & 31);
+            const unsigned old = atomicOr(&seen[t >> 5], bit);
+            if (old & bit) continue;
+            const float v = s[t];
+            if (v == -INFINITY) continue;
+            s[t] = v > 0.0f ? __fdiv_rn(v, P.repeat_penalty) : __fmul_rn(v, P.repeat_penalty);
+        }
+        __syncthreads();
+    }
+
+    // (5) softmax over survivors in index order (main.cpp:783-793)
+    float lm = -INFINITY;
+    for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
+    const float mx = block_max(lm, redf);
+    // index-ordered compaction: thread t owns [t*per, (t+1)*per)
+    const int per = (V + nth - 1) / nth;
+    const int i0 = min(V, tid * per), i1 = min(V, i0 + per);
+    int cnt = 0;
+    for (int i = i0; i < i1; ++i) cnt += s[i] != -INFINITY ? 1 : 0;
+    // block exclusive scan of cnt
+    int incl = cnt;
+    const int lane = tid & 31, w = tid >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) redi[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        const int nw = nth >> 5;
+        int v = lane < nw ? redi[lane] : 0;
+        int vi = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, vi, o);
+            if (lane >= o) vi += n;
+        }
+        if (lane < nw) redi[lane] = vi - v;
+        if (lane == nw - 1) shi[4] = vi;
+    }
+    __syncthreads();
+    {
+        int o = redi[w] + incl - cnt;
+        for (int i = i0; i < i1; ++i)
+            if (s[i] != -INFINITY) { lst[o] = i; e[o] = t3_expf_dev(__fsub_rn(s[i], mx), a.fx); ++o; }
+    }
+    __syncthreads();
+    const int cf = shi[4];
+    if (tid == 0) {
+        float ps = 0.0f;
+        for (int j = 0; j < cf; ++j) ps = __fadd_rn(ps, e[j]);
+        shf[1] = ps;
+    }
+    __syncthreads();
+    const float psum = shf[1];
+    int tok = 0;
+    if (psum != 0.0f) {
+        for (int j = tid; j < cf; j += nth) e[j] = __fdiv_rn(e[j], psum);
+        __syncthreads();
+        if (P.temp <= 0.0f) {
+            // (6) first maximum in index order
+            if (tid == 0) {
+                int best = lst[0]; float bp = e[0];
+                for (int j = 1; j < cf; ++j) if (e[j] > bp) { bp = e[j]; best = lst[j]; }
+                // an index before the first survivor has p = 0 < bp
+                shi[5] = best;
+            }
+            __syncthreads();
+            tok = shi[5];
+        } else {
+            // (7) discrete_distribution draw
+            const int mode = a.rng_mode ? a.rng_mode[slot] : T3B_RNG_PHILOX;
+            uint32_t x1, x2;
+            if (mode == T3B_RNG_MT19937) {
+                uint32_t * st = a.mt + (size_t) slot * 625;
+                for (int i = tid; i < 625; i += nth) mtx[i] = st[i];
+                __syncthreads();
+                int idx = (int) mtx[624];
+                bool tw = false;
+                if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
+                x1 = mt_temper(mtx[idx]); ++idx;
+                if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
+                x2 = mt_temper(mtx[idx]); ++idx;
+                if (tw) for (int i = tid; i < 624; i += nth) st[i] = mtx[i];
+                if (tid == 0) st[624] = (uint32_t) idx;
+            } else {
+                const unsigned long long sd = a.ph_seed[slot];
+                const unsigned long long ct = a.ph_ctr[slot];
+                uint32_t c4[4] = {(uint32_t) ct, (uint32_t) (ct >> 32), (uint32_t) slot, 0u};
+                philox4x32_10(c4, (uint32_t) sd, (uint32_t) (sd >> 32));
+                x1 = c4[0]; x2 = c4[1];
+                __syncthreads();
+                if (tid == 0) a.ph_ctr[slot] = ct + 1ull;
+            }
+            if (tid == 0) {
+                double sum = (double) x1;
+                sum += (double) x2 * 4294967296.0;
+                double u = sum / 18446744073709551616.0;
+                if (u >= 1.0) u = nextafter(1.0, 0.0);
+                double dsum = 0.0;
+                for (int j = 0; j < cf; ++j) dsum += (double) e[j];
+                int pick = V - 1;
+                if (u <= 0.0) pick = 0;
+                else {
+                    double c = 0.0;
+                    for (int j = 0; j < cf; ++j) {
+                        c = c + (double) e[j] / dsum;
+                        const double ci = lst[j] == V - 1 ? 1.0 : c;
+                        if (ci >= u) { pick = lst[j]; break; }
+                    }
+                }
+                shi[6] = pick;
+            }
+            __syncthreads();
+            tok = shi[6];
+        }
+    }
+    if (tid == 0) {
+        a.tok_out[r] = tok;
+        if (a.step_tok) a.step_tok[slot] = tok;
+        if (a.hist_append && a.hist && a.hist_len) {
+            if (hl < a.hist_stride) {
+                a.hist[(size_t) slot * a.hist_stride + hl] = tok;
+                a.hist_len[slot] = hl + 1;
+            }
+        }
+        if (a.done && tok == a.stop_token) a.done[slot] = 1;
+    }
+}
+
+// exp test hook
+__global__ void expf_test_kernel(const float * in, float * out, int n, ExpFix fx) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = t3_expf_dev(in[i], fx);
+}
+
+// Advance per-row positions after a decode step (graph-captured loops).
+__global__ void advance_pos_kernel(int * pos, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) pos[i] += 1;
+}
