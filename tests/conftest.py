@@ -73,3 +73,32 @@ def gpu_available():
         return torch.cuda.is_available()
     except Exception:
         return False
+
+
+def nudged(tensors):
+    """Copy of a T3 tensor dict with model/wpe moved by one ulp: the
+    perturbation used to measure the quantized path's own sensitivity."""
+    t = dict(tensors)
+    ty, w = tensors["model/wpe"]
+    t["model/wpe"] = (ty, np.nextafter(w, np.float32(np.inf)).astype(np.float32))
+    return t
+
+
+def noise_floor(orc, hp, tensors, text, tokens, max_ctx, kv_f16=1):
+    """rel distance between the oracle and the oracle on 1-ulp-nudged
+    positions, for the prefill logits and each step's logits.
+
+    With Q8_0 re-quantised activations a 1-ulp input change flips a few
+    rounding decisions, each moving a GEMV output by ~d_x * w, and the flips
+    compound through GELU's f16 rounding and the following layers: on the
+    random-init T3 this is ~1e-2 of max|logit| (F16 weights: ~5e-4).  Two
+    implementations that do not sum in the same order cannot agree more
+    closely than this."""
+    a = orc.Model(hp, tensors, max_ctx=max_ctx, gemv_mode=1, gelu_f16=1, kv_f16=kv_f16)
+    b = orc.Model(hp, nudged(tensors), max_ctx=max_ctx, gemv_mode=1, gelu_f16=1, kv_f16=kv_f16)
+    P, la = a.prompt(text)
+    _, lb = b.prompt(text)
+    out = [rel_err(lb, la)]
+    for i, tok in enumerate(tokens):
+        out.append(rel_err(b.step(P + i, tok), a.step(P + i, tok)))
+    return out

@@ -98,7 +98,10 @@ def test_gemv_matches_oracle(pkg, orc, ty, KN, M):
             ref = np.vectorize(lambda v: orc.lib().orc_gelu(float(v), 1), otypes=[np.float32])(ref)
         if epi == 2:
             ref = ref + res
-        assert rel_err(y, ref) < 2e-4, (ty, K, N, M, epi)
+        # the GELU epilogue rounds through f16: an input 1 ulp away from the
+        # oracle's can land on the neighbouring f16 (2^-11 relative)
+        tol = 1e-3 if epi == 1 else 2e-4
+        assert rel_err(y, ref) < tol, (ty, K, N, M, epi)
 
 
 @pytest.mark.parametrize("L_", [1, 7, 128, 129, 300, 2048])
