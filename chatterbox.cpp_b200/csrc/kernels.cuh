@@ -429,9 +429,9 @@ __device__ __forceinline__ float t3_expf_dev(float x, const ExpFix & f) {
     uint32_t h = t3_expf_hash(key, f.bits);
     for (int i = 0; i < f.max_probe; ++i) {
         const unsigned long long e = __ldg(f.tab + ((h + (uint32_t) i) & mask));
-        const uint32_t k = (uint32_t) (e >> 32);
-        if (k == key) return __uint_as_float((uint32_t) e);
-        if (k == 0u) break;
+        // an empty slot is all-zero; test it first, because +0.0 has key 0
+        if (e == 0ull) break;
+        if ((uint32_t) (e >> 32) == key) return __uint_as_float((uint32_t) e);
     }
     return y;
 }
