@@ -288,6 +288,7 @@ def main():
                          "kernel": "decode step (graph of embed + 24 layers + head + sampler)",
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
+            "sampler": sampler_microbench(pkg, torch, peak),
             "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": K * (1 + hp["n_layer"] * 9 + 2 + 2) + 1,
             "tokens_head": [int(x) for x in toks[:8]]}
@@ -300,6 +301,47 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def sampler_microbench(pkg, torch, peak, reps=200):
+    """128 rows x 6563, cond/uncond ~N(0, 3^2), CFG 0.5,
+    256-token histories, penalty 1.2, temp 0.8, min_p 0.05, top_k 1000,
+    top_p 0.95, one Philox stream per row.  Device time per call (CUDA events
+    on the launching stream), median over `reps` calls."""
+    import ctypes as C
+    L = pkg.lib()
+    rows, V, HL = 128, 6563, 256
+    g = torch.Generator(device="cuda").manual_seed(0)
+    cond = torch.randn(rows, V, device="cuda", generator=g) * 3
+    unc = torch.randn(rows, V, device="cuda", generator=g) * 3
+    hist = torch.randint(0, V, (rows, HL), device="cuda", dtype=torch.int32, generator=g)
+    hlen = torch.full((rows,), HL, device="cuda", dtype=torch.int32)
+    P = (pkg.SampleParams * rows)(*[pkg.SampleParams.make(1000, 0.95, 0.8, 1.2, 0.05, 0.5)] * rows)
+    pd = torch.frombuffer(bytearray(bytes(P)), dtype=torch.uint8).cuda()
+    seeds = torch.arange(rows, device="cuda", dtype=torch.int64)
+    ctr = torch.zeros(rows, device="cuda", dtype=torch.int64)
+    tok = torch.zeros(rows, device="cuda", dtype=torch.int32)
+    s = torch.cuda.current_stream()
+    a = [C.c_void_p(t.data_ptr()) for t in (cond, unc)]
+    args = (a[0], a[1], rows, V, C.c_void_p(hist.data_ptr()), C.c_void_p(hlen.data_ptr()), HL,
+            C.c_void_p(pd.data_ptr()), C.c_void_p(seeds.data_ptr()), C.c_void_p(ctr.data_ptr()),
+            C.c_void_p(tok.data_ptr()), C.c_void_p(s.cuda_stream))
+    for _ in range(5):
+        pkg.check(L.t3b_op_sample_philox(*args))
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        pkg.check(L.t3b_op_sample_philox(*args))
+        e1.record(s)
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    us = sorted(e0.elapsed_time(e1) * 1000.0 for e0, e1 in times)
+    med = us[len(us) // 2]
+    byts = 2 * rows * V * 4 + rows * HL * 4 + rows * 4
+    return {"config": "configs[1]: 128x6563, CFG 0.5, min_p 0.05, top_k 1000, top_p 0.95, penalty 1.2, temp 0.8, "
+                      "Philox", "us_per_step": med, "us_min": us[0], "target_us": 10.0,
+            "achieved_gbs": byts / (med * 1e-6) / 1e9, "peak": peak}
 
 
 def gemv_roofline(pkg, torch, peak):

@@ -27,7 +27,7 @@ ERRORS = {-1: "ARG", -2: "CUDA", -3: "OOM", -4: "STATE", -5: "DEVICE", -6: "CANC
 EXPORTS = [
     "t3b_create", "t3b_destroy", "t3b_last_error", "t3b_stream_alloc", "t3b_prefill", "t3b_step", "t3b_sample",
     "t3b_set_rng", "t3b_set_rng_state", "t3b_get_rng_state", "t3b_set_history", "t3b_decode", "t3b_cancel",
-    "t3b_last_device_ms", "t3b_stream_handle", "t3b_op_row_bytes", "t3b_op_repack", "t3b_op_gemv", "t3b_op_attention",
+    "t3b_last_device_ms", "t3b_stream_handle", "t3b_trace_logits", "t3b_get_logits_trace", "t3b_op_row_bytes", "t3b_op_repack", "t3b_op_gemv", "t3b_op_attention",
     "t3b_op_sample_philox", "t3b_expf_fixup_count", "t3b_op_expf",
 ]
 
@@ -90,6 +90,8 @@ def lib():
             "t3b_cancel": (None, [vp]),
             "t3b_last_device_ms": (C.c_float, [vp]),
             "t3b_stream_handle": (vp, [vp]),
+            "t3b_trace_logits": (C.c_int, [vp, C.c_int]),
+            "t3b_get_logits_trace": (C.c_int, [vp, vp, C.c_int]),
             "t3b_op_row_bytes": (C.c_size_t, [C.c_int, C.c_int]),
             "t3b_op_repack": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, vp]),
             "t3b_op_gemv": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, C.c_float, vp, vp, C.c_int,
@@ -226,6 +228,15 @@ class T3Model:
         check(lib().t3b_decode(self.ctx, n, _ptr(st), C.cast(pa, C.c_void_p), max_steps, 1 if ignore_stop else 0,
                                _ptr(out), _ptr(cnt)), self.ctx)
         return [out[i, :cnt[i]].copy() for i in range(n)]
+
+    def trace_logits(self, max_steps):
+        """Record the logits every decode step samples from (debug)."""
+        check(lib().t3b_trace_logits(self.ctx, max_steps), self.ctx)
+
+    def logits_trace(self, n):
+        out = np.zeros((n, self.V), np.float32)
+        check(lib().t3b_get_logits_trace(self.ctx, _ptr(out), n), self.ctx)
+        return out
 
     def stream_handle(self):
         """cudaStream_t of this context (int), e.g. for torch.cuda.ExternalStream."""

@@ -491,6 +491,53 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32
     }
 }
 
+// Sequential float / double chains the reference evaluates left to right.
+// One thread walks them; operands come in as float4 loads, eight at a time,
+// so the only serial dependency left is the add itself.
+__device__ __forceinline__ float seq_sum_f32(const float * a, int n) {
+    float s = 0.0f;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+        const float4 u = *(const float4 *) (a + j), v = *(const float4 *) (a + j + 4);
+        s = __fadd_rn(s, u.x); s = __fadd_rn(s, u.y); s = __fadd_rn(s, u.z); s = __fadd_rn(s, u.w);
+        s = __fadd_rn(s, v.x); s = __fadd_rn(s, v.y); s = __fadd_rn(s, v.z); s = __fadd_rn(s, v.w);
+    }
+    for (; j < n; ++j) s = __fadd_rn(s, a[j]);
+    return s;
+}
+__device__ __forceinline__ double seq_sum_f64(const float * a, int n) {
+    double s = 0.0;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+        const float4 u = *(const float4 *) (a + j), v = *(const float4 *) (a + j + 4);
+        s = __dadd_rn(s, (double) u.x); s = __dadd_rn(s, (double) u.y);
+        s = __dadd_rn(s, (double) u.z); s = __dadd_rn(s, (double) u.w);
+        s = __dadd_rn(s, (double) v.x); s = __dadd_rn(s, (double) v.y);
+        s = __dadd_rn(s, (double) v.z); s = __dadd_rn(s, (double) v.w);
+    }
+    for (; j < n; ++j) s = __dadd_rn(s, (double) a[j]);
+    return s;
+}
+// First j with fl(fl(...(a[0]) + a[1]) ... + a[j]) >= target; n if none.
+__device__ __forceinline__ int seq_cut_f32(const float * a, int n, float target) {
+    float c = 0.0f;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+        const float4 u = *(const float4 *) (a + j), v = *(const float4 *) (a + j + 4);
+        const float w[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            c = __fadd_rn(c, w[t]);
+            if (c >= target) return j + t;
+        }
+    }
+    for (; j < n; ++j) {
+        c = __fadd_rn(c, a[j]);
+        if (c >= target) return j;
+    }
+    return n;
+}
+
 struct SampArgs {
     const float * cond; long long cond_stride;
     const float * uncond; long long uncond_stride;   // nullable
@@ -512,8 +559,10 @@ struct SampArgs {
 // dynamic smem: s[VMAX] f32 | keys[VMAX] u64 | e[VMAX] f32
 #define T3B_SAMPLER_SMEM (T3B_SAMPLER_VMAX * (4 + 8 + 4))
 
-__global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArgs a) {
-    extern __shared__ __align__(16) unsigned char smraw[];
+// One row of sample_next_token_ex by the whole block (any blockDim.x that
+// is a multiple of 32 and >= 256).  smraw: T3B_SAMPLER_SMEM bytes of shared
+// memory.  Returns the token (every thread), or -1 for a finished stream.
+__device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned char * smraw) {
     float * s = (float *) smraw;
     unsigned long long * keys = (unsigned long long *) (smraw + T3B_SAMPLER_VMAX * 4);
     float * e = (float *) (smraw + T3B_SAMPLER_VMAX * 12);
@@ -526,9 +575,9 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
     __shared__ float shf[4];
     __shared__ uint32_t mtx[625];
 
-    const int r = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
+    const int tid = threadIdx.x, nth = blockDim.x;
     const int slot = a.slot_of ? a.slot_of[r] : r;
-    if (a.done && a.done[slot]) return;
+    if (a.done && a.done[slot]) return -1;
     const t3b_sample_params P = a.params[a.params_per_row ? r : 0];
     const int V = a.V;
     const float * cond = a.cond + (long long) slot * a.cond_stride;
@@ -565,9 +614,17 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
             const int shift = 24 - 8 * pass;
             for (int i = tid; i < 256; i += nth) hist256[i] = 0;
             __syncthreads();
-            for (int i = tid; i < V; i += nth) {
-                const uint32_t k = desc_key(s[i]);
-                if ((k & maskb) == prefix) atomicAdd(&hist256[(k >> shift) & 255u], 1);
+            // float keys pile into a few bins (shared exponents): aggregate
+            // equal bins across the warp so each bin gets one atomic per warp
+            for (int i0 = 0; i0 < V; i0 += nth) {
+                const int i = i0 + tid;
+                int bin = 256;                               // 256 = not a candidate
+                if (i < V) {
+                    const uint32_t k = desc_key(s[i]);
+                    if ((k & maskb) == prefix) bin = (int) ((k >> shift) & 255u);
+                }
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (bin < 256 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist256[bin], __popc(peers));
             }
             __syncthreads();
             if (tid < 32) {
@@ -636,23 +693,14 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
             const float mx = s[(int) (keys[0] & 0xffffffffu)];
             for (int j = tid; j < c; j += nth) e[j] = t3_expf_dev(__fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx), a.fx);
             __syncthreads();
-            if (tid == 0) {
-                float ps = 0.0f;
-                for (int j = 0; j < c; ++j) ps = __fadd_rn(ps, e[j]);
-                shf[0] = ps;
-            }
+            if (tid == 0) shf[0] = seq_sum_f32(e, c);
             __syncthreads();
             const float psum = shf[0];
             for (int j = tid; j < c; j += nth) e[j] = __fdiv_rn(e[j], psum);
             __syncthreads();
             if (tid == 0) {
-                float cum = 0.0f;
-                int cut = c;
-                for (int j = 0; j < c; ++j) {
-                    cum = __fadd_rn(cum, e[j]);
-                    if (cum >= P.top_p) { cut = j + 1; break; }
-                }
-                shi[3] = cut;
+                const int j = seq_cut_f32(e, c, P.top_p);
+                shi[3] = j < c ? j + 1 : c;
             }
             __syncthreads();
             for (int j = shi[3] + tid; j < c; j += nth) s[(int) (keys[j] & 0xffffffffu)] = -INFINITY;
@@ -718,11 +766,7 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
     }
     __syncthreads();
     const int cf = shi[4];
-    if (tid == 0) {
-        float ps = 0.0f;
-        for (int j = 0; j < cf; ++j) ps = __fadd_rn(ps, e[j]);
-        shf[1] = ps;
-    }
+    if (tid == 0) shf[1] = seq_sum_f32(e, cf);
     __syncthreads();
     const float psum = shf[1];
     int tok = 0;
@@ -769,16 +813,31 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
                 sum += (double) x2 * 4294967296.0;
                 double u = sum / 18446744073709551616.0;
                 if (u >= 1.0) u = nextafter(1.0, 0.0);
-                double dsum = 0.0;
-                for (int j = 0; j < cf; ++j) dsum += (double) e[j];
+                const double dsum = seq_sum_f64(e, cf);
                 int pick = V - 1;
                 if (u <= 0.0) pick = 0;
                 else {
+                    // cp_i = cp_{i-1} + p_i / dsum (partial_sum of the
+                    // normalised weights); the divisions do not depend on
+                    // the running sum, so four are issued ahead of the adds
                     double c = 0.0;
-                    for (int j = 0; j < cf; ++j) {
-                        c = c + (double) e[j] / dsum;
+                    int j = 0;
+                    bool found = false;
+                    for (; j + 4 <= cf && !found; j += 4) {
+                        const double q0 = (double) e[j] / dsum, q1 = (double) e[j + 1] / dsum;
+                        const double q2 = (double) e[j + 2] / dsum, q3 = (double) e[j + 3] / dsum;
+                        const double qq[4] = {q0, q1, q2, q3};
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            c = __dadd_rn(c, qq[t]);
+                            const double ci = lst[j + t] == V - 1 ? 1.0 : c;
+                            if (ci >= u) { pick = lst[j + t]; found = true; break; }
+                        }
+                    }
+                    for (; j < cf && !found; ++j) {
+                        c = __dadd_rn(c, (double) e[j] / dsum);
                         const double ci = lst[j] == V - 1 ? 1.0 : c;
-                        if (ci >= u) { pick = lst[j]; break; }
+                        if (ci >= u) { pick = lst[j]; found = true; }
                     }
                 }
                 shi[6] = pick;
@@ -788,7 +847,7 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
         }
     }
     if (tid == 0) {
-        a.tok_out[r] = tok;
+        if (a.tok_out) a.tok_out[r] = tok;
         if (a.step_tok) a.step_tok[slot] = tok;
         if (a.hist_append && a.hist && a.hist_len) {
             if (hl < a.hist_stride) {
@@ -798,6 +857,13 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
         }
         if (a.done && tok == a.stop_token) a.done[slot] = 1;
     }
+    __syncthreads();
+    return tok;
+}
+
+__global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArgs a) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    sample_row_block(a, blockIdx.x, smraw);
 }
 
 // exp test hook

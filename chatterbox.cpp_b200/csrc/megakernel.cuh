@@ -1,4 +1,575 @@
-// megakernel.cuh — persistent batch-1 decode step (filled in below).
+// megakernel.cuh — persistent batch-1 T3 decode: one cooperative launch runs
+// n_steps full decode steps (embedding, 24 layers, head, sampler).
+//
+// Why: at batch 1 a T3 step moves ~190 MB (25-30 us of HBM time on a B200)
+// but is a chain of ~120 dependent matrix-vector products, each needing the
+// whole previous vector.  As separate kernels every link costs a launch;
+// here every CTA (one per SM) stays resident and the links become waits on
+// epoch-tagged 8-byte slots:
+//
+//   slot = (epoch << 32) | float_bits, written with one 64-bit store.
+//
+// A consumer polls the slots of the vector it needs until every epoch
+// matches, so the wait and the data transfer are a single L2 round trip and
+// producers need no atomics.  Each CTA issues the loads of its weight slice
+// for a phase BEFORE waiting for that phase's input, so weight streaming
+// overlaps the dependency latency.
+//
+// Phases per layer (rows split evenly over the G CTAs):
+//   P1 LN1 + QKV GEMV (+ K/V append to the f16 cache)        -> q,k,v slots
+//   P2 attention, CTA h < n_head owns head h                  -> attn slots
+//   P3 proj GEMV + bias + residual                            -> x_mid slots
+//   P4 LN2 + fc GEMV + bias + GELU                            -> h slots
+//   P5 fc2 GEMV + bias + residual                             -> x slots
+// then LN_f + head GEMV -> logit slots, CTA 0 runs the sampler, publishes
+// the token slot, and every CTA builds the next step's embedding itself.
+//
+// Every wait is bounded (MK_SPIN polls); on timeout the CTA raises the abort
+// flag and the error word, and all CTAs leave at their next wait.
 #pragma once
-struct MegaState { int ready = 0; };
-inline void mega_free(MegaState & m) { m.ready = 0; }
+
+#include "kernels.cuh"
+
+#define MK_THREADS 512
+#define MK_MAX_POS 640            // positions whose K/V fit the attention stage
+#define MK_SPIN (1u << 21)        // polls per wait before giving up (~1 s)
+#define MK_MAXI 3                 // weight items (32-element blocks) per thread per phase
+
+// slot buffer offsets (in u64 slots)
+#define MK_LL_QKV 0
+#define MK_LL_ATT (MK_LL_QKV + 3072)
+#define MK_LL_XM (MK_LL_ATT + 1024)
+#define MK_LL_H (MK_LL_XM + 1024)
+#define MK_LL_X (MK_LL_H + 4096)
+#define MK_LL_LOG (MK_LL_X + 1024)
+#define MK_LL_TOK (MK_LL_LOG + T3B_SAMPLER_VMAX)
+#define MK_LL_TOTAL (MK_LL_TOK + 32)
+
+struct MkMat { const uint8_t * w; int type; int rb; };
+struct MkLayer {
+    const float * ln1g, * ln1b, * ln2g, * ln2b, * bqkv, * bo, * bfc, * bfc2;
+    MkMat qkv, o, fc, fc2;
+};
+
+struct MegaArgs {
+    const MkLayer * layers; int n_layer;
+    const __half * semb; const float * wpe; const float * lnfg; const float * lnfb;
+    MkMat head; const float * headb;
+    int V; float eps;
+    __half * kv; size_t layer_stride; size_t v_off; int max_ctx;
+    int p0, n_steps, ignore_stop, stop_token;
+    unsigned long long * ll;
+    unsigned * err; int * abort_flag; const int * cancel;
+    int * steps_done;
+    float * trace;                 // nullable: [n_steps + 1][V] logits, row 0 = prefill
+    SampArgs samp;
+};
+
+struct MegaState {
+    int ready = 0;
+    MkLayer * layers = nullptr;
+    unsigned long long * ll = nullptr;
+    int * abort_flag = nullptr;
+    int * steps_done = nullptr;
+    int * cancel_host = nullptr;   // mapped pinned flag written by t3b_cancel
+    int * cancel_dev = nullptr;
+    int grid = 0;
+    size_t smem = 0;
+};
+inline void mega_free(MegaState & m) {
+    if (m.layers) cudaFree(m.layers);
+    if (m.ll) cudaFree(m.ll);
+    if (m.abort_flag) cudaFree(m.abort_flag);
+    if (m.steps_done) cudaFree(m.steps_done);
+    if (m.cancel_host) cudaFreeHost(m.cancel_host);
+    m = MegaState();
+}
+
+// ---------------------------------------------------------------------------
+// slots
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ll_put(unsigned long long * p, unsigned epoch, float v) {
+    const unsigned long long w = ((unsigned long long) epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_get(const unsigned long long * p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Wait until slots [0, n) carry `epoch`; copy their floats to dst (smem).
+// Each thread keeps up to E slots in flight, so the whole vector costs one
+// round trip once it is ready.  Returns false when the wait gave up.
+template <int E>
+__device__ bool ll_wait(const unsigned long long * buf, int n, unsigned epoch, float * dst, const MegaArgs & a) {
+    const int tid = threadIdx.x;
+    unsigned long long v[E];
+    bool ok = true;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = tid + e * MK_THREADS;
+        v[e] = i < n ? ll_get(buf + i) : ((unsigned long long) epoch << 32);
+    }
+    unsigned spins = 0;
+    while (true) {
+        bool all = true;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            if ((unsigned) (v[e] >> 32) != epoch) {
+                all = false;
+                v[e] = ll_get(buf + tid + e * MK_THREADS);
+            }
+        }
+        if (all) break;
+        if (++spins > MK_SPIN || ((spins & 1023u) == 0 && *(volatile int *) a.abort_flag)) {
+            ok = false;
+            if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+            break;
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = tid + e * MK_THREADS;
+        if (i < n) dst[i] = __uint_as_float((unsigned) v[e]);
+    }
+    __threadfence();   // acquire side: later reads of data published before the slots
+    return __syncthreads_and(ok) != 0;
+}
+
+// ---------------------------------------------------------------------------
+// activation prep in shared memory (same arithmetic as prep_act_kernel)
+// ---------------------------------------------------------------------------
+struct MkAct {
+    float * v;      // input vector [K]
+    int8_t * q;     // Q8_0 quants [K]
+    float * d;      // block scales [K/32]
+    int * s;        // block sums [K/32]
+    __half * h;     // f16 copy [K] (F16 weights)
+};
+
+__device__ void mk_layernorm(float * v, int K, const float * g, const float * b, float eps, double * redd) {
+    const int tid = threadIdx.x;
+    double s = 0.0;
+    for (int i = tid; i < K; i += MK_THREADS) s += (double) v[i];
+    s = block_sum_d(s, redd);
+    const float mean = (float) (s / K);
+    double s2 = 0.0;
+    for (int i = tid; i < K; i += MK_THREADS) {
+        const float t = __fsub_rn(v[i], mean);
+        s2 += (double) __fmul_rn(t, t);
+    }
+    s2 = block_sum_d(s2, redd);
+    const float var = (float) (s2 / K);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    __syncthreads();
+    for (int i = tid; i < K; i += MK_THREADS) {
+        const float t = __fsub_rn(v[i], mean);
+        v[i] = __fadd_rn(__fmul_rn(__fmul_rn(t, scale), g[i]), b[i]);
+    }
+    __syncthreads();
+}
+
+__device__ void mk_quantize(const MkAct & x, int K, bool f16) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    if (f16) {
+        for (int i = tid; i < K; i += MK_THREADS) x.h[i] = __float2half_rn(x.v[i]);
+    } else {
+        for (int blk = w; blk < K / 32; blk += MK_THREADS / 32) {
+            const float v = x.v[blk * 32 + lane];
+            const float amax = warp_max(fabsf(v));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q = (int) roundf(__fmul_rn(v, id));
+            x.q[blk * 32 + lane] = (int8_t) q;
+            const int s = warp_sum_i(q);
+            if (lane == 0) { x.d[blk] = __half2float(__float2half_rn(d)); x.s[blk] = s; }
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// weight slices: items are (row, 32-element block) pairs of rows [r0, r1)
+// ---------------------------------------------------------------------------
+template <int T> struct MkW { static constexpr int QW = T == T3B_Q4_0 ? 1 : (T == T3B_Q8_0 ? 2 : 4); };
+
+template <int T>
+struct MkPref {
+    uint4 q[MK_MAXI][MkW<T>::QW];
+    float d[MK_MAXI];
+};
+
+template <int T>
+__device__ __forceinline__ void mk_prefetch(const MkMat & W, int K, int r0, int r1, MkPref<T> & pf) {
+    const int NB = K / 32;
+    const int nit = (r1 - r0) * NB;
+#pragma unroll
+    for (int j = 0; j < MK_MAXI; ++j) {
+        const int i = threadIdx.x + j * MK_THREADS;
+        if (i < nit) {
+            const int row = r0 + i / NB, b = i % NB;
+            const uint8_t * wr = W.w + (size_t) row * W.rb;
+            if (T == T3B_Q4_0) {
+                pf.q[j][0] = __ldg((const uint4 *) (wr + b * 16));
+                pf.d[j] = __half2float(__ldg((const __half *) (wr + K / 2 + b * 2)));
+            } else if (T == T3B_Q8_0) {
+                pf.q[j][0] = __ldg((const uint4 *) (wr + b * 32));
+                pf.q[j][1 % MkW<T>::QW] = __ldg((const uint4 *) (wr + b * 32 + 16));
+                pf.d[j] = __half2float(__ldg((const __half *) (wr + K + b * 2)));
+            } else {
+#pragma unroll
+                for (int c = 0; c < MkW<T>::QW; ++c) pf.q[j][c] = __ldg((const uint4 *) (wr + b * 64 + c * 16));
+                pf.d[j] = 1.0f;
+            }
+        }
+    }
+}
+
+// Dot products of the prefetched items with the prepared activation; row
+// sums (bias not added) land in rowsum[0 .. r1-r0).
+template <int T>
+__device__ void mk_dot(const MkPref<T> & pf, int K, int r0, int r1, const MkAct & x, float * part, float * rowsum) {
+    const int NB = K / 32, NP = NB / 32;   // warp portions per row
+    const int nit = (r1 - r0) * NB;
+    const int tid = threadIdx.x, lane = tid & 31;
+#pragma unroll
+    for (int j = 0; j < MK_MAXI; ++j) {
+        const int i0 = j * MK_THREADS + (tid & ~31);   // first item of this warp
+        if (i0 >= nit) break;                          // warp-uniform
+        const int i = i0 + lane;
+        const int b = i % NB;
+        float v = 0.0f;
+        if (T == T3B_Q4_0) {
+            const int * xv = (const int *) (x.q + b * 32);
+            const uint4 qv = pf.q[j][0];
+            int si = 0;
+            si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), xv[0], si);
+            si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), xv[4], si);
+            si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), xv[1], si);
+            si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), xv[5], si);
+            si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), xv[2], si);
+            si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), xv[6], si);
+            si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), xv[3], si);
+            si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), xv[7], si);
+            si -= 8 * x.s[b];
+            v = __fmul_rn(__fmul_rn((float) si, pf.d[j]), x.d[b]);
+        } else if (T == T3B_Q8_0) {
+            const int * xv = (const int *) (x.q + b * 32);
+            const uint4 q0 = pf.q[j][0], q1 = pf.q[j][1 % MkW<T>::QW];
+            int si = 0;
+            si = __dp4a((int) q0.x, xv[0], si); si = __dp4a((int) q0.y, xv[1], si);
+            si = __dp4a((int) q0.z, xv[2], si); si = __dp4a((int) q0.w, xv[3], si);
+            si = __dp4a((int) q1.x, xv[4], si); si = __dp4a((int) q1.y, xv[5], si);
+            si = __dp4a((int) q1.z, xv[6], si); si = __dp4a((int) q1.w, xv[7], si);
+            v = __fmul_rn(__fmul_rn((float) si, pf.d[j]), x.d[b]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < MkW<T>::QW; ++c) {
+                const uint4 wv = pf.q[j][c];
+                const __half2 * wp = (const __half2 *) &wv;
+                const __half2 * xp = (const __half2 *) (x.h + b * 32 + c * 8);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float2 wf = __half22float2(wp[t]), xf = __half22float2(xp[t]);
+                    v = fmaf(wf.x, xf.x, v);
+                    v = fmaf(wf.y, xf.y, v);
+                }
+            }
+        }
+        v = warp_sum(v);
+        if (lane == 0) part[i0 / 32] = v;             // (row, portion) in item order
+    }
+    __syncthreads();
+    for (int r = tid; r < r1 - r0; r += MK_THREADS) {
+        float acc = 0.0f;
+        for (int p = 0; p < NP; ++p) acc = __fadd_rn(acc, part[r * NP + p]);
+        rowsum[r] = acc;
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int mk_r0(int N, int c, int G) { return (int) (((long long) N * c) / G); }
+
+// rows of one GEMV phase: prefetch (before the caller's wait), then dot
+#define MK_GEMV_BEGIN(W, K, N)                                                   \
+    const int r0_ = mk_r0((N), blockIdx.x, gridDim.x), r1_ = mk_r0((N), blockIdx.x + 1, gridDim.x); \
+    MkPref<T> pf_;                                                              \
+    mk_prefetch<T>((W), (K), r0_, r1_, pf_);
+
+// LN_f + speech_head rows of this CTA; the head keeps its own weight type.
+template <int HT>
+__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, unsigned eh, float * vec, const MkAct & act, float * part,
+                        float * rowsum, double * redd, const unsigned long long * LLx, unsigned long long * LLl) {
+    const int D = 1024, tid = threadIdx.x;
+    const int r0 = mk_r0(a.V, blockIdx.x, gridDim.x), r1 = mk_r0(a.V, blockIdx.x + 1, gridDim.x);
+    MkPref<HT> pf;
+    mk_prefetch<HT>(a.head, D, r0, r1, pf);
+    if (!ll_wait<2>(LLx, D, eh - 1u, vec, a)) return false;
+    mk_layernorm(vec, D, a.lnfg, a.lnfb, a.eps, redd);
+    mk_quantize(act, D, HT == T3B_F16);
+    mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
+    float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
+    for (int r = tid; r < r1 - r0; r += MK_THREADS) {
+        const int n = r0 + r;
+        const float v = __fadd_rn(rowsum[r], a.headb[n]);
+        if (tr) tr[n] = v;
+        ll_put(LLl + n, eh, v);
+    }
+    return true;
+}
+
+// Dynamic shared memory the megakernel needs.
+constexpr size_t mk_smem_bytes() {
+    return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 512) * 4;
+}
+static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
+
+template <int T>
+__global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    // persistent region at the top of shared memory: residual stream copies
+    const int D = 1024;
+    __shared__ float xres[1024];          // layer input x (residual for P3)
+    __shared__ float xmid[1024];          // x after attention (residual for P5)
+    __shared__ double redd[32];
+    __shared__ float rowsum[128];
+    __shared__ int tokv;
+    // scratch (reused by every phase): vec[4096] f32 | q[4096] i8 | d,s [128] | h[4096] f16 | part[512]
+    float * vec = (float *) smem;
+    MkAct act;
+    act.v = vec;
+    act.q = (int8_t *) (smem + 16384);
+    act.d = (float *) (smem + 16384 + 4096);
+    act.s = (int *) (smem + 16384 + 4096 + 512);
+    act.h = (__half *) (smem + 16384 + 4096 + 1024);
+    float * part = (float *) (smem + 16384 + 4096 + 1024 + 8192);
+    // attention stage and sampler reuse the same bytes
+    __half * kst = (__half *) smem;
+    __half * vst = kst + MK_MAX_POS * T3B_HD;
+    float * att_s = (float *) (smem + 2 * MK_MAX_POS * T3B_HD * 2);   // qkv[192] | p[MK_MAX_POS] | o[8][64]
+
+    const int tid = threadIdx.x, cta = blockIdx.x;
+    const int NL = a.n_layer;
+    const unsigned EPS = 5u * NL + 2u;    // epochs per step
+    unsigned long long * LLq = a.ll + MK_LL_QKV, * LLa = a.ll + MK_LL_ATT, * LLm = a.ll + MK_LL_XM;
+    unsigned long long * LLh = a.ll + MK_LL_H, * LLx = a.ll + MK_LL_X, * LLl = a.ll + MK_LL_LOG, * LLt = a.ll + MK_LL_TOK;
+    const int Hn = 16;
+
+    int tok = a.samp.step_tok[a.samp.slot_of ? a.samp.slot_of[0] : 0];
+    for (int step = 0; step < a.n_steps; ++step) {
+        const int pos = a.p0 + step;
+        const unsigned e0 = 1u + (unsigned) step * EPS;
+        // embedding: x = speech_emb[tok] + wpe[pos]
+        for (int i = tid; i < D; i += MK_THREADS)
+            xres[i] = __fadd_rn(__half2float(a.semb[(size_t) tok * D + i]), a.wpe[(size_t) pos * D + i]);
+        __syncthreads();
+        for (int l = 0; l < NL; ++l) {
+            const MkLayer & Ly = a.layers[l];
+            const unsigned eb = e0 + 5u * l;
+            // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
+            {
+                MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
+                if (l > 0) {   // layer input = previous layer's P5 output
+                    if (!ll_wait<2>(LLx, D, eb - 1u, xres, a)) return;
+                }
+                for (int i = tid; i < D; i += MK_THREADS) vec[i] = xres[i];
+                __syncthreads();
+                mk_layernorm(vec, D, Ly.ln1g, Ly.ln1b, a.eps, redd);
+                mk_quantize(act, D, T == T3B_F16);
+                mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                __half * kb = a.kv + (size_t) l * a.layer_stride;
+                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
+                    const int n = r0_ + r;
+                    const float v = __fadd_rn(rowsum[r], Ly.bqkv[n]);
+                    if (n >= D) {
+                        const int which = n >= 2 * D, rem = n - D - which * D;
+                        __half * base = kb + (which ? a.v_off : 0);
+                        base[((size_t) (rem >> 6) * a.max_ctx + pos) * T3B_HD + (rem & 63)] = __float2half_rn(v);
+                    }
+                    __threadfence();
+                    ll_put(LLq + n, eb, v);
+                }
+            }
+            // ---------------- P2: attention (CTA h < 16 owns head h) ----------
+            if (cta < Hn) {
+                const int h = cta;
+                const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) h * a.max_ctx * T3B_HD;
+                const __half * vb = kb + a.v_off;
+                // stage K/V of positions [0, pos) while q/k/v are computed
+                const int nchunk = pos * (T3B_HD * 2 / 16);     // 16-byte chunks per tensor
+                for (int i = tid; i < nchunk; i += MK_THREADS) {
+                    const unsigned sk = (unsigned) __cvta_generic_to_shared(kst) + i * 16;
+                    const unsigned sv = (unsigned) __cvta_generic_to_shared(vst) + i * 16;
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sk), "l"(kb + i * 8) : "memory");
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sv), "l"(vb + i * 8) : "memory");
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                // q, k, v of head h for this position
+                float * qkvh = att_s;   // [192]
+                {
+                    unsigned long long w[1];
+                    const int i = tid;
+                    bool ok = true;
+                    if (i < 192) {
+                        const int n = (i / 64) * D + h * 64 + (i & 63);
+                        unsigned spins = 0;
+                        w[0] = ll_get(LLq + n);
+                        while ((unsigned) (w[0] >> 32) != eb) {
+                            w[0] = ll_get(LLq + n);
+                            if (++spins > MK_SPIN || ((spins & 1023u) == 0 && *(volatile int *) a.abort_flag)) {
+                                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                                ok = false;
+                                break;
+                            }
+                        }
+                        qkvh[i] = __uint_as_float((unsigned) w[0]);
+                    }
+                    asm volatile("cp.async.wait_all;" ::: "memory");
+                    __threadfence();
+                    if (!__syncthreads_and(ok)) return;
+                }
+                if (tid < T3B_HD) {
+                    kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
+                    vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
+                }
+                __syncthreads();
+                const int L = pos + 1;
+                // scores: thread t owns keys t, t + 512
+                float sc[2];
+                float lm = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int j = tid + u * MK_THREADS;
+                    sc[u] = -INFINITY;
+                    if (j < L) {
+                        const uint4 * kp = (const uint4 *) (kst + (size_t) j * T3B_HD);
+                        float dot = 0.0f;
+#pragma unroll
+                        for (int cidx = 0; cidx < 8; ++cidx) {
+                            const uint4 uu = kp[cidx];
+                            const __half2 * hp = (const __half2 *) &uu;
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                const float2 f = __half22float2(hp[t]);
+                                dot = fmaf(qkvh[cidx * 8 + 2 * t], f.x, dot);
+                                dot = fmaf(qkvh[cidx * 8 + 2 * t + 1], f.y, dot);
+                            }
+                        }
+                        sc[u] = dot * 0.125f;
+                        lm = fmaxf(lm, sc[u]);
+                    }
+                }
+                float * rf = (float *) redd;
+                const float mx = block_max(lm, rf);
+                float * pw = att_s + 256;  // [L] weights
+                float ls = 0.0f;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int j = tid + u * MK_THREADS;
+                    if (j < L) { const float p = expf(sc[u] - mx); pw[j] = p; ls += p; }
+                }
+                const float lsum = block_sum(ls, rf);
+                __syncthreads();
+                // o[d] = sum_j p_j v_j[d]: 8 key groups x 64 dims
+                {
+                    const int d = tid & 63, g = tid >> 6;
+                    float o = 0.0f;
+                    for (int j = g; j < L; j += 8) o = fmaf(pw[j], __half2float(vst[(size_t) j * T3B_HD + d]), o);
+                    float * og = att_s + 256 + MK_MAX_POS;   // [8][64]
+                    og[g * 64 + d] = o;
+                    __syncthreads();
+                    if (tid < 64) {
+                        float t = 0.0f;
+                        for (int gg = 0; gg < 8; ++gg) t += og[gg * 64 + tid];
+                        ll_put(LLa + h * 64 + tid, eb + 1u, t / lsum);
+                    }
+                }
+            }
+            // ---------------- P3: proj + bias + residual -----------------------
+            {
+                MK_GEMV_BEGIN(Ly.o, D, D)
+                if (!ll_wait<2>(LLa, D, eb + 1u, vec, a)) return;
+                mk_quantize(act, D, T == T3B_F16);
+                mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
+                    const int n = r0_ + r;
+                    ll_put(LLm + n, eb + 2u, __fadd_rn(__fadd_rn(rowsum[r], Ly.bo[n]), xres[n]));
+                }
+            }
+            // ---------------- P4: LN2 + fc + GELU ------------------------------
+            {
+                MK_GEMV_BEGIN(Ly.fc, D, 4 * D)
+                if (!ll_wait<2>(LLm, D, eb + 2u, xmid, a)) return;
+                for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
+                __syncthreads();
+                mk_layernorm(vec, D, Ly.ln2g, Ly.ln2b, a.eps, redd);
+                mk_quantize(act, D, T == T3B_F16);
+                mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
+                    const int n = r0_ + r;
+                    ll_put(LLh + n, eb + 3u, gelu_ggml(__fadd_rn(rowsum[r], Ly.bfc[n])));
+                }
+            }
+            // ---------------- P5: fc2 + bias + residual ------------------------
+            {
+                MK_GEMV_BEGIN(Ly.fc2, 4 * D, D)
+                if (!ll_wait<8>(LLh, 4 * D, eb + 3u, vec, a)) return;
+                mk_quantize(act, 4 * D, T == T3B_F16);
+                mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
+                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
+                    const int n = r0_ + r;
+                    ll_put(LLx + n, eb + 4u, __fadd_rn(__fadd_rn(rowsum[r], Ly.bfc2[n]), xmid[n]));
+                }
+            }
+        }
+        // ---------------- head: LN_f + speech_head ------------------------------
+        const unsigned eh = e0 + 5u * NL;
+        {
+            bool ok;
+            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, eh, vec, act, part, rowsum, redd, LLx, LLl);
+            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, eh, vec, act, part, rowsum, redd, LLx, LLl);
+            else ok = mk_head<T3B_Q4_0>(a, step, eh, vec, act, part, rowsum, redd, LLx, LLl);
+            if (!ok) return;
+        }
+        // ---------------- sampler (CTA 0) and token broadcast -------------------
+        if (cta == 0) {
+            // host cancel flag (mapped memory): read before the wait so the
+            // PCIe round trip overlaps it
+            const int cancelled = a.cancel ? *(volatile const int *) a.cancel : 0;
+            float * lg = (float *) (smem + T3B_SAMPLER_SMEM);   // logits staged after the sampler's arrays
+            if (!ll_wait<(T3B_SAMPLER_VMAX + MK_THREADS - 1) / MK_THREADS>(LLl, a.V, eh, lg, a)) return;
+            SampArgs sa = a.samp;
+            sa.cond = lg; sa.cond_stride = 0; sa.uncond = nullptr;
+            int t = sample_row_block(sa, 0, smem);
+            if (tid == 0) {
+                const int stop = (t == a.stop_token && !a.ignore_stop) || cancelled || t < 0;
+                __threadfence();
+                ll_put(LLt, eh + 1u, __int_as_float((t & 0xffff) | (stop ? 0x10000 : 0)));
+                *a.steps_done = step + 1;
+            }
+        }
+        {
+            if (tid == 0) {
+                unsigned long long w = ll_get(LLt);
+                unsigned spins = 0;
+                while ((unsigned) (w >> 32) != eh + 1u) {
+                    w = ll_get(LLt);
+                    if (++spins > MK_SPIN || ((spins & 1023u) == 0 && *(volatile int *) a.abort_flag)) {
+                        if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                        w = ((unsigned long long) (eh + 1u) << 32) | 0x10000u;
+                        break;
+                    }
+                }
+                tokv = __float_as_int(__uint_as_float((unsigned) w));
+            }
+            __syncthreads();
+            const int tv = tokv;
+            if (tv & 0x10000) return;
+            tok = tv & 0xffff;
+        }
+    }
+}

@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -172,6 +173,8 @@ struct t3b_ctx {
     std::map<std::vector<int>, StepGraph> graphs;
     // persistent batch-1 decode kernel state
     MegaState mega{};
+    // logits trace (debug)
+    float * trace = nullptr; int trace_cap = 0;
 };
 
 #undef ERRP
@@ -446,6 +449,7 @@ void t3b_destroy(t3b_ctx * ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->st);
     free_streams(ctx);
+    if (ctx->trace) cudaFree(ctx->trace);
     for (void * p : ctx->allocs) cudaFree(p);
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
@@ -453,9 +457,34 @@ void t3b_destroy(t3b_ctx * ctx) {
     delete ctx;
 }
 
-void t3b_cancel(t3b_ctx * ctx) { if (ctx) ctx->cancel = 1; }
+void t3b_cancel(t3b_ctx * ctx) {
+    if (!ctx) return;
+    ctx->cancel = 1;
+    if (ctx->mega.cancel_host) *(volatile int *) ctx->mega.cancel_host = 1;
+}
 float t3b_last_device_ms(const t3b_ctx * ctx) { return ctx ? ctx->last_ms : 0.0f; }
 void * t3b_stream_handle(const t3b_ctx * ctx) { return ctx ? (void *) ctx->st : nullptr; }
+
+int t3b_trace_logits(t3b_ctx * ctx, int max_steps) {
+    if (!ctx || max_steps < 0) return T3B_ERR_ARG;
+    CK(cudaSetDevice(ctx->device));
+    if (ctx->trace) { CK(cudaFree(ctx->trace)); ctx->trace = nullptr; ctx->trace_cap = 0; }
+    if (max_steps > 0) {
+        CK(cudaMalloc(&ctx->trace, sizeof(float) * (size_t) (max_steps + 1) * ctx->hp.n_speech_vocab));
+        ctx->trace_cap = max_steps;
+    }
+    return T3B_OK;
+}
+
+int t3b_get_logits_trace(t3b_ctx * ctx, float * out, int n) {
+    if (!ctx || !out || n < 0 || n > ctx->trace_cap + 1 || !ctx->trace) {
+        if (ctx) set_err(&ctx->err, "t3b_get_logits_trace: bad args or tracing off");
+        return T3B_ERR_ARG;
+    }
+    CK(cudaSetDevice(ctx->device));
+    CK(cudaMemcpy(out, ctx->trace, sizeof(float) * (size_t) n * ctx->hp.n_speech_vocab, cudaMemcpyDeviceToHost));
+    return T3B_OK;
+}
 
 int t3b_stream_alloc(t3b_ctx * ctx, int n_streams, int max_ctx, int cfg) {
     if (!ctx) return T3B_ERR_ARG;
@@ -679,6 +708,105 @@ int ensure_graph(t3b_ctx * ctx, int n, bool sample, StepGraph ** out) {
     return T3B_OK;
 }
 
+
+// Persistent batch-1 decode (megakernel.cuh).  Eligible when one stream
+// without CFG decodes a T3 with n_embd 1024 / 16 heads, every layer matrix in
+// one of Q4_0 / Q8_0 / F16, and the positions fit the attention stage.  The
+// CTA count is the SM count; each CTA's row slices must fit its registers.
+bool mega_eligible(t3b_ctx * ctx, int n, int max_pos_after) {
+    if (getenv("T3B_NO_MEGAKERNEL")) return false;
+    if (n != 1 || ctx->rps != 1) return false;
+    if (ctx->hp.n_embd != 1024 || ctx->hp.n_head != 16) return false;
+    if (ctx->hp.n_speech_vocab > T3B_SAMPLER_VMAX) return false;
+    if (max_pos_after > MK_MAX_POS) return false;
+    const int T = ctx->L[0].attn.type;
+    for (const Layer & Ly : ctx->L)
+        if (Ly.attn.type != T || Ly.proj.type != T || Ly.fc.type != T || Ly.fc2.type != T) return false;
+    return T == T3B_Q4_0 || T == T3B_Q8_0 || T == T3B_F16;
+}
+
+int mega_prepare(t3b_ctx * ctx) {
+    MegaState & m = ctx->mega;
+    if (m.ready) return T3B_OK;
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device));
+    const int G = sms;
+    auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
+    // per-CTA limits of the register prefetch (MK_MAXI items of 32 elements
+    // per thread) and of the row scratch
+    if (cdiv(3 * 1024, G) * 32 > MK_MAXI * MK_THREADS || cdiv(4 * 1024, G) * 32 > MK_MAXI * MK_THREADS ||
+        cdiv(1024, G) * 128 > MK_MAXI * MK_THREADS || cdiv(ctx->hp.n_speech_vocab, G) * 32 > MK_MAXI * MK_THREADS ||
+        cdiv(ctx->hp.n_speech_vocab, G) > 128 || G < 16) {
+        set_err(&ctx->err, "megakernel: %d SMs too few for the row split", G);
+        return T3B_ERR_STATE;
+    }
+    std::vector<MkLayer> hl(ctx->hp.n_layer);
+    for (int l = 0; l < ctx->hp.n_layer; ++l) {
+        const Layer & Ly = ctx->L[l];
+        hl[l].ln1g = Ly.ln1g; hl[l].ln1b = Ly.ln1b; hl[l].ln2g = Ly.ln2g; hl[l].ln2b = Ly.ln2b;
+        hl[l].bqkv = Ly.attn_b; hl[l].bo = Ly.proj_b; hl[l].bfc = Ly.fc_b; hl[l].bfc2 = Ly.fc2_b;
+        hl[l].qkv = {Ly.attn.p, Ly.attn.type, Ly.attn.rb};
+        hl[l].o = {Ly.proj.p, Ly.proj.type, Ly.proj.rb};
+        hl[l].fc = {Ly.fc.p, Ly.fc.type, Ly.fc.rb};
+        hl[l].fc2 = {Ly.fc2.p, Ly.fc2.type, Ly.fc2.rb};
+    }
+    CK(cudaMalloc(&m.layers, sizeof(MkLayer) * hl.size()));
+    CK(cudaMemcpy(m.layers, hl.data(), sizeof(MkLayer) * hl.size(), cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&m.ll, sizeof(unsigned long long) * MK_LL_TOTAL));
+    CK(cudaMalloc(&m.abort_flag, sizeof(int)));
+    CK(cudaMalloc(&m.steps_done, sizeof(int)));
+    CK(cudaHostAlloc(&m.cancel_host, sizeof(int), cudaHostAllocMapped));
+    *m.cancel_host = 0;
+    CK(cudaHostGetDevicePointer(&m.cancel_dev, m.cancel_host, 0));
+    m.smem = mk_smem_bytes();
+    const int T = ctx->L[0].attn.type;
+    const void * fn = T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0>
+                    : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0>
+                                    : (const void *) t3_decode_megakernel<T3B_F16>;
+    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) m.smem));
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, MK_THREADS, m.smem));
+    if (per_sm < 1) { set_err(&ctx->err, "megakernel: does not fit on an SM"); return T3B_ERR_STATE; }
+    m.grid = G;
+    m.ready = 1;
+    return T3B_OK;
+}
+
+// One cooperative launch decoding max_steps steps of stream `slot` (row
+// slot).  The first token is already in step_tok (sampled from the prefill
+// logits).  Returns the number of steps run in *steps.
+int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop, int * steps) {
+    MegaState & m = ctx->mega;
+    cudaStream_t st = ctx->st;
+    const int H = ctx->hp.n_head;
+    MegaArgs a{};
+    a.layers = m.layers; a.n_layer = ctx->hp.n_layer;
+    a.semb = ctx->semb; a.wpe = ctx->wpe; a.lnfg = ctx->lnf_g; a.lnfb = ctx->lnf_b;
+    a.head = {ctx->head.p, ctx->head.type, ctx->head.rb}; a.headb = ctx->head_b;
+    a.V = ctx->hp.n_speech_vocab; a.eps = ctx->hp.eps;
+    a.kv = ctx->kv + (size_t) slot * ctx->row_elems;
+    a.layer_stride = (size_t) 2 * H * ctx->max_ctx * T3B_HD;
+    a.v_off = (size_t) H * ctx->max_ctx * T3B_HD;
+    a.max_ctx = ctx->max_ctx;
+    a.p0 = p0; a.n_steps = max_steps; a.ignore_stop = ignore_stop; a.stop_token = ctx->hp.stop_speech_token;
+    a.ll = m.ll; a.err = ctx->err_word; a.abort_flag = m.abort_flag; a.cancel = m.cancel_dev;
+    a.steps_done = m.steps_done;
+    a.trace = ctx->trace_cap >= max_steps ? ctx->trace : nullptr;
+    a.samp = sampler_args(ctx, false);
+    a.samp.done = nullptr;
+    CK(cudaMemsetAsync(m.ll, 0, sizeof(unsigned long long) * MK_LL_TOTAL, st));
+    CK(cudaMemsetAsync(m.abort_flag, 0, sizeof(int), st));
+    CK(cudaMemsetAsync(m.steps_done, 0, sizeof(int), st));
+    void * args[] = {&a};
+    const int T = ctx->L[0].attn.type;
+    const void * fn = T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0>
+                    : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0>
+                                    : (const void *) t3_decode_megakernel<T3B_F16>;
+    CK(cudaLaunchCooperativeKernel(fn, dim3(m.grid), dim3(MK_THREADS), args, m.smem, st));
+    CK(cudaMemcpyAsync(steps, m.steps_done, sizeof(int), cudaMemcpyDeviceToHost, st));
+    return T3B_OK;
+}
+
 int check_streams(t3b_ctx * ctx, int n, const int32_t * streams, std::vector<int> & slots) {
     if (ctx->S == 0) { set_err(&ctx->err, "no streams allocated"); return T3B_ERR_STATE; }
     if (n <= 0 || n > ctx->S) { set_err(&ctx->err, "bad stream count %d", n); return T3B_ERR_ARG; }
@@ -777,6 +905,7 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     CK(cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->st;
     ctx->cancel = 0;
+    if (ctx->mega.cancel_host) *(volatile int *) ctx->mega.cancel_host = 0;
     const int M = n * ctx->rps;
     // positions of every row must leave room for max_steps
     std::vector<int> pos(M);
@@ -801,10 +930,48 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     CK(cudaMemcpyAsync(ctx->done, zeros.data(), sizeof(int) * ctx->S, cudaMemcpyHostToDevice, st));
     // first token from the prefill logits (run_t3: sample before the loop)
     SampArgs a = sampler_args(ctx, !ignore_stop);
+    const bool mega = mega_eligible(ctx, n, max_pos + max_steps) && mega_prepare(ctx) == T3B_OK;
+    const bool trace = ctx->trace && ctx->trace_cap >= max_steps;
+    const size_t Vb = sizeof(float) * ctx->hp.n_speech_vocab;
+    if (trace) CK(cudaMemcpyAsync(ctx->trace, ctx->logits + (size_t) slots[0] * ctx->rps * ctx->hp.n_speech_vocab, Vb,
+                                  cudaMemcpyDeviceToDevice, st));
     CK(cudaEventRecord(ctx->ev0, st));
     sampler_kernel<<<n, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, st>>>(a);
     CK(cudaGetLastError());
     int steps_done = 0;
+    if (mega) {
+        // a stop token drawn from the prefill logits ends the loop at once
+        int first_stop = 0;
+        if (!ignore_stop) {
+            int t0 = 0;
+            CK(cudaMemcpyAsync(&t0, ctx->step_tok + slots[0], sizeof(int), cudaMemcpyDeviceToHost, st));
+            CK(cudaStreamSynchronize(st));
+            first_stop = t0 == ctx->hp.stop_speech_token;
+        }
+        int ran = 0;
+        if (!first_stop && max_steps > 0) {
+            rc = mega_decode(ctx, slots[0], pos[0], max_steps, ignore_stop, &ran);
+            if (rc != T3B_OK) return rc;
+        }
+        CK(cudaEventRecord(ctx->ev1, st));
+        CK(cudaStreamSynchronize(st));
+        cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1);
+        rc = check_dev_err(ctx);
+        if (rc != T3B_OK) return rc;
+        if (ctx->mega.cancel_host && *ctx->mega.cancel_host) {
+            *ctx->mega.cancel_host = 0;
+            set_err(&ctx->err, "t3b_decode: cancelled");
+            return T3B_ERR_CANCELLED;
+        }
+        ctx->pos_host[slots[0]] = pos[0] + ran;
+        std::vector<int> hl(ctx->S);
+        CK(cudaMemcpy(hl.data(), ctx->hist_len, sizeof(int) * ctx->S, cudaMemcpyDeviceToHost));
+        const int cnt = std::min(hl[slots[0]], max_steps + 1);
+        if (tokens_out) CK(cudaMemcpy(tokens_out, ctx->hist + (size_t) slots[0] * ctx->hist_cap, sizeof(int) * cnt,
+                                      cudaMemcpyDeviceToHost));
+        if (n_out) n_out[0] = cnt;
+        return T3B_OK;
+    }
     for (int s = 0; s < max_steps; ++s) {
         if (ctx->cancel) { set_err(&ctx->err, "t3b_decode: cancelled"); CK(cudaStreamSynchronize(st)); return T3B_ERR_CANCELLED; }
         if (!ignore_stop && s > 0 && (s % 16) == 0) {
@@ -816,6 +983,10 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
             if (all) break;
         }
         CK(cudaGraphLaunch(g->ge, st));
+        if (trace)
+            CK(cudaMemcpyAsync(ctx->trace + (size_t) (s + 1) * ctx->hp.n_speech_vocab,
+                               ctx->logits + (size_t) slots[0] * ctx->rps * ctx->hp.n_speech_vocab, Vb,
+                               cudaMemcpyDeviceToDevice, st));
         ++steps_done;
     }
     CK(cudaEventRecord(ctx->ev1, st));

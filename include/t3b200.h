@@ -162,6 +162,13 @@ void t3b_cancel(t3b_ctx * ctx);
 /* Device time of the last t3b_decode / t3b_step call, in milliseconds. */
 float t3b_last_device_ms(const t3b_ctx * ctx);
 
+/* Logits tracing (debug): with max_steps > 0, every t3b_decode records the
+ * logits its first stream samples from (prefill logits, then each step's)
+ * into a device buffer of max_steps + 1 rows; t3b_get_logits_trace copies
+ * the first n rows to host memory [n][n_speech_vocab].  0 disables. */
+int t3b_trace_logits(t3b_ctx * ctx, int max_steps);
+int t3b_get_logits_trace(t3b_ctx * ctx, float * out, int n);
+
 /* The cudaStream_t (as void*) every kernel of this context runs on, for
  * callers that order their own work or timing events against it. */
 void * t3b_stream_handle(const t3b_ctx * ctx);

@@ -198,32 +198,63 @@ def test_sampler_sequences_golden(pkg):
         assert out == s["tokens"]
 
 
-def test_decode_loop_tokens_follow_sampler_on_device_logits(pkg, orc):
-    """t3b_decode (graph-captured step + sampler on the device) emits the
-    tokens the oracle sampler draws from the same logits and mt19937 stream."""
-    hp, t, m = model(pkg, "q4_0", 2)
+def _decode_traced(pkg, m, text, params, seed, steps, graph_path):
+    """Device decode with the logits trace on; graph_path forces the
+    multi-kernel CUDA-graph loop instead of the persistent megakernel."""
+    if graph_path:
+        os.environ["T3B_NO_MEGAKERNEL"] = "1"
+    try:
+        m.trace_logits(steps)
+        m.prefill(0, text)
+        m.set_rng(0, pkg.T3B_RNG_MT19937, seed, 0)
+        toks = m.decode([pkg.SampleParams.make(**params)], steps, ignore_stop=True)[0]
+        tr = m.logits_trace(steps + 1)
+    finally:
+        os.environ.pop("T3B_NO_MEGAKERNEL", None)
+        m.trace_logits(0)
+    return toks, tr
+
+
+@pytest.mark.parametrize("graph_path", [False, True])
+@pytest.mark.parametrize("quant", ["q4_0", "f16"])
+def test_decode_loop_matches_oracle(pkg, orc, quant, graph_path):
+    """t3b_decode (persistent megakernel, or the CUDA-graph step loop): every
+    token is the one the oracle sampler draws from the logits the device
+    sampled from (exact, same mt19937 stream), and those logits match the
+    oracle's teacher-forced logits (tight for F16, the quantized path's
+    noise floor for Q4_0)."""
+    hp, t, m = model(pkg, quant, 2)
     m.alloc_streams(1, 512)
     text = _prompt(9, 30)
     params = dict(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2)
-    seed = 1234
-    m.prefill(0, text)
-    m.set_rng(0, pkg.T3B_RNG_MT19937, seed, 0)
-    toks = m.decode([pkg.SampleParams.make(**params)], 24, ignore_stop=True)[0]
-    assert toks.size == 25
-    # replay: step-by-step logits, oracle sampler on them
-    P, lg = m.prefill(0, text)
-    words = orc.mt19937_words(seed, 0, 200)
-    k = 0
-    hist = []
-    logits = lg[0]
-    for i in range(25):
-        tok, aux = orc.sample(logits, params, words[k], words[k + 1], hist=np.array(hist, np.int32))
-        k += 2
+    seed, steps = 1234, 24
+    toks, tr = _decode_traced(pkg, m, text, params, seed, steps, graph_path)
+    assert toks.size == steps + 1
+    words = orc.mt19937_words(seed, 0, 2 * steps + 4)
+    mir = orc.Model(hp, t, max_ctx=512, gemv_mode=1, gelu_f16=1, kv_f16=1)
+    P, lo = mir.prompt(text)
+    nz = max(noise_floor(orc, hp, t, text, [int(x) for x in toks[:steps]], 512))
+    for i in range(steps + 1):
+        tok, aux = orc.sample(tr[i], params, words[2 * i], words[2 * i + 1], hist=toks[:i].astype(np.int32))
         if not aux[2]:
-            assert tok == toks[i], i
-        hist.append(int(toks[i]))
-        if i < 24:
-            logits = m.step([int(toks[i])])[0, 0]
+            assert tok == toks[i], (i, tok, toks[i])
+        e = rel_err(tr[i], lo)
+        assert e < bound(quant, nz, 1e-3), (i, e, nz)
+        if i < steps:
+            lo = mir.step(P + i, int(toks[i]))
+
+
+def test_megakernel_matches_graph_path(pkg):
+    """F16 weights (continuous arithmetic): the persistent kernel and the
+    graph loop produce the same tokens and logits within 1e-4."""
+    hp, t, m = model(pkg, "f16", 2)
+    m.alloc_streams(1, 512)
+    text = _prompt(12, 40)
+    params = dict(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2)
+    ta, la = _decode_traced(pkg, m, text, params, 77, 32, False)
+    tb, lb = _decode_traced(pkg, m, text, params, 77, 32, True)
+    assert rel_err(la, lb) < 1e-4
+    assert ta.tolist() == tb.tolist()
 
 
 def test_decode_stops_at_stop_token(pkg):
