@@ -5,15 +5,14 @@
 // but is a chain of ~120 dependent matrix-vector products, each needing the
 // whole previous vector.  As separate kernels every link costs a launch;
 // here every CTA (one per SM) stays resident and the links become waits on
-// epoch-tagged 8-byte slots:
-//
-//   slot = (epoch << 32) | float_bits, written with one 64-bit store.
-//
-// A consumer polls the slots of the vector it needs until every epoch
-// matches, so the wait and the data transfer are a single L2 round trip and
-// producers need no atomics.  Each CTA issues the loads of its weight slice
-// for a phase BEFORE waiting for that phase's input, so weight streaming
-// overlaps the dependency latency.
+// per-phase arrival counters: a producer CTA stores its slice of the output
+// vector, then one thread releases it with a fenced atomic increment; a
+// consumer CTA has ONE thread poll the counter (with a short back-off) and
+// then reads the whole vector once.  (Polling the data itself with every
+// thread put ~150K loads per round on the same few L2 lines and delayed the
+// producers' stores; one poller per CTA keeps the hot line cool.)  Each CTA
+// issues the loads of its weight slice for a phase BEFORE waiting for that
+// phase's input, so weight streaming overlaps the dependency latency.
 //
 // Phases per layer (rows split evenly over the G CTAs):
 //   P1 LN1 + QKV GEMV (+ K/V append to the f16 cache)        -> q,k,v slots
@@ -35,15 +34,17 @@
 #define MK_SPIN (1u << 21)        // polls per wait before giving up (~1 s)
 #define MK_MAXI 3                 // weight items (32-element blocks) per thread per phase
 
-// slot buffer offsets (in u64 slots)
-#define MK_LL_QKV 0
-#define MK_LL_ATT (MK_LL_QKV + 3072)
-#define MK_LL_XM (MK_LL_ATT + 1024)
-#define MK_LL_H (MK_LL_XM + 1024)
-#define MK_LL_X (MK_LL_H + 4096)
-#define MK_LL_LOG (MK_LL_X + 1024)
-#define MK_LL_TOK (MK_LL_LOG + T3B_SAMPLER_VMAX)
-#define MK_LL_TOTAL (MK_LL_TOK + 32)
+// activation buffers (floats) and arrival counters (one 128-byte line each)
+#define MK_B_QKV 0
+#define MK_B_ATT (MK_B_QKV + 3072)
+#define MK_B_XM (MK_B_ATT + 1024)
+#define MK_B_H (MK_B_XM + 1024)
+#define MK_B_X (MK_B_H + 4096)
+#define MK_B_LOG (MK_B_X + 1024)
+#define MK_B_TOK (MK_B_LOG + T3B_SAMPLER_VMAX)
+#define MK_B_TOTAL (MK_B_TOK + 32)
+enum { MK_C_QKV, MK_C_ATT, MK_C_XM, MK_C_H, MK_C_X, MK_C_LOG, MK_C_TOK, MK_C_N };
+#define MK_C_STRIDE 32   // counters 128 bytes apart
 
 struct MkMat { const uint8_t * w; int type; int rb; };
 struct MkLayer {
@@ -58,7 +59,8 @@ struct MegaArgs {
     int V; float eps;
     __half * kv; size_t layer_stride; size_t v_off; int max_ctx;
     int p0, n_steps, ignore_stop, stop_token;
-    unsigned long long * ll;
+    float * buf;              // MK_B_TOTAL floats
+    unsigned * cnt;           // MK_C_N * MK_C_STRIDE counters, zero at launch
     unsigned * err; int * abort_flag; const int * cancel;
     int * steps_done;
     float * trace;                 // nullable: [n_steps + 1][V] logits, row 0 = prefill
@@ -68,7 +70,8 @@ struct MegaArgs {
 struct MegaState {
     int ready = 0;
     MkLayer * layers = nullptr;
-    unsigned long long * ll = nullptr;
+    float * buf = nullptr;
+    unsigned * cnt = nullptr;
     int * abort_flag = nullptr;
     int * steps_done = nullptr;
     int * cancel_host = nullptr;   // mapped pinned flag written by t3b_cancel
@@ -78,7 +81,8 @@ struct MegaState {
 };
 inline void mega_free(MegaState & m) {
     if (m.layers) cudaFree(m.layers);
-    if (m.ll) cudaFree(m.ll);
+    if (m.buf) cudaFree(m.buf);
+    if (m.cnt) cudaFree(m.cnt);
     if (m.abort_flag) cudaFree(m.abort_flag);
     if (m.steps_done) cudaFree(m.steps_done);
     if (m.cancel_host) cudaFreeHost(m.cancel_host);
@@ -86,55 +90,54 @@ inline void mega_free(MegaState & m) {
 }
 
 // ---------------------------------------------------------------------------
-// slots
+// phase hand-off: release = stores, CTA barrier, fence, counter increment;
+// acquire = one thread polls the counter, CTA barrier, L2-coherent reads
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void ll_put(unsigned long long * p, unsigned epoch, float v) {
-    const unsigned long long w = ((unsigned long long) epoch << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ unsigned long long ll_get(const unsigned long long * p) {
-    unsigned long long w;
-    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return w;
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
-// Wait until slots [0, n) carry `epoch`; copy their floats to dst (smem).
-// Each thread keeps up to E slots in flight, so the whole vector costs one
-// round trip once it is ready.  Returns false when the wait gave up.
-template <int E>
-__device__ bool ll_wait(const unsigned long long * buf, int n, unsigned epoch, float * dst, const MegaArgs & a) {
-    const int tid = threadIdx.x;
-    unsigned long long v[E];
-    bool ok = true;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const int i = tid + e * MK_THREADS;
-        v[e] = i < n ? ll_get(buf + i) : ((unsigned long long) epoch << 32);
+__device__ __forceinline__ void mk_release(unsigned * c) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
     }
-    unsigned spins = 0;
-    while (true) {
-        bool all = true;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-            if ((unsigned) (v[e] >> 32) != epoch) {
-                all = false;
-                v[e] = ll_get(buf + tid + e * MK_THREADS);
+}
+
+// Wait until *c >= target.  Returns false (every thread) when the wait gave
+// up or another CTA aborted.
+__device__ __forceinline__ bool mk_acquire(const unsigned * c, unsigned target, const MegaArgs & a) {
+    __shared__ int ok_s;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        unsigned spins = 0;
+        while (ld_acquire_u32(c) < target) {
+            __nanosleep(20);
+            if (++spins > MK_SPIN || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag)) {
+                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                ok = 0;
+                break;
             }
         }
-        if (all) break;
-        if (++spins > MK_SPIN || ((spins & 1023u) == 0 && *(volatile int *) a.abort_flag)) {
-            ok = false;
-            if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
-            break;
-        }
+        ok_s = ok;
     }
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const int i = tid + e * MK_THREADS;
-        if (i < n) dst[i] = __uint_as_float((unsigned) v[e]);
+    __syncthreads();
+    return ok_s != 0;
+}
+
+// wait, then copy n floats of src (L2-coherent loads) into dst (smem)
+__device__ __forceinline__ bool mk_wait_vec(const unsigned * c, unsigned target, const float * src, int n, float * dst,
+                                            const MegaArgs & a) {
+    if (!mk_acquire(c, target, a)) return false;
+    for (int i = threadIdx.x * 4; i < n; i += MK_THREADS * 4) {
+        const float4 v = __ldcg((const float4 *) (src + i));
+        *(float4 *) (dst + i) = v;
     }
-    __threadfence();   // acquire side: later reads of data published before the slots
-    return __syncthreads_and(ok) != 0;
+    __syncthreads();
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -302,23 +305,26 @@ __device__ __forceinline__ int mk_r0(int N, int c, int G) { return (int) (((long
 
 // LN_f + speech_head rows of this CTA; the head keeps its own weight type.
 template <int HT>
-__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, unsigned eh, float * vec, const MkAct & act, float * part,
-                        float * rowsum, double * redd, const unsigned long long * LLx, unsigned long long * LLl) {
-    const int D = 1024, tid = threadIdx.x;
-    const int r0 = mk_r0(a.V, blockIdx.x, gridDim.x), r1 = mk_r0(a.V, blockIdx.x + 1, gridDim.x);
+__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, const MkAct & act, float * part,
+                                     float * rowsum, double * redd) {
+    const int D = 1024, tid = threadIdx.x, G = gridDim.x;
+    const int r0 = mk_r0(a.V, blockIdx.x, G), r1 = mk_r0(a.V, blockIdx.x + 1, G);
     MkPref<HT> pf;
     mk_prefetch<HT>(a.head, D, r0, r1, pf);
-    if (!ll_wait<2>(LLx, D, eh - 1u, vec, a)) return false;
+    const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
+    if (!mk_wait_vec(a.cnt + MK_C_X * MK_C_STRIDE, kx * G, a.buf + MK_B_X, D, vec, a)) return false;
     mk_layernorm(vec, D, a.lnfg, a.lnfb, a.eps, redd);
     mk_quantize(act, D, HT == T3B_F16);
     mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
     float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
+    float * lg = a.buf + MK_B_LOG;
     for (int r = tid; r < r1 - r0; r += MK_THREADS) {
         const int n = r0 + r;
         const float v = __fadd_rn(rowsum[r], a.headb[n]);
         if (tr) tr[n] = v;
-        ll_put(LLl + n, eh, v);
+        lg[n] = v;
     }
+    mk_release(a.cnt + MK_C_LOG * MK_C_STRIDE);
     return true;
 }
 
@@ -328,17 +334,22 @@ constexpr size_t mk_smem_bytes() {
 }
 static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
 
+// rows of one GEMV phase: prefetch (before the caller's wait)
+#define MK_GEMV_BEGIN(W, K, N)                                                                      \
+    const int r0_ = mk_r0((N), blockIdx.x, gridDim.x), r1_ = mk_r0((N), blockIdx.x + 1, gridDim.x); \
+    MkPref<T> pf_;                                                                                 \
+    mk_prefetch<T>((W), (K), r0_, r1_, pf_);
+
 template <int T>
 __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
-    // persistent region at the top of shared memory: residual stream copies
     const int D = 1024;
-    __shared__ float xres[1024];          // layer input x (residual for P3)
-    __shared__ float xmid[1024];          // x after attention (residual for P5)
+    __shared__ __align__(16) float xres[1024];   // layer input x (residual for P3)
+    __shared__ __align__(16) float xmid[1024];   // x after attention (residual for P5)
     __shared__ double redd[32];
     __shared__ float rowsum[128];
     __shared__ int tokv;
-    // scratch (reused by every phase): vec[4096] f32 | q[4096] i8 | d,s [128] | h[4096] f16 | part[512]
+    // scratch (reused by every phase): vec[4096] f32 | q[4096] i8 | d,s [128] | h[4096] f16 | part
     float * vec = (float *) smem;
     MkAct act;
     act.v = vec;
@@ -347,35 +358,36 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     act.s = (int *) (smem + 16384 + 4096 + 512);
     act.h = (__half *) (smem + 16384 + 4096 + 1024);
     float * part = (float *) (smem + 16384 + 4096 + 1024 + 8192);
-    // attention stage and sampler reuse the same bytes
+    // attention stage (and, in CTA 0, the sampler) reuse the same bytes
     __half * kst = (__half *) smem;
     __half * vst = kst + MK_MAX_POS * T3B_HD;
     float * att_s = (float *) (smem + 2 * MK_MAX_POS * T3B_HD * 2);   // qkv[192] | p[MK_MAX_POS] | o[8][64]
 
-    const int tid = threadIdx.x, cta = blockIdx.x;
+    const int tid = threadIdx.x, cta = blockIdx.x, G = gridDim.x;
     const int NL = a.n_layer;
-    const unsigned EPS = 5u * NL + 2u;    // epochs per step
-    unsigned long long * LLq = a.ll + MK_LL_QKV, * LLa = a.ll + MK_LL_ATT, * LLm = a.ll + MK_LL_XM;
-    unsigned long long * LLh = a.ll + MK_LL_H, * LLx = a.ll + MK_LL_X, * LLl = a.ll + MK_LL_LOG, * LLt = a.ll + MK_LL_TOK;
     const int Hn = 16;
+    unsigned * cQKV = a.cnt + MK_C_QKV * MK_C_STRIDE, * cATT = a.cnt + MK_C_ATT * MK_C_STRIDE;
+    unsigned * cXM = a.cnt + MK_C_XM * MK_C_STRIDE, * cH = a.cnt + MK_C_H * MK_C_STRIDE;
+    unsigned * cX = a.cnt + MK_C_X * MK_C_STRIDE, * cLOG = a.cnt + MK_C_LOG * MK_C_STRIDE;
+    unsigned * cTOK = a.cnt + MK_C_TOK * MK_C_STRIDE;
+    float * bQKV = a.buf + MK_B_QKV, * bATT = a.buf + MK_B_ATT, * bXM = a.buf + MK_B_XM;
+    float * bH = a.buf + MK_B_H, * bX = a.buf + MK_B_X, * bLOG = a.buf + MK_B_LOG;
+    int * bTOK = (int *) (a.buf + MK_B_TOK);
 
     int tok = a.samp.step_tok[a.samp.slot_of ? a.samp.slot_of[0] : 0];
     for (int step = 0; step < a.n_steps; ++step) {
         const int pos = a.p0 + step;
-        const unsigned e0 = 1u + (unsigned) step * EPS;
         // embedding: x = speech_emb[tok] + wpe[pos]
         for (int i = tid; i < D; i += MK_THREADS)
             xres[i] = __fadd_rn(__half2float(a.semb[(size_t) tok * D + i]), a.wpe[(size_t) pos * D + i]);
         __syncthreads();
         for (int l = 0; l < NL; ++l) {
             const MkLayer & Ly = a.layers[l];
-            const unsigned eb = e0 + 5u * l;
+            const unsigned k = (unsigned) (step * NL + l) + 1u;   // occurrence of this layer's phases
             // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
             {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
-                if (l > 0) {   // layer input = previous layer's P5 output
-                    if (!ll_wait<2>(LLx, D, eb - 1u, xres, a)) return;
-                }
+                if (l > 0 && !mk_wait_vec(cX, (k - 1u) * G, bX, D, xres, a)) return;
                 for (int i = tid; i < D; i += MK_THREADS) vec[i] = xres[i];
                 __syncthreads();
                 mk_layernorm(vec, D, Ly.ln1g, Ly.ln1b, a.eps, redd);
@@ -390,9 +402,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         __half * base = kb + (which ? a.v_off : 0);
                         base[((size_t) (rem >> 6) * a.max_ctx + pos) * T3B_HD + (rem & 63)] = __float2half_rn(v);
                     }
-                    __threadfence();
-                    ll_put(LLq + n, eb, v);
+                    bQKV[n] = v;
                 }
+                mk_release(cQKV);
             }
             // ---------------- P2: attention (CTA h < 16 owns head h) ----------
             if (cta < Hn) {
@@ -408,30 +420,12 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sv), "l"(vb + i * 8) : "memory");
                 }
                 asm volatile("cp.async.commit_group;" ::: "memory");
-                // q, k, v of head h for this position
                 float * qkvh = att_s;   // [192]
-                {
-                    unsigned long long w[1];
-                    const int i = tid;
-                    bool ok = true;
-                    if (i < 192) {
-                        const int n = (i / 64) * D + h * 64 + (i & 63);
-                        unsigned spins = 0;
-                        w[0] = ll_get(LLq + n);
-                        while ((unsigned) (w[0] >> 32) != eb) {
-                            w[0] = ll_get(LLq + n);
-                            if (++spins > MK_SPIN || ((spins & 1023u) == 0 && *(volatile int *) a.abort_flag)) {
-                                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
-                                ok = false;
-                                break;
-                            }
-                        }
-                        qkvh[i] = __uint_as_float((unsigned) w[0]);
-                    }
-                    asm volatile("cp.async.wait_all;" ::: "memory");
-                    __threadfence();
-                    if (!__syncthreads_and(ok)) return;
-                }
+                const bool ok = mk_acquire(cQKV, k * G, a);
+                if (tid < 192) qkvh[tid] = __ldcg(bQKV + (tid / 64) * D + h * 64 + (tid & 63));
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                __syncthreads();
+                if (!ok) return;
                 if (tid < T3B_HD) {
                     kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
                     vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
@@ -485,25 +479,27 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     if (tid < 64) {
                         float t = 0.0f;
                         for (int gg = 0; gg < 8; ++gg) t += og[gg * 64 + tid];
-                        ll_put(LLa + h * 64 + tid, eb + 1u, t / lsum);
+                        bATT[h * 64 + tid] = t / lsum;
                     }
                 }
+                mk_release(cATT);
             }
             // ---------------- P3: proj + bias + residual -----------------------
             {
                 MK_GEMV_BEGIN(Ly.o, D, D)
-                if (!ll_wait<2>(LLa, D, eb + 1u, vec, a)) return;
+                if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) return;
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
                 for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
                     const int n = r0_ + r;
-                    ll_put(LLm + n, eb + 2u, __fadd_rn(__fadd_rn(rowsum[r], Ly.bo[n]), xres[n]));
+                    bXM[n] = __fadd_rn(__fadd_rn(rowsum[r], Ly.bo[n]), xres[n]);
                 }
+                mk_release(cXM);
             }
             // ---------------- P4: LN2 + fc + GELU ------------------------------
             {
                 MK_GEMV_BEGIN(Ly.fc, D, 4 * D)
-                if (!ll_wait<2>(LLm, D, eb + 2u, xmid, a)) return;
+                if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
                 for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
                 __syncthreads();
                 mk_layernorm(vec, D, Ly.ln2g, Ly.ln2b, a.eps, redd);
@@ -511,28 +507,29 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
                 for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
                     const int n = r0_ + r;
-                    ll_put(LLh + n, eb + 3u, gelu_ggml(__fadd_rn(rowsum[r], Ly.bfc[n])));
+                    bH[n] = gelu_ggml(__fadd_rn(rowsum[r], Ly.bfc[n]));
                 }
+                mk_release(cH);
             }
             // ---------------- P5: fc2 + bias + residual ------------------------
             {
                 MK_GEMV_BEGIN(Ly.fc2, 4 * D, D)
-                if (!ll_wait<8>(LLh, 4 * D, eb + 3u, vec, a)) return;
+                if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
                 mk_quantize(act, 4 * D, T == T3B_F16);
                 mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
                 for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
                     const int n = r0_ + r;
-                    ll_put(LLx + n, eb + 4u, __fadd_rn(__fadd_rn(rowsum[r], Ly.bfc2[n]), xmid[n]));
+                    bX[n] = __fadd_rn(__fadd_rn(rowsum[r], Ly.bfc2[n]), xmid[n]);
                 }
+                mk_release(cX);
             }
         }
         // ---------------- head: LN_f + speech_head ------------------------------
-        const unsigned eh = e0 + 5u * NL;
         {
             bool ok;
-            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, eh, vec, act, part, rowsum, redd, LLx, LLl);
-            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, eh, vec, act, part, rowsum, redd, LLx, LLl);
-            else ok = mk_head<T3B_Q4_0>(a, step, eh, vec, act, part, rowsum, redd, LLx, LLl);
+            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, vec, act, part, rowsum, redd);
+            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, vec, act, part, rowsum, redd);
+            else ok = mk_head<T3B_Q4_0>(a, step, vec, act, part, rowsum, redd);
             if (!ok) return;
         }
         // ---------------- sampler (CTA 0) and token broadcast -------------------
@@ -541,31 +538,22 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // PCIe round trip overlaps it
             const int cancelled = a.cancel ? *(volatile const int *) a.cancel : 0;
             float * lg = (float *) (smem + T3B_SAMPLER_SMEM);   // logits staged after the sampler's arrays
-            if (!ll_wait<(T3B_SAMPLER_VMAX + MK_THREADS - 1) / MK_THREADS>(LLl, a.V, eh, lg, a)) return;
+            if (!mk_acquire(cLOG, (unsigned) (step + 1) * G, a)) return;
+            for (int i = tid; i < a.V; i += MK_THREADS) lg[i] = __ldcg(bLOG + i);
+            __syncthreads();
             SampArgs sa = a.samp;
             sa.cond = lg; sa.cond_stride = 0; sa.uncond = nullptr;
-            int t = sample_row_block(sa, 0, smem);
+            const int t = sample_row_block(sa, 0, smem);
             if (tid == 0) {
                 const int stop = (t == a.stop_token && !a.ignore_stop) || cancelled || t < 0;
-                __threadfence();
-                ll_put(LLt, eh + 1u, __int_as_float((t & 0xffff) | (stop ? 0x10000 : 0)));
+                *bTOK = (t & 0xffff) | (stop ? 0x10000 : 0);
                 *a.steps_done = step + 1;
             }
+            mk_release(cTOK);
         }
         {
-            if (tid == 0) {
-                unsigned long long w = ll_get(LLt);
-                unsigned spins = 0;
-                while ((unsigned) (w >> 32) != eh + 1u) {
-                    w = ll_get(LLt);
-                    if (++spins > MK_SPIN || ((spins & 1023u) == 0 && *(volatile int *) a.abort_flag)) {
-                        if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
-                        w = ((unsigned long long) (eh + 1u) << 32) | 0x10000u;
-                        break;
-                    }
-                }
-                tokv = __float_as_int(__uint_as_float((unsigned) w));
-            }
+            if (!mk_acquire(cTOK, (unsigned) (step + 1), a)) return;
+            if (tid == 0) tokv = __ldcg(bTOK);
             __syncthreads();
             const int tv = tokv;
             if (tv & 0x10000) return;

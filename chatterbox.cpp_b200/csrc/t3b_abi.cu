@@ -752,7 +752,8 @@ int mega_prepare(t3b_ctx * ctx) {
     }
     CK(cudaMalloc(&m.layers, sizeof(MkLayer) * hl.size()));
     CK(cudaMemcpy(m.layers, hl.data(), sizeof(MkLayer) * hl.size(), cudaMemcpyHostToDevice));
-    CK(cudaMalloc(&m.ll, sizeof(unsigned long long) * MK_LL_TOTAL));
+    CK(cudaMalloc(&m.buf, sizeof(float) * MK_B_TOTAL));
+    CK(cudaMalloc(&m.cnt, sizeof(unsigned) * MK_C_N * MK_C_STRIDE));
     CK(cudaMalloc(&m.abort_flag, sizeof(int)));
     CK(cudaMalloc(&m.steps_done, sizeof(int)));
     CK(cudaHostAlloc(&m.cancel_host, sizeof(int), cudaHostAllocMapped));
@@ -789,12 +790,12 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     a.v_off = (size_t) H * ctx->max_ctx * T3B_HD;
     a.max_ctx = ctx->max_ctx;
     a.p0 = p0; a.n_steps = max_steps; a.ignore_stop = ignore_stop; a.stop_token = ctx->hp.stop_speech_token;
-    a.ll = m.ll; a.err = ctx->err_word; a.abort_flag = m.abort_flag; a.cancel = m.cancel_dev;
+    a.buf = m.buf; a.cnt = m.cnt; a.err = ctx->err_word; a.abort_flag = m.abort_flag; a.cancel = m.cancel_dev;
     a.steps_done = m.steps_done;
     a.trace = ctx->trace_cap >= max_steps ? ctx->trace : nullptr;
     a.samp = sampler_args(ctx, false);
     a.samp.done = nullptr;
-    CK(cudaMemsetAsync(m.ll, 0, sizeof(unsigned long long) * MK_LL_TOTAL, st));
+    CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_C_N * MK_C_STRIDE, st));
     CK(cudaMemsetAsync(m.abort_flag, 0, sizeof(int), st));
     CK(cudaMemsetAsync(m.steps_done, 0, sizeof(int), st));
     void * args[] = {&a};
