@@ -200,7 +200,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["sampler", "gemv"], default=None,
+                    help="run one kernel micro-benchmark alone (for ncu captures)")
     args = ap.parse_args()
+    if args.only:
+        import torch
+        import __graft_entry__ as ge
+        pkg = ge.load_package()
+        peak, _ = peaks()
+        r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
+        print(json.dumps(r), flush=True)
+        return 0
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)

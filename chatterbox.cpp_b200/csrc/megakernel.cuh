@@ -64,8 +64,11 @@ struct MegaArgs {
     unsigned * err; int * abort_flag; const int * cancel;
     int * steps_done;
     float * trace;                 // nullable: [n_steps + 1][V] logits, row 0 = prefill
+    unsigned long long * tl;       // nullable: [G][MK_TL] globaltimer stamps of step tl_step
+    int tl_step;
     SampArgs samp;
 };
+#define MK_TL 256
 
 struct MegaState {
     int ready = 0;
@@ -101,10 +104,7 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned * p) {
 
 __device__ __forceinline__ void mk_release(unsigned * c) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
-    }
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
 }
 
 // Wait until *c >= target.  Returns false (every thread) when the wait gave
@@ -128,16 +128,36 @@ __device__ __forceinline__ bool mk_acquire(const unsigned * c, unsigned target, 
     return ok_s != 0;
 }
 
-// wait, then copy n floats of src (L2-coherent loads) into dst (smem)
+// wait, then copy n (<= 4096, multiple of 4) floats of src into dst (smem);
+// every load is issued before the first store so the copy is one round trip
 __device__ __forceinline__ bool mk_wait_vec(const unsigned * c, unsigned target, const float * src, int n, float * dst,
                                             const MegaArgs & a) {
     if (!mk_acquire(c, target, a)) return false;
-    for (int i = threadIdx.x * 4; i < n; i += MK_THREADS * 4) {
-        const float4 v = __ldcg((const float4 *) (src + i));
-        *(float4 *) (dst + i) = v;
+    float4 v[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int i = (threadIdx.x + u * MK_THREADS) * 4;
+        if (i < n) v[u] = __ldcg((const float4 *) (src + i));
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int i = (threadIdx.x + u * MK_THREADS) * 4;
+        if (i < n) *(float4 *) (dst + i) = v[u];
     }
     __syncthreads();
     return true;
+}
+
+// LayerNorm parameters of this thread's two elements, loaded before a wait
+struct MkLn { float g[2], b[2]; };
+__device__ __forceinline__ MkLn mk_ln_prefetch(const float * g, const float * b) {
+    MkLn p;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        p.g[u] = __ldg(g + threadIdx.x + u * MK_THREADS);
+        p.b[u] = __ldg(b + threadIdx.x + u * MK_THREADS);
+    }
+    return p;
 }
 
 // ---------------------------------------------------------------------------
@@ -151,25 +171,18 @@ struct MkAct {
     __half * h;     // f16 copy [K] (F16 weights)
 };
 
-__device__ void mk_layernorm(float * v, int K, const float * g, const float * b, float eps, double * redd) {
-    const int tid = threadIdx.x;
-    double s = 0.0;
-    for (int i = tid; i < K; i += MK_THREADS) s += (double) v[i];
-    s = block_sum_d(s, redd);
+// LayerNorm of the 1024-vector v in place (two elements per thread).
+__device__ void mk_layernorm(float * v, const MkLn & p, float eps, double * redd) {
+    const int tid = threadIdx.x, K = 2 * MK_THREADS;
+    const float x0 = v[tid], x1 = v[tid + MK_THREADS];
+    double s = block_sum_d((double) x0 + (double) x1, redd);
     const float mean = (float) (s / K);
-    double s2 = 0.0;
-    for (int i = tid; i < K; i += MK_THREADS) {
-        const float t = __fsub_rn(v[i], mean);
-        s2 += (double) __fmul_rn(t, t);
-    }
-    s2 = block_sum_d(s2, redd);
+    const float t0 = __fsub_rn(x0, mean), t1 = __fsub_rn(x1, mean);
+    double s2 = block_sum_d((double) __fmul_rn(t0, t0) + (double) __fmul_rn(t1, t1), redd);
     const float var = (float) (s2 / K);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-    __syncthreads();
-    for (int i = tid; i < K; i += MK_THREADS) {
-        const float t = __fsub_rn(v[i], mean);
-        v[i] = __fadd_rn(__fmul_rn(__fmul_rn(t, scale), g[i]), b[i]);
-    }
+    v[tid] = __fadd_rn(__fmul_rn(__fmul_rn(t0, scale), p.g[0]), p.b[0]);
+    v[tid + MK_THREADS] = __fadd_rn(__fmul_rn(__fmul_rn(t1, scale), p.g[1]), p.b[1]);
     __syncthreads();
 }
 
@@ -203,6 +216,19 @@ struct MkPref {
     float d[MK_MAXI];
 };
 
+__device__ __forceinline__ uint4 ldg_v4(const void * p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ldg_h(const void * p) {
+    unsigned short h;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(h) : "l"(p));
+    return __half2float(__ushort_as_half(h));
+}
+
+// volatile loads: issued here, before the caller's wait, and not sunk past it
 template <int T>
 __device__ __forceinline__ void mk_prefetch(const MkMat & W, int K, int r0, int r1, MkPref<T> & pf) {
     const int NB = K / 32;
@@ -214,15 +240,15 @@ __device__ __forceinline__ void mk_prefetch(const MkMat & W, int K, int r0, int 
             const int row = r0 + i / NB, b = i % NB;
             const uint8_t * wr = W.w + (size_t) row * W.rb;
             if (T == T3B_Q4_0) {
-                pf.q[j][0] = __ldg((const uint4 *) (wr + b * 16));
-                pf.d[j] = __half2float(__ldg((const __half *) (wr + K / 2 + b * 2)));
+                pf.q[j][0] = ldg_v4(wr + b * 16);
+                pf.d[j] = ldg_h(wr + K / 2 + b * 2);
             } else if (T == T3B_Q8_0) {
-                pf.q[j][0] = __ldg((const uint4 *) (wr + b * 32));
-                pf.q[j][1 % MkW<T>::QW] = __ldg((const uint4 *) (wr + b * 32 + 16));
-                pf.d[j] = __half2float(__ldg((const __half *) (wr + K + b * 2)));
+                pf.q[j][0] = ldg_v4(wr + b * 32);
+                pf.q[j][1 % MkW<T>::QW] = ldg_v4(wr + b * 32 + 16);
+                pf.d[j] = ldg_h(wr + K + b * 2);
             } else {
 #pragma unroll
-                for (int c = 0; c < MkW<T>::QW; ++c) pf.q[j][c] = __ldg((const uint4 *) (wr + b * 64 + c * 16));
+                for (int c = 0; c < MkW<T>::QW; ++c) pf.q[j][c] = ldg_v4(wr + b * 64 + c * 16);
                 pf.d[j] = 1.0f;
             }
         }
@@ -311,16 +337,18 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
     const int r0 = mk_r0(a.V, blockIdx.x, G), r1 = mk_r0(a.V, blockIdx.x + 1, G);
     MkPref<HT> pf;
     mk_prefetch<HT>(a.head, D, r0, r1, pf);
+    const MkLn lp = mk_ln_prefetch(a.lnfg, a.lnfb);
+    const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
     if (!mk_wait_vec(a.cnt + MK_C_X * MK_C_STRIDE, kx * G, a.buf + MK_B_X, D, vec, a)) return false;
-    mk_layernorm(vec, D, a.lnfg, a.lnfb, a.eps, redd);
+    mk_layernorm(vec, lp, a.eps, redd);
     mk_quantize(act, D, HT == T3B_F16);
     mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
     float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
     float * lg = a.buf + MK_B_LOG;
-    for (int r = tid; r < r1 - r0; r += MK_THREADS) {
-        const int n = r0 + r;
-        const float v = __fadd_rn(rowsum[r], a.headb[n]);
+    if (tid < r1 - r0) {
+        const int n = r0 + tid;
+        const float v = __fadd_rn(rowsum[tid], hb);
         if (tr) tr[n] = v;
         lg[n] = v;
     }
@@ -339,6 +367,14 @@ static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampl
     const int r0_ = mk_r0((N), blockIdx.x, gridDim.x), r1_ = mk_r0((N), blockIdx.x + 1, gridDim.x); \
     MkPref<T> pf_;                                                                                 \
     mk_prefetch<T>((W), (K), r0_, r1_, pf_);
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// phase timeline (debug): stamp point `i` of the traced step
+#define MK_STAMP(i) do { if (a.tl && step == a.tl_step && tid == 0) a.tl[(size_t) cta * MK_TL + (i)] = globaltimer_ns(); } while (0)
 
 template <int T>
 __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a) {
@@ -387,16 +423,20 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
             {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
+                const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
+                const float bias = tid < r1_ - r0_ ? __ldg(Ly.bqkv + r0_ + tid) : 0.0f;
+                MK_STAMP(l * 10 + 0);
                 if (l > 0 && !mk_wait_vec(cX, (k - 1u) * G, bX, D, xres, a)) return;
+                MK_STAMP(l * 10 + 1);
                 for (int i = tid; i < D; i += MK_THREADS) vec[i] = xres[i];
                 __syncthreads();
-                mk_layernorm(vec, D, Ly.ln1g, Ly.ln1b, a.eps, redd);
+                mk_layernorm(vec, lp, a.eps, redd);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
                 __half * kb = a.kv + (size_t) l * a.layer_stride;
-                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
-                    const int n = r0_ + r;
-                    const float v = __fadd_rn(rowsum[r], Ly.bqkv[n]);
+                if (tid < r1_ - r0_) {
+                    const int n = r0_ + tid;
+                    const float v = __fadd_rn(rowsum[tid], bias);
                     if (n >= D) {
                         const int which = n >= 2 * D, rem = n - D - which * D;
                         __half * base = kb + (which ? a.v_off : 0);
@@ -405,6 +445,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     bQKV[n] = v;
                 }
                 mk_release(cQKV);
+                MK_STAMP(l * 10 + 2);
             }
             // ---------------- P2: attention (CTA h < 16 owns head h) ----------
             if (cta < Hn) {
@@ -426,6 +467,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 asm volatile("cp.async.wait_all;" ::: "memory");
                 __syncthreads();
                 if (!ok) return;
+                MK_STAMP(l * 10 + 3);
                 if (tid < T3B_HD) {
                     kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
                     vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
@@ -483,48 +525,55 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     }
                 }
                 mk_release(cATT);
+                MK_STAMP(l * 10 + 4);
             }
             // ---------------- P3: proj + bias + residual -----------------------
             {
                 MK_GEMV_BEGIN(Ly.o, D, D)
+                const float bias = tid < r1_ - r0_ ? __ldg(Ly.bo + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) return;
+                MK_STAMP(l * 10 + 5);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
-                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
-                    const int n = r0_ + r;
-                    bXM[n] = __fadd_rn(__fadd_rn(rowsum[r], Ly.bo[n]), xres[n]);
+                if (tid < r1_ - r0_) {
+                    const int n = r0_ + tid;
+                    bXM[n] = __fadd_rn(__fadd_rn(rowsum[tid], bias), xres[n]);
                 }
                 mk_release(cXM);
             }
             // ---------------- P4: LN2 + fc + GELU ------------------------------
             {
                 MK_GEMV_BEGIN(Ly.fc, D, 4 * D)
+                const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
+                const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
+                MK_STAMP(l * 10 + 6);
                 for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
                 __syncthreads();
-                mk_layernorm(vec, D, Ly.ln2g, Ly.ln2b, a.eps, redd);
+                mk_layernorm(vec, lp, a.eps, redd);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
-                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
-                    const int n = r0_ + r;
-                    bH[n] = gelu_ggml(__fadd_rn(rowsum[r], Ly.bfc[n]));
-                }
+                if (tid < r1_ - r0_) bH[r0_ + tid] = gelu_ggml(__fadd_rn(rowsum[tid], bias));
                 mk_release(cH);
             }
             // ---------------- P5: fc2 + bias + residual ------------------------
             {
                 MK_GEMV_BEGIN(Ly.fc2, 4 * D, D)
+                const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
+                MK_STAMP(l * 10 + 7);
                 mk_quantize(act, 4 * D, T == T3B_F16);
                 mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
-                for (int r = tid; r < r1_ - r0_; r += MK_THREADS) {
-                    const int n = r0_ + r;
-                    bX[n] = __fadd_rn(__fadd_rn(rowsum[r], Ly.bfc2[n]), xmid[n]);
+                if (tid < r1_ - r0_) {
+                    const int n = r0_ + tid;
+                    bX[n] = __fadd_rn(__fadd_rn(rowsum[tid], bias), xmid[n]);
                 }
                 mk_release(cX);
+                MK_STAMP(l * 10 + 8);
             }
         }
         // ---------------- head: LN_f + speech_head ------------------------------
+        MK_STAMP(240);
         {
             bool ok;
             if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, vec, act, part, rowsum, redd);
@@ -532,6 +581,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             else ok = mk_head<T3B_Q4_0>(a, step, vec, act, part, rowsum, redd);
             if (!ok) return;
         }
+        MK_STAMP(241);
         // ---------------- sampler (CTA 0) and token broadcast -------------------
         if (cta == 0) {
             // host cancel flag (mapped memory): read before the wait so the
@@ -539,11 +589,20 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             const int cancelled = a.cancel ? *(volatile const int *) a.cancel : 0;
             float * lg = (float *) (smem + T3B_SAMPLER_SMEM);   // logits staged after the sampler's arrays
             if (!mk_acquire(cLOG, (unsigned) (step + 1) * G, a)) return;
-            for (int i = tid; i < a.V; i += MK_THREADS) lg[i] = __ldcg(bLOG + i);
+            {
+                constexpr int E = (T3B_SAMPLER_VMAX + MK_THREADS - 1) / MK_THREADS;
+                float v[E];
+#pragma unroll
+                for (int u = 0; u < E; ++u) { const int i = tid + u * MK_THREADS; v[u] = i < a.V ? __ldcg(bLOG + i) : 0.0f; }
+#pragma unroll
+                for (int u = 0; u < E; ++u) { const int i = tid + u * MK_THREADS; if (i < a.V) lg[i] = v[u]; }
+            }
             __syncthreads();
             SampArgs sa = a.samp;
             sa.cond = lg; sa.cond_stride = 0; sa.uncond = nullptr;
+            MK_STAMP(242);
             const int t = sample_row_block(sa, 0, smem);
+            MK_STAMP(243);
             if (tid == 0) {
                 const int stop = (t == a.stop_token && !a.ignore_stop) || cancelled || t < 0;
                 *bTOK = (t & 0xffff) | (stop ? 0x10000 : 0);
@@ -553,6 +612,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         }
         {
             if (!mk_acquire(cTOK, (unsigned) (step + 1), a)) return;
+            MK_STAMP(244);
             if (tid == 0) tokv = __ldcg(bTOK);
             __syncthreads();
             const int tv = tokv;

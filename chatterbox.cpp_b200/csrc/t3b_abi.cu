@@ -798,6 +798,16 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_C_N * MK_C_STRIDE, st));
     CK(cudaMemsetAsync(m.abort_flag, 0, sizeof(int), st));
     CK(cudaMemsetAsync(m.steps_done, 0, sizeof(int), st));
+    // debug: T3B_MK_TIMELINE=<file> stamps every phase boundary of step
+    // T3B_MK_TIMELINE_STEP (default 2) per CTA and writes [G][256] u64 ns
+    const char * tl_file = getenv("T3B_MK_TIMELINE");
+    unsigned long long * tl = nullptr;
+    if (tl_file) {
+        CK(cudaMalloc(&tl, sizeof(unsigned long long) * m.grid * MK_TL));
+        CK(cudaMemsetAsync(tl, 0, sizeof(unsigned long long) * m.grid * MK_TL, st));
+        a.tl = tl;
+        a.tl_step = getenv("T3B_MK_TIMELINE_STEP") ? atoi(getenv("T3B_MK_TIMELINE_STEP")) : 2;
+    }
     void * args[] = {&a};
     const int T = ctx->L[0].attn.type;
     const void * fn = T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0>
@@ -805,6 +815,13 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
                                     : (const void *) t3_decode_megakernel<T3B_F16>;
     CK(cudaLaunchCooperativeKernel(fn, dim3(m.grid), dim3(MK_THREADS), args, m.smem, st));
     CK(cudaMemcpyAsync(steps, m.steps_done, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (tl) {
+        std::vector<unsigned long long> h((size_t) m.grid * MK_TL);
+        CK(cudaMemcpyAsync(h.data(), tl, sizeof(unsigned long long) * h.size(), cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        if (FILE * f = fopen(tl_file, "wb")) { fwrite(h.data(), 8, h.size(), f); fclose(f); }
+        cudaFree(tl);
+    }
     return T3B_OK;
 }
 
