@@ -552,6 +552,7 @@ struct SampArgs {
     int * step_tok;                                   // nullable: [slot] next-step token
     int * done; int stop_token;                       // nullable
     ExpFix fx;
+    unsigned long long * tl;                          // nullable: stage stamps of row 0 (debug)
 };
 
 #define T3B_SAMPLER_THREADS 1024
@@ -578,6 +579,9 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const int tid = threadIdx.x, nth = blockDim.x;
     const int slot = a.slot_of ? a.slot_of[r] : r;
     if (a.done && a.done[slot]) return -1;
+    unsigned long long * tls = (a.tl && r == 0) ? a.tl : nullptr;
+#define SAMP_STAMP(i) do { if (tls && tid == 0) { unsigned long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); tls[i] = t_; } } while (0)
+    SAMP_STAMP(0);
     const t3b_sample_params P = a.params[a.params_per_row ? r : 0];
     const int V = a.V;
     const float * cond = a.cond + (long long) slot * a.cond_stride;
@@ -595,6 +599,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     }
     __syncthreads();
 
+    SAMP_STAMP(1);
     // (1b) min-p: drop exp(s - max) < min_p
     if (P.min_p > 0.0f) {
         float lm = -INFINITY;
@@ -605,6 +610,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         __syncthreads();
     }
 
+    SAMP_STAMP(2);
     // (2) top-k (main.cpp:740-748): radix-select the value at descending
     // rank k, then keep s > thr (thr nudged by 1e-10f if fewer than k).
     if (P.top_k > 0 && P.top_k < V) {
@@ -661,6 +667,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         __syncthreads();
     }
 
+    SAMP_STAMP(3);
     // (3) top-p (main.cpp:750-772): survivors sorted by score descending
     // (ties by ascending index), sequential float sums in that order.
     if (P.top_p < 1.0f) {
@@ -678,6 +685,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             while (n2 < c) n2 <<= 1;
             for (int i = c + tid; i < n2; i += nth) keys[i] = ~0ull;
             __syncthreads();
+            SAMP_STAMP(4);
             for (int k = 2; k <= n2; k <<= 1)
                 for (int j = k >> 1; j > 0; j >>= 1) {
                     for (int i = tid; i < n2; i += nth) {
@@ -690,6 +698,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                     }
                     __syncthreads();
                 }
+            SAMP_STAMP(5);
             const float mx = s[(int) (keys[0] & 0xffffffffu)];
             for (int j = tid; j < c; j += nth) e[j] = t3_expf_dev(__fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx), a.fx);
             __syncthreads();
@@ -708,6 +717,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         }
     }
 
+    SAMP_STAMP(6);
     // (4) repetition penalty over distinct history ids (main.cpp:774-781)
     const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
     const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
@@ -727,6 +737,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         __syncthreads();
     }
 
+    SAMP_STAMP(7);
     // (5) softmax over survivors in index order (main.cpp:783-793)
     float lm = -INFINITY;
     for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
@@ -766,6 +777,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     }
     __syncthreads();
     const int cf = shi[4];
+    SAMP_STAMP(8);
     if (tid == 0) shf[1] = seq_sum_f32(e, cf);
     __syncthreads();
     const float psum = shf[1];
@@ -785,6 +797,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             tok = shi[5];
         } else {
             // (7) discrete_distribution draw
+            SAMP_STAMP(9);
             const int mode = a.rng_mode ? a.rng_mode[slot] : T3B_RNG_PHILOX;
             uint32_t x1, x2;
             if (mode == T3B_RNG_MT19937) {
@@ -808,6 +821,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 __syncthreads();
                 if (tid == 0) a.ph_ctr[slot] = ct + 1ull;
             }
+            SAMP_STAMP(10);
             if (tid == 0) {
                 double sum = (double) x1;
                 sum += (double) x2 * 4294967296.0;
@@ -846,6 +860,8 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             tok = shi[6];
         }
     }
+    SAMP_STAMP(11);
+#undef SAMP_STAMP
     if (tid == 0) {
         if (a.tok_out) a.tok_out[r] = tok;
         if (a.step_tok) a.step_tok[slot] = tok;

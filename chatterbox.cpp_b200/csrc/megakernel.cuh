@@ -68,7 +68,7 @@ struct MegaArgs {
     int tl_step;
     SampArgs samp;
 };
-#define MK_TL 256
+#define MK_TL 512
 
 struct MegaState {
     int ready = 0;
@@ -171,14 +171,29 @@ struct MkAct {
     __half * h;     // f16 copy [K] (F16 weights)
 };
 
+// Sum over the CTA in double with a single barrier: warp trees, then every
+// warp reduces the 16 warp partials itself (same order in every warp).
+__device__ __forceinline__ double mk_block_sum_d(double v, double * red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    double r = red[lane & (MK_THREADS / 32 - 1)];
+#pragma unroll
+    for (int o = MK_THREADS / 64; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    __syncthreads();   // red is reused by the next reduction
+    return r;
+}
+
 // LayerNorm of the 1024-vector v in place (two elements per thread).
 __device__ void mk_layernorm(float * v, const MkLn & p, float eps, double * redd) {
     const int tid = threadIdx.x, K = 2 * MK_THREADS;
     const float x0 = v[tid], x1 = v[tid + MK_THREADS];
-    double s = block_sum_d((double) x0 + (double) x1, redd);
+    const double s = mk_block_sum_d((double) x0 + (double) x1, redd);
     const float mean = (float) (s / K);
     const float t0 = __fsub_rn(x0, mean), t1 = __fsub_rn(x1, mean);
-    double s2 = block_sum_d((double) __fmul_rn(t0, t0) + (double) __fmul_rn(t1, t1), redd);
+    const double s2 = mk_block_sum_d((double) __fmul_rn(t0, t0) + (double) __fmul_rn(t1, t1), redd);
     const float var = (float) (s2 / K);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
     v[tid] = __fadd_rn(__fmul_rn(__fmul_rn(t0, scale), p.g[0]), p.b[0]);
@@ -186,21 +201,35 @@ __device__ void mk_layernorm(float * v, const MkLn & p, float eps, double * redd
     __syncthreads();
 }
 
+// Q8_0 re-quantisation of the K-vector (K = 1024 or 4096): eight lanes own
+// one 32-element block (four elements each), so every block of the vector is
+// processed at once instead of warps walking blocks one after another.
+__device__ __forceinline__ void mk_quant_block(const MkAct & x, int g, int sub) {
+    const float4 v = *(const float4 *) (x.v + g * 32 + sub * 4);
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    const float d = __fdiv_rn(m, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const int q0 = (int) roundf(__fmul_rn(v.x, id)), q1 = (int) roundf(__fmul_rn(v.y, id));
+    const int q2 = (int) roundf(__fmul_rn(v.z, id)), q3 = (int) roundf(__fmul_rn(v.w, id));
+    *(int *) (x.q + g * 32 + sub * 4) = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
+    int s = q0 + q1 + q2 + q3;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if (sub == 0) { x.d[g] = __half2float(__float2half_rn(d)); x.s[g] = s; }
+}
+
 __device__ void mk_quantize(const MkAct & x, int K, bool f16) {
-    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int tid = threadIdx.x;
     if (f16) {
         for (int i = tid; i < K; i += MK_THREADS) x.h[i] = __float2half_rn(x.v[i]);
     } else {
-        for (int blk = w; blk < K / 32; blk += MK_THREADS / 32) {
-            const float v = x.v[blk * 32 + lane];
-            const float amax = warp_max(fabsf(v));
-            const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-            const int q = (int) roundf(__fmul_rn(v, id));
-            x.q[blk * 32 + lane] = (int8_t) q;
-            const int s = warp_sum_i(q);
-            if (lane == 0) { x.d[blk] = __half2float(__float2half_rn(d)); x.s[blk] = s; }
-        }
+        const int g = tid >> 3, sub = tid & 7;              // 64 groups of 8 lanes
+        if (g < K / 32) mk_quant_block(x, g, sub);          // K = 1024: warps 8..15 idle
+        if (K == 4096) mk_quant_block(x, g + 64, sub);      // K = 4096: blocks 64..127
     }
     __syncthreads();
 }
@@ -256,58 +285,71 @@ __device__ __forceinline__ void mk_prefetch(const MkMat & W, int K, int r0, int 
 }
 
 // Dot products of the prefetched items with the prepared activation; row
-// sums (bias not added) land in rowsum[0 .. r1-r0).
+// sums (bias not added) land in rowsum[0 .. r1-r0).  All item partials are
+// formed first and their warp reductions run side by side.
+template <int T>
+__device__ __forceinline__ float mk_item_dot(const MkPref<T> & pf, int j, int b, const MkAct & x) {
+    float v = 0.0f;
+    if (T == T3B_Q4_0) {
+        const int4 x0 = *(const int4 *) (x.q + b * 32), x1 = *(const int4 *) (x.q + b * 32 + 16);
+        const uint4 qv = pf.q[j][0];
+        int si = 0;
+        si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), x0.x, si);
+        si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), x1.x, si);
+        si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), x0.y, si);
+        si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), x1.y, si);
+        si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), x0.z, si);
+        si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), x1.z, si);
+        si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), x0.w, si);
+        si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), x1.w, si);
+        si -= 8 * x.s[b];
+        v = __fmul_rn(__fmul_rn((float) si, pf.d[j]), x.d[b]);
+    } else if (T == T3B_Q8_0) {
+        const int4 x0 = *(const int4 *) (x.q + b * 32), x1 = *(const int4 *) (x.q + b * 32 + 16);
+        const uint4 q0 = pf.q[j][0], q1 = pf.q[j][1 % MkW<T>::QW];
+        int si = 0;
+        si = __dp4a((int) q0.x, x0.x, si); si = __dp4a((int) q0.y, x0.y, si);
+        si = __dp4a((int) q0.z, x0.z, si); si = __dp4a((int) q0.w, x0.w, si);
+        si = __dp4a((int) q1.x, x1.x, si); si = __dp4a((int) q1.y, x1.y, si);
+        si = __dp4a((int) q1.z, x1.z, si); si = __dp4a((int) q1.w, x1.w, si);
+        v = __fmul_rn(__fmul_rn((float) si, pf.d[j]), x.d[b]);
+    } else {
+#pragma unroll
+        for (int c = 0; c < MkW<T>::QW; ++c) {
+            const uint4 wv = pf.q[j][c];
+            const __half2 * wp = (const __half2 *) &wv;
+            const uint4 xv = *(const uint4 *) (x.h + b * 32 + c * 8);
+            const __half2 * xp = (const __half2 *) &xv;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 wf = __half22float2(wp[t]), xf = __half22float2(xp[t]);
+                v = fmaf(wf.x, xf.x, v);
+                v = fmaf(wf.y, xf.y, v);
+            }
+        }
+    }
+    return v;
+}
+
 template <int T>
 __device__ void mk_dot(const MkPref<T> & pf, int K, int r0, int r1, const MkAct & x, float * part, float * rowsum) {
     const int NB = K / 32, NP = NB / 32;   // warp portions per row
     const int nit = (r1 - r0) * NB;
     const int tid = threadIdx.x, lane = tid & 31;
+    float v[MK_MAXI];
 #pragma unroll
     for (int j = 0; j < MK_MAXI; ++j) {
-        const int i0 = j * MK_THREADS + (tid & ~31);   // first item of this warp
-        if (i0 >= nit) break;                          // warp-uniform
-        const int i = i0 + lane;
-        const int b = i % NB;
-        float v = 0.0f;
-        if (T == T3B_Q4_0) {
-            const int * xv = (const int *) (x.q + b * 32);
-            const uint4 qv = pf.q[j][0];
-            int si = 0;
-            si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), xv[0], si);
-            si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), xv[4], si);
-            si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), xv[1], si);
-            si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), xv[5], si);
-            si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), xv[2], si);
-            si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), xv[6], si);
-            si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), xv[3], si);
-            si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), xv[7], si);
-            si -= 8 * x.s[b];
-            v = __fmul_rn(__fmul_rn((float) si, pf.d[j]), x.d[b]);
-        } else if (T == T3B_Q8_0) {
-            const int * xv = (const int *) (x.q + b * 32);
-            const uint4 q0 = pf.q[j][0], q1 = pf.q[j][1 % MkW<T>::QW];
-            int si = 0;
-            si = __dp4a((int) q0.x, xv[0], si); si = __dp4a((int) q0.y, xv[1], si);
-            si = __dp4a((int) q0.z, xv[2], si); si = __dp4a((int) q0.w, xv[3], si);
-            si = __dp4a((int) q1.x, xv[4], si); si = __dp4a((int) q1.y, xv[5], si);
-            si = __dp4a((int) q1.z, xv[6], si); si = __dp4a((int) q1.w, xv[7], si);
-            v = __fmul_rn(__fmul_rn((float) si, pf.d[j]), x.d[b]);
-        } else {
+        const int i = j * MK_THREADS + tid;
+        v[j] = i < nit ? mk_item_dot<T>(pf, j, i % NB, x) : 0.0f;
+    }
 #pragma unroll
-            for (int c = 0; c < MkW<T>::QW; ++c) {
-                const uint4 wv = pf.q[j][c];
-                const __half2 * wp = (const __half2 *) &wv;
-                const __half2 * xp = (const __half2 *) (x.h + b * 32 + c * 8);
+    for (int o = 16; o; o >>= 1)
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float2 wf = __half22float2(wp[t]), xf = __half22float2(xp[t]);
-                    v = fmaf(wf.x, xf.x, v);
-                    v = fmaf(wf.y, xf.y, v);
-                }
-            }
-        }
-        v = warp_sum(v);
-        if (lane == 0) part[i0 / 32] = v;             // (row, portion) in item order
+        for (int j = 0; j < MK_MAXI; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+#pragma unroll
+    for (int j = 0; j < MK_MAXI; ++j) {
+        const int i0 = j * MK_THREADS + (tid & ~31);
+        if (lane == 0 && i0 < nit) part[i0 / 32] = v[j];
     }
     __syncthreads();
     for (int r = tid; r < r1 - r0; r += MK_THREADS) {
@@ -358,7 +400,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
 
 // Dynamic shared memory the megakernel needs.
 constexpr size_t mk_smem_bytes() {
-    return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 512) * 4;
+    return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 1024) * 4;
 }
 static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
 
@@ -425,14 +467,18 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bqkv + r0_ + tid) : 0.0f;
-                MK_STAMP(l * 10 + 0);
+                MK_STAMP(l * 20 + 0);
                 if (l > 0 && !mk_wait_vec(cX, (k - 1u) * G, bX, D, xres, a)) return;
-                MK_STAMP(l * 10 + 1);
+                MK_STAMP(l * 20 + 1);
                 for (int i = tid; i < D; i += MK_THREADS) vec[i] = xres[i];
                 __syncthreads();
+                MK_STAMP(l * 20 + 12);
                 mk_layernorm(vec, lp, a.eps, redd);
+                MK_STAMP(l * 20 + 13);
                 mk_quantize(act, D, T == T3B_F16);
+                MK_STAMP(l * 20 + 14);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                MK_STAMP(l * 20 + 15);
                 __half * kb = a.kv + (size_t) l * a.layer_stride;
                 if (tid < r1_ - r0_) {
                     const int n = r0_ + tid;
@@ -444,8 +490,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     }
                     bQKV[n] = v;
                 }
+                MK_STAMP(l * 20 + 16);
                 mk_release(cQKV);
-                MK_STAMP(l * 10 + 2);
+                MK_STAMP(l * 20 + 2);
             }
             // ---------------- P2: attention (CTA h < 16 owns head h) ----------
             if (cta < Hn) {
@@ -467,14 +514,17 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 asm volatile("cp.async.wait_all;" ::: "memory");
                 __syncthreads();
                 if (!ok) return;
-                MK_STAMP(l * 10 + 3);
+                MK_STAMP(l * 20 + 3);
                 if (tid < T3B_HD) {
                     kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
                     vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
                 }
                 __syncthreads();
                 const int L = pos + 1;
-                // scores: thread t owns keys t, t + 512
+                const int lane = tid & 31, w = tid >> 5;
+                // scores: thread t owns keys t and t + 512; each thread walks the
+                // 8 16-byte chunks of its K row in a rotated order so the warp's
+                // shared-memory reads spread over all banks
                 float sc[2];
                 float lm = -INFINITY;
 #pragma unroll
@@ -485,54 +535,75 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         const uint4 * kp = (const uint4 *) (kst + (size_t) j * T3B_HD);
                         float dot = 0.0f;
 #pragma unroll
-                        for (int cidx = 0; cidx < 8; ++cidx) {
-                            const uint4 uu = kp[cidx];
+                        for (int cc = 0; cc < 8; ++cc) {
+                            const int c = (cc + tid) & 7;
+                            const uint4 uu = kp[c];
+                            const float4 qa = *(const float4 *) (qkvh + c * 8), qb = *(const float4 *) (qkvh + c * 8 + 4);
                             const __half2 * hp = (const __half2 *) &uu;
-#pragma unroll
-                            for (int t = 0; t < 4; ++t) {
-                                const float2 f = __half22float2(hp[t]);
-                                dot = fmaf(qkvh[cidx * 8 + 2 * t], f.x, dot);
-                                dot = fmaf(qkvh[cidx * 8 + 2 * t + 1], f.y, dot);
-                            }
+                            const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
+                            const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
+                            dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
+                            dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
+                            dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
+                            dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
                         }
                         sc[u] = dot * 0.125f;
                         lm = fmaxf(lm, sc[u]);
                     }
                 }
-                float * rf = (float *) redd;
-                const float mx = block_max(lm, rf);
-                float * pw = att_s + 256;  // [L] weights
+                float * rf = (float *) redd;   // 64 floats: [0,16) max, [32,48) sum
+                lm = warp_max(lm);
+                if (lane == 0) rf[w] = lm;
+                __syncthreads();
+                const float mx = warp_max(rf[lane & 15]);
+                float * pw = att_s + 256;      // [L] weights
                 float ls = 0.0f;
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     const int j = tid + u * MK_THREADS;
                     if (j < L) { const float p = expf(sc[u] - mx); pw[j] = p; ls += p; }
                 }
-                const float lsum = block_sum(ls, rf);
+                ls = warp_sum(ls);
+                if (lane == 0) rf[32 + w] = ls;
                 __syncthreads();
-                // o[d] = sum_j p_j v_j[d]: 8 key groups x 64 dims
+                const float lsum = warp_sum(rf[32 + (lane & 15)]);
+                // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
+                // dims 2l, 2l+1; two accumulators hide the load latency
                 {
-                    const int d = tid & 63, g = tid >> 6;
-                    float o = 0.0f;
-                    for (int j = g; j < L; j += 8) o = fmaf(pw[j], __half2float(vst[(size_t) j * T3B_HD + d]), o);
-                    float * og = att_s + 256 + MK_MAX_POS;   // [8][64]
-                    og[g * 64 + d] = o;
+                    float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
+                    int j = w;
+                    for (; j + 16 < L; j += 32) {
+                        const float2 v0 = __half22float2(*(const __half2 *) (vst + (size_t) j * T3B_HD + 2 * lane));
+                        const float2 v1 = __half22float2(*(const __half2 *) (vst + (size_t) (j + 16) * T3B_HD + 2 * lane));
+                        const float p0 = pw[j], p1 = pw[j + 16];
+                        o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+                        o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
+                    }
+                    if (j < L) {
+                        const float2 v0 = __half22float2(*(const __half2 *) (vst + (size_t) j * T3B_HD + 2 * lane));
+                        const float p0 = pw[j];
+                        o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+                    }
+                    float * og = att_s + 256 + MK_MAX_POS;   // [16][64]
+                    og[w * 64 + 2 * lane] = o0.x + o1.x;
+                    og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
                     __syncthreads();
                     if (tid < 64) {
                         float t = 0.0f;
-                        for (int gg = 0; gg < 8; ++gg) t += og[gg * 64 + tid];
+#pragma unroll
+                        for (int gg = 0; gg < 16; ++gg) t += og[gg * 64 + tid];
                         bATT[h * 64 + tid] = t / lsum;
                     }
                 }
                 mk_release(cATT);
-                MK_STAMP(l * 10 + 4);
+                MK_STAMP(l * 20 + 4);
             }
             // ---------------- P3: proj + bias + residual -----------------------
             {
                 MK_GEMV_BEGIN(Ly.o, D, D)
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bo + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) return;
-                MK_STAMP(l * 10 + 5);
+                MK_STAMP(l * 20 + 5);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
                 if (tid < r1_ - r0_) {
@@ -547,7 +618,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
-                MK_STAMP(l * 10 + 6);
+                MK_STAMP(l * 20 + 6);
                 for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
                 __syncthreads();
                 mk_layernorm(vec, lp, a.eps, redd);
@@ -561,19 +632,21 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 MK_GEMV_BEGIN(Ly.fc2, 4 * D, D)
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
-                MK_STAMP(l * 10 + 7);
+                MK_STAMP(l * 20 + 7);
                 mk_quantize(act, 4 * D, T == T3B_F16);
+                MK_STAMP(l * 20 + 10);
                 mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
+                MK_STAMP(l * 20 + 11);
                 if (tid < r1_ - r0_) {
                     const int n = r0_ + tid;
                     bX[n] = __fadd_rn(__fadd_rn(rowsum[tid], bias), xmid[n]);
                 }
                 mk_release(cX);
-                MK_STAMP(l * 10 + 8);
+                MK_STAMP(l * 20 + 8);
             }
         }
         // ---------------- head: LN_f + speech_head ------------------------------
-        MK_STAMP(240);
+        MK_STAMP(480);
         {
             bool ok;
             if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, vec, act, part, rowsum, redd);
@@ -581,7 +654,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             else ok = mk_head<T3B_Q4_0>(a, step, vec, act, part, rowsum, redd);
             if (!ok) return;
         }
-        MK_STAMP(241);
+        MK_STAMP(481);
         // ---------------- sampler (CTA 0) and token broadcast -------------------
         if (cta == 0) {
             // host cancel flag (mapped memory): read before the wait so the
@@ -600,9 +673,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             __syncthreads();
             SampArgs sa = a.samp;
             sa.cond = lg; sa.cond_stride = 0; sa.uncond = nullptr;
-            MK_STAMP(242);
+            sa.tl = (a.tl && step == a.tl_step) ? a.tl + 490 : nullptr;
+            MK_STAMP(482);
             const int t = sample_row_block(sa, 0, smem);
-            MK_STAMP(243);
+            MK_STAMP(483);
             if (tid == 0) {
                 const int stop = (t == a.stop_token && !a.ignore_stop) || cancelled || t < 0;
                 *bTOK = (t & 0xffff) | (stop ? 0x10000 : 0);
@@ -612,7 +686,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         }
         {
             if (!mk_acquire(cTOK, (unsigned) (step + 1), a)) return;
-            MK_STAMP(244);
+            MK_STAMP(484);
             if (tid == 0) tokv = __ldcg(bTOK);
             __syncthreads();
             const int tv = tokv;

@@ -1147,7 +1147,17 @@ int t3b_op_sample_philox(const float * cond_dev, const float * uncond_dev, int r
     a.params = params_dev; a.params_per_row = 1; a.rng_mode = nullptr; a.mt = nullptr;
     a.ph_seed = (const unsigned long long *) seed_dev; a.ph_ctr = (unsigned long long *) counter_dev;
     a.tok_out = tokens_out_dev; a.step_tok = nullptr; a.done = nullptr; a.stop_token = -1; a.fx = fx;
+    // debug: T3B_SAMPLER_TIMELINE=<file> writes stage stamps of row 0 (16 u64 ns)
+    const char * tl_file = getenv("T3B_SAMPLER_TIMELINE");
+    if (tl_file) { cudaMalloc(&a.tl, 16 * 8); cudaMemsetAsync(a.tl, 0, 16 * 8, (cudaStream_t) cuda_stream); }
     sampler_kernel<<<rows, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, (cudaStream_t) cuda_stream>>>(a);
+    if (tl_file) {
+        unsigned long long h[16];
+        cudaMemcpyAsync(h, a.tl, sizeof h, cudaMemcpyDeviceToHost, (cudaStream_t) cuda_stream);
+        cudaStreamSynchronize((cudaStream_t) cuda_stream);
+        if (FILE * f = fopen(tl_file, "wb")) { fwrite(h, 8, 16, f); fclose(f); }
+        cudaFree(a.tl);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_sample_philox: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
     return T3B_OK;
