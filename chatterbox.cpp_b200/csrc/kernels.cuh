@@ -560,9 +560,120 @@ struct SampArgs {
 // dynamic smem: s[VMAX] f32 | keys[VMAX] u64 | e[VMAX] f32
 #define T3B_SAMPLER_SMEM (T3B_SAMPLER_VMAX * (4 + 8 + 4))
 
+// exp(x) with the host libm's rounding for N values at once: the cores are
+// computed first and every fix-up table probe is issued before any result
+// is needed, so the common case costs one memory round trip per batch.
+template <int N>
+__device__ __forceinline__ void t3_expf_batch(float (&x)[N], const ExpFix & f) {
+    const uint32_t mask = (1u << f.bits) - 1u;
+    uint32_t key[N], h[N];
+    unsigned long long e[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        key[n] = __float_as_uint(x[n]);
+        h[n] = t3_expf_hash(key[n], f.bits);
+        // fix-ups exist only for arguments in [-104, 0]
+        e[n] = (x[n] >= -104.0f && x[n] <= 0.0f) ? __ldg(f.tab + (h[n] & mask)) : 0ull;
+    }
+    unsigned pend = 0;
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const float y = t3_expf_core(x[n]);
+        // an empty slot is all-zero; test it first, because +0.0 has key 0
+        if (e[n] == 0ull) x[n] = y;
+        else if ((uint32_t) (e[n] >> 32) == key[n]) x[n] = __uint_as_float((uint32_t) e[n]);
+        else { x[n] = y; pend |= 1u << n; }
+    }
+    for (int p = 1; pend != 0u && p < f.max_probe; ++p) {
+#pragma unroll
+        for (int n = 0; n < N; ++n)
+            if ((pend >> n) & 1u) e[n] = __ldg(f.tab + ((h[n] + (uint32_t) p) & mask));
+#pragma unroll
+        for (int n = 0; n < N; ++n)
+            if ((pend >> n) & 1u) {
+                if (e[n] == 0ull) pend &= ~(1u << n);
+                else if ((uint32_t) (e[n] >> 32) == key[n]) { x[n] = __uint_as_float((uint32_t) e[n]); pend &= ~(1u << n); }
+            }
+    }
+}
+
+// Block-wide exclusive scan of doubles (blockDim.x multiple of 32, <= 1024).
+__device__ __forceinline__ double block_excl_scan_d(double v, double * red, double * total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    double incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    __syncthreads();
+    if (lane == 31) red[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        const double x = lane < nw ? red[lane] : 0.0;
+        double xi = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double n = __shfl_up_sync(0xffffffffu, xi, o);
+            if (lane >= o) xi += n;
+        }
+        if (lane < nw) red[lane] = xi - x;
+        if (lane == 31) red[32] = xi;
+    }
+    __syncthreads();
+    const double r = red[w] + (incl - v);
+    *total = red[32];
+    return r;
+}
+
+// Index of the first element whose running sum reaches `target`, for values
+// a[0..n) (float or double via the loader), split in per-thread contiguous
+// chunks.  The running sum is evaluated exactly enough (double) to locate the
+// crossing; *margin_ok tells whether both neighbours of the crossing are at
+// least eps away from target, so that any evaluation order that keeps its
+// error below eps crosses at the same index.  Returns n when the total stays
+// below target.
+template <class LoadF>
+__device__ int block_first_crossing(int n, double target, double eps, LoadF load, double * red, int * shi, bool * margin_ok) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const int per = (n + nth - 1) / nth;
+    const int c0 = min(n, tid * per), c1 = min(n, c0 + per);
+    double sum = 0.0;
+    for (int j = c0; j < c1; ++j) sum += load(j);
+    double total;
+    const double excl = block_excl_scan_d(sum, red, &total);
+    if (tid == 0) { shi[0] = n; shi[1] = 1; }
+    __syncthreads();
+    if (c0 < c1 && excl < target && excl + sum >= target) {
+        double run = excl, prev = excl;
+        int j = c0;
+        for (; j < c1; ++j) {
+            prev = run;
+            run += load(j);
+            if (run >= target) break;
+        }
+        if (j >= c1) j = c1 - 1;
+        shi[0] = j;
+        shi[1] = (run >= target + eps) && (j == 0 || prev < target - eps);
+    }
+    __syncthreads();
+    const int idx = shi[0];
+    if (idx == n) *margin_ok = total < target - eps;
+    else *margin_ok = shi[1] != 0;
+    __syncthreads();
+    return idx;
+}
+
 // One row of sample_next_token_ex by the whole block (any blockDim.x that
 // is a multiple of 32 and >= 256).  smraw: T3B_SAMPLER_SMEM bytes of shared
 // memory.  Returns the token (every thread), or -1 for a finished stream.
+//
+// Every value the reference computes is reproduced bit for bit: its
+// sequential float sums are either evaluated sequentially (one thread) or,
+// where the reference only compares a running sum with a threshold, located
+// with a double-precision parallel prefix and accepted only when the
+// crossing is farther from the threshold than the sequential rounding error
+// can reach; otherwise the sequential chain runs.
 __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned char * smraw) {
     float * s = (float *) smraw;
     unsigned long long * keys = (unsigned long long *) (smraw + T3B_SAMPLER_VMAX * 4);
@@ -570,13 +681,13 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     int * lst = (int *) keys;   // index list, reused after the sort
     __shared__ float redf[32];
     __shared__ int redi[32];
-    __shared__ int hist256[256];
+    __shared__ double redd[33];
     __shared__ unsigned seen[T3B_SAMPLER_VMAX / 32];
     __shared__ int shi[8];
     __shared__ float shf[4];
     __shared__ uint32_t mtx[625];
 
-    const int tid = threadIdx.x, nth = blockDim.x;
+    const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31;
     const int slot = a.slot_of ? a.slot_of[r] : r;
     if (a.done && a.done[slot]) return -1;
     unsigned long long * tls = (a.tl && r == 0) ? a.tl : nullptr;
@@ -586,6 +697,8 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const int V = a.V;
     const float * cond = a.cond + (long long) slot * a.cond_stride;
     const float * unc = a.uncond ? a.uncond + (long long) slot * a.uncond_stride : nullptr;
+    const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
+    const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
 
     // (0) CFG mix, (1) temperature  (main.cpp:735-738)
     const bool cfg = unc != nullptr && P.cfg_weight != 0.0f;
@@ -605,8 +718,20 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         float lm = -INFINITY;
         for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
         const float mx = block_max(lm, redf);
-        for (int i = tid; i < V; i += nth)
-            if (s[i] != -INFINITY && t3_expf_dev(__fsub_rn(s[i], mx), a.fx) < P.min_p) s[i] = -INFINITY;
+        for (int i0 = 0; i0 < V; i0 += 8 * nth) {
+            float x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * nth + tid;
+                x[u] = (i < V && s[i] != -INFINITY) ? __fsub_rn(s[i], mx) : -INFINITY;
+            }
+            t3_expf_batch<8>(x, a.fx);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * nth + tid;
+                if (i < V && s[i] != -INFINITY && x[u] < P.min_p) s[i] = -INFINITY;
+            }
+        }
         __syncthreads();
     }
 
@@ -614,48 +739,59 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     // (2) top-k (main.cpp:740-748): radix-select the value at descending
     // rank k, then keep s > thr (thr nudged by 1e-10f if fewer than k).
     if (P.top_k > 0 && P.top_k < V) {
+        // digits of 11, 11 and 10 bits: the first already spreads the scores
+        // over their exponent and leading mantissa bits, so few keys share a
+        // bin and plain shared-memory atomics stay cheap
+        int * hist = (int *) keys;     // 2048 bins, free until the top-p gather
         uint32_t prefix = 0u, maskb = 0u;
         int rank = P.top_k;
-        for (int pass = 0; pass < 4; ++pass) {
-            const int shift = 24 - 8 * pass;
-            for (int i = tid; i < 256; i += nth) hist256[i] = 0;
+        for (int pass = 0; pass < 3; ++pass) {
+            const int sh = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+            const int nb = pass == 2 ? 1024 : 2048;
+            for (int i = tid; i < nb; i += nth) hist[i] = 0;
             __syncthreads();
-            // float keys pile into a few bins (shared exponents): aggregate
-            // equal bins across the warp so each bin gets one atomic per warp
-            for (int i0 = 0; i0 < V; i0 += nth) {
-                const int i = i0 + tid;
-                int bin = 256;                               // 256 = not a candidate
-                if (i < V) {
-                    const uint32_t k = desc_key(s[i]);
-                    if ((k & maskb) == prefix) bin = (int) ((k >> shift) & 255u);
-                }
-                const unsigned peers = __match_any_sync(0xffffffffu, bin);
-                if (bin < 256 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist256[bin], __popc(peers));
+            for (int i = tid; i < V; i += nth) {
+                const uint32_t k = desc_key(s[i]);
+                if ((k & maskb) == prefix) atomicAdd(&hist[(k >> sh) & (uint32_t) (nb - 1)], 1);
             }
             __syncthreads();
-            if (tid < 32) {
-                int c[8], tot = 0;
+            // block scan over the bins: thread t owns bins [t*bpt, (t+1)*bpt)
+            const int bpt = (nb + nth - 1) / nth;
+            const int b0 = min(nb, tid * bpt), b1 = min(nb, b0 + bpt);
+            int tot = 0;
+            for (int b = b0; b < b1; ++b) tot += hist[b];
+            int inc = tot;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) { c[j] = hist256[tid * 8 + j]; tot += c[j]; }
-                int incl = tot;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += n;
+            }
+            if (lane == 31) redi[tid >> 5] = inc;
+            __syncthreads();
+            if (tid < 32) {
+                const int nw = nth >> 5;
+                const int v = lane < nw ? redi[lane] : 0;
+                int vi = v;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
-                    const int n = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (tid >= o) incl += n;
+                    const int n = __shfl_up_sync(0xffffffffu, vi, o);
+                    if (lane >= o) vi += n;
                 }
-                const int excl = incl - tot;
-                if (excl <= rank && rank < incl) {
-                    int run = excl;
-                    for (int j = 0; j < 8; ++j) {
-                        if (rank < run + c[j]) { shi[0] = tid * 8 + j; shi[1] = run; break; }
-                        run += c[j];
-                    }
+                if (lane < nw) redi[lane] = vi - v;
+            }
+            __syncthreads();
+            const int excl = redi[tid >> 5] + inc - tot;
+            if (excl <= rank && rank < excl + tot) {
+                int run = excl;
+                for (int b = b0; b < b1; ++b) {
+                    if (rank < run + hist[b]) { shi[0] = b; shi[1] = run; break; }
+                    run += hist[b];
                 }
             }
             __syncthreads();
             rank -= shi[1];
-            prefix |= ((uint32_t) shi[0]) << shift;
-            maskb |= 255u << shift;
+            prefix |= ((uint32_t) shi[0]) << sh;
+            maskb |= ((uint32_t) (nb - 1)) << sh;
             __syncthreads();
         }
         float thr = desc_key_inv(prefix);
@@ -673,54 +809,79 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     if (P.top_p < 1.0f) {
         if (tid == 0) shi[2] = 0;
         __syncthreads();
-        for (int i = tid; i < V; i += nth)
-            if (s[i] != -INFINITY) {
-                const int p = atomicAdd(&shi[2], 1);
-                keys[p] = ((unsigned long long) desc_key(s[i]) << 32) | (unsigned) i;
-            }
+        for (int i0 = 0; i0 < V; i0 += nth) {            // warp-aggregated gather
+            const int i = i0 + tid;
+            const bool keep = i < V && s[i] != -INFINITY;
+            const unsigned b = __ballot_sync(0xffffffffu, keep);
+            int base = 0;
+            if (lane == 0 && b) base = atomicAdd(&shi[2], __popc(b));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (keep) keys[base + __popc(b & ((1u << lane) - 1u))] = ((unsigned long long) desc_key(s[i]) << 32) | (unsigned) i;
+        }
         __syncthreads();
         const int c = shi[2];
         if (c > 0) {
-            int n2 = 1;
+            int n2 = 2;
             while (n2 < c) n2 <<= 1;
             for (int i = c + tid; i < n2; i += nth) keys[i] = ~0ull;
             __syncthreads();
             SAMP_STAMP(4);
+            // bitonic sort on compare-exchange pairs: pair p touches elements of
+            // the 64-element segment p/32 whenever the stride j <= 32, so those
+            // stages need only a warp barrier
             for (int k = 2; k <= n2; k <<= 1)
                 for (int j = k >> 1; j > 0; j >>= 1) {
-                    for (int i = tid; i < n2; i += nth) {
-                        const int ixj = i ^ j;
-                        if (ixj > i) {
-                            const unsigned long long x0 = keys[i], x1 = keys[ixj];
-                            const bool up = (i & k) == 0;
-                            if ((x0 > x1) == up) { keys[i] = x1; keys[ixj] = x0; }
-                        }
+                    for (int p = tid; p < n2 / 2; p += nth) {
+                        const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));
+                        const unsigned long long x0 = keys[i], x1 = keys[i + j];
+                        const bool up = (i & k) == 0;
+                        if ((x0 > x1) == up) { keys[i] = x1; keys[i + j] = x0; }
                     }
-                    __syncthreads();
+                    const int jn = j > 1 ? j >> 1 : k;          // next stage's stride
+                    if (j >= 64 || (jn >= 64 && k < n2)) __syncthreads();
+                    else __syncwarp();
                 }
+            __syncthreads();
             SAMP_STAMP(5);
             const float mx = s[(int) (keys[0] & 0xffffffffu)];
-            for (int j = tid; j < c; j += nth) e[j] = t3_expf_dev(__fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx), a.fx);
+            for (int j0 = 0; j0 < c; j0 += 8 * nth) {
+                float x[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int j = j0 + u * nth + tid;
+                    x[u] = j < c ? __fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx) : -INFINITY;
+                }
+                t3_expf_batch<8>(x, a.fx);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int j = j0 + u * nth + tid;
+                    if (j < c) e[j] = x[u];
+                }
+            }
             __syncthreads();
             if (tid == 0) shf[0] = seq_sum_f32(e, c);
             __syncthreads();
             const float psum = shf[0];
             for (int j = tid; j < c; j += nth) e[j] = __fdiv_rn(e[j], psum);
             __syncthreads();
-            if (tid == 0) {
-                const int j = seq_cut_f32(e, c, P.top_p);
-                shi[3] = j < c ? j + 1 : c;
+            // cut = 1 + first j with fl(...fl(e0 + e1)... + ej) >= top_p
+            bool ok;
+            const double eps = (double) (c + 2) * 0x1p-24 * 1.01 + 1e-12;
+            int j = block_first_crossing(c, (double) P.top_p, eps, [&](int q) { return (double) e[q]; }, redd, shi, &ok);
+            if (!ok) {
+                if (tid == 0) shi[3] = seq_cut_f32(e, c, P.top_p);
+                __syncthreads();
+                j = shi[3];
+                __syncthreads();
             }
-            __syncthreads();
-            for (int j = shi[3] + tid; j < c; j += nth) s[(int) (keys[j] & 0xffffffffu)] = -INFINITY;
+            const int cut = j < c ? j + 1 : c;
+            for (int q = cut + tid; q < c; q += nth) s[(int) (keys[q] & 0xffffffffu)] = -INFINITY;
             __syncthreads();
         }
     }
 
     SAMP_STAMP(6);
     // (4) repetition penalty over distinct history ids (main.cpp:774-781)
-    const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
-    const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
     if (P.repeat_penalty != 1.0f && hl > 0) {
         for (int i = tid; i < (V + 31) / 32; i += nth) seen[i] = 0u;
         __syncthreads();
@@ -738,18 +899,34 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     }
 
     SAMP_STAMP(7);
-    // (5) softmax over survivors in index order (main.cpp:783-793)
+    // (5) softmax over survivors in index order (main.cpp:783-793).  Entries
+    // that were dropped get p = 0, which adds nothing to any later sum, so
+    // they are equivalent to survivors whose exp underflowed.
     float lm = -INFINITY;
     for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
     const float mx = block_max(lm, redf);
-    // index-ordered compaction: thread t owns [t*per, (t+1)*per)
+    for (int i0 = 0; i0 < V; i0 += 8 * nth) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * nth + tid;
+            x[u] = (i < V && s[i] != -INFINITY) ? __fsub_rn(s[i], mx) : -INFINITY;
+        }
+        t3_expf_batch<8>(x, a.fx);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * nth + tid;
+            if (i < V) s[i] = x[u];       // exp(-inf) = 0 for dropped entries
+        }
+    }
+    __syncthreads();
+    // index-ordered compaction of the nonzero p: thread t owns [t*per, (t+1)*per)
     const int per = (V + nth - 1) / nth;
     const int i0 = min(V, tid * per), i1 = min(V, i0 + per);
     int cnt = 0;
-    for (int i = i0; i < i1; ++i) cnt += s[i] != -INFINITY ? 1 : 0;
-    // block exclusive scan of cnt
+    for (int i = i0; i < i1; ++i) cnt += s[i] != 0.0f ? 1 : 0;
     int incl = cnt;
-    const int lane = tid & 31, w = tid >> 5;
+    const int w = tid >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, incl, o);
@@ -773,7 +950,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     {
         int o = redi[w] + incl - cnt;
         for (int i = i0; i < i1; ++i)
-            if (s[i] != -INFINITY) { lst[o] = i; e[o] = t3_expf_dev(__fsub_rn(s[i], mx), a.fx); ++o; }
+            if (s[i] != 0.0f) { lst[o] = i; e[o] = s[i]; ++o; }
     }
     __syncthreads();
     const int cf = shi[4];
@@ -787,11 +964,23 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         __syncthreads();
         if (P.temp <= 0.0f) {
             // (6) first maximum in index order
+            const int per2 = (cf + nth - 1) / nth;
+            const int c0 = min(cf, tid * per2), c1 = min(cf, c0 + per2);
+            float bp = -1.0f; int bi = 0x7fffffff;
+            for (int j = c0; j < c1; ++j) if (e[j] > bp) { bp = e[j]; bi = lst[j]; }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+            }
+            if (lane == 0) { redf[w] = bp; redi[w] = bi; }
+            __syncthreads();
             if (tid == 0) {
-                int best = lst[0]; float bp = e[0];
-                for (int j = 1; j < cf; ++j) if (e[j] > bp) { bp = e[j]; best = lst[j]; }
-                // an index before the first survivor has p = 0 < bp
-                shi[5] = best;
+                float b = -1.0f; int ix = 0x7fffffff;
+                for (int q = 0; q < (nth >> 5); ++q)
+                    if (redf[q] > b || (redf[q] == b && redi[q] < ix)) { b = redf[q]; ix = redi[q]; }
+                shi[5] = ix;
             }
             __syncthreads();
             tok = shi[5];
@@ -822,42 +1011,54 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 if (tid == 0) a.ph_ctr[slot] = ct + 1ull;
             }
             SAMP_STAMP(10);
-            if (tid == 0) {
-                double sum = (double) x1;
-                sum += (double) x2 * 4294967296.0;
-                double u = sum / 18446744073709551616.0;
-                if (u >= 1.0) u = nextafter(1.0, 0.0);
-                const double dsum = seq_sum_f64(e, cf);
-                int pick = V - 1;
-                if (u <= 0.0) pick = 0;
-                else {
-                    // cp_i = cp_{i-1} + p_i / dsum (partial_sum of the
-                    // normalised weights); the divisions do not depend on
-                    // the running sum, so four are issued ahead of the adds
-                    double c = 0.0;
-                    int j = 0;
-                    bool found = false;
-                    for (; j + 4 <= cf && !found; j += 4) {
-                        const double q0 = (double) e[j] / dsum, q1 = (double) e[j + 1] / dsum;
-                        const double q2 = (double) e[j + 2] / dsum, q3 = (double) e[j + 3] / dsum;
-                        const double qq[4] = {q0, q1, q2, q3};
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            c = __dadd_rn(c, qq[t]);
-                            const double ci = lst[j + t] == V - 1 ? 1.0 : c;
-                            if (ci >= u) { pick = lst[j + t]; found = true; break; }
-                        }
-                    }
-                    for (; j < cf && !found; ++j) {
-                        c = __dadd_rn(c, (double) e[j] / dsum);
-                        const double ci = lst[j] == V - 1 ? 1.0 : c;
-                        if (ci >= u) { pick = lst[j]; found = true; }
-                    }
-                }
-                shi[6] = pick;
+            double sum = (double) x1;
+            sum += (double) x2 * 4294967296.0;
+            double u = sum / 18446744073709551616.0;
+            if (u >= 1.0) u = nextafter(1.0, 0.0);
+            // dsum = sequential double sum of the p (std::accumulate).  When
+            // every p >= 2^-29 all partial sums (< 2) are exact in double, so
+            // any order gives the same value.
+            float pmin = INFINITY;
+            for (int j = tid; j < cf; j += nth) pmin = fminf(pmin, e[j]);
+            pmin = -block_max(-pmin, redf);
+            double dsum;
+            if (pmin >= 0x1p-29f) {
+                double ls = 0.0;
+                for (int j = tid; j < cf; j += nth) ls += (double) e[j];
+                double tot;
+                block_excl_scan_d(ls, redd, &tot);
+                dsum = tot;
+            } else {
+                if (tid == 0) redd[32] = seq_sum_f64(e, cf);
+                __syncthreads();
+                dsum = redd[32];
+                __syncthreads();
             }
-            __syncthreads();
-            tok = shi[6];
+            // lower_bound(cp, u) with cp_j = cp_{j-1} + p_j / dsum and the last
+            // entry (index V-1) forced to 1
+            int pick;
+            if (u <= 0.0) pick = 0;
+            else {
+                bool ok;
+                const double eps = (double) (cf + 16) * 0x1p-52;
+                const int j = block_first_crossing(cf, u, eps, [&](int q) { return (double) e[q] / dsum; }, redd, shi, &ok);
+                if (ok) pick = j < cf ? lst[j] : V - 1;
+                else {
+                    if (tid == 0) {
+                        int pk = V - 1;
+                        double c = 0.0;
+                        for (int q = 0; q < cf; ++q) {
+                            c = __dadd_rn(c, (double) e[q] / dsum);
+                            const double ci = lst[q] == V - 1 ? 1.0 : c;
+                            if (ci >= u) { pk = lst[q]; break; }
+                        }
+                        shi[6] = pk;
+                    }
+                    __syncthreads();
+                    pick = shi[6];
+                }
+            }
+            tok = pick;
         }
     }
     SAMP_STAMP(11);
