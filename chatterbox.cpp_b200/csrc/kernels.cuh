@@ -421,19 +421,24 @@ __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a)
 // ---------------------------------------------------------------------------
 struct ExpFix { const unsigned long long * tab; int bits; int max_probe; };
 
-// exp with the host libm's rounding: t3_expf_core + fix-up table lookup.
+// exp with the host libm's rounding: t3_expf_core + fix-up table lookup
+// (two 32-byte buckets, read together).
+__device__ __forceinline__ float t3_expf_fix(float x, float y, uint4 a0, uint4 a1, uint4 b0, uint4 b1) {
+    const uint32_t key = __float_as_uint(x);
+    const uint32_t w[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
+                            b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k)   // slot = (key << 32) | value: little-endian words (value, key)
+        if ((w[2 * k] | w[2 * k + 1]) != 0u && w[2 * k + 1] == key) y = __uint_as_float(w[2 * k]);
+    return y;
+}
 __device__ __forceinline__ float t3_expf_dev(float x, const ExpFix & f) {
     const float y = t3_expf_core(x);
+    if (!(x >= -104.0f && x <= 0.0f)) return y;
     const uint32_t key = __float_as_uint(x);
-    const uint32_t mask = (1u << f.bits) - 1u;
-    uint32_t h = t3_expf_hash(key, f.bits);
-    for (int i = 0; i < f.max_probe; ++i) {
-        const unsigned long long e = __ldg(f.tab + ((h + (uint32_t) i) & mask));
-        // an empty slot is all-zero; test it first, because +0.0 has key 0
-        if (e == 0ull) break;
-        if ((uint32_t) (e >> 32) == key) return __uint_as_float((uint32_t) e);
-    }
-    return y;
+    const uint4 * b1 = (const uint4 *) (f.tab + (size_t) t3_expf_hash1(key, f.bits) * T3_EXPF_SLOTS);
+    const uint4 * b2 = (const uint4 *) (f.tab + (size_t) t3_expf_hash2(key, f.bits) * T3_EXPF_SLOTS);
+    return t3_expf_fix(x, y, __ldg(b1), __ldg(b1 + 1), __ldg(b2), __ldg(b2 + 1));
 }
 
 // float -> 32-bit key whose ascending order is the float's DEScending order.
@@ -560,41 +565,25 @@ struct SampArgs {
 // dynamic smem: s[VMAX] f32 | keys[VMAX] u64 | e[VMAX] f32
 #define T3B_SAMPLER_SMEM (T3B_SAMPLER_VMAX * (4 + 8 + 4))
 
-// exp(x) with the host libm's rounding for N values at once: the cores are
-// computed first and every fix-up table probe is issued before any result
-// is needed, so the common case costs one memory round trip per batch.
+// exp(x) with the host libm's rounding for N values at once: every bucket
+// read is issued before any result is needed, so a batch costs one memory
+// round trip.
 template <int N>
 __device__ __forceinline__ void t3_expf_batch(float (&x)[N], const ExpFix & f) {
-    const uint32_t mask = (1u << f.bits) - 1u;
-    uint32_t key[N], h[N];
-    unsigned long long e[N];
+    uint4 a0[N], a1[N], b0[N], b1[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) {
-        key[n] = __float_as_uint(x[n]);
-        h[n] = t3_expf_hash(key[n], f.bits);
-        // fix-ups exist only for arguments in [-104, 0]
-        e[n] = (x[n] >= -104.0f && x[n] <= 0.0f) ? __ldg(f.tab + (h[n] & mask)) : 0ull;
+        if (x[n] >= -104.0f && x[n] <= 0.0f) {   // fix-ups exist only in [-104, 0]
+            const uint32_t key = __float_as_uint(x[n]);
+            const uint4 * p1 = (const uint4 *) (f.tab + (size_t) t3_expf_hash1(key, f.bits) * T3_EXPF_SLOTS);
+            const uint4 * p2 = (const uint4 *) (f.tab + (size_t) t3_expf_hash2(key, f.bits) * T3_EXPF_SLOTS);
+            a0[n] = __ldg(p1); a1[n] = __ldg(p1 + 1); b0[n] = __ldg(p2); b1[n] = __ldg(p2 + 1);
+        } else {
+            a0[n] = a1[n] = b0[n] = b1[n] = make_uint4(0u, 0u, 0u, 0u);
+        }
     }
-    unsigned pend = 0;
 #pragma unroll
-    for (int n = 0; n < N; ++n) {
-        const float y = t3_expf_core(x[n]);
-        // an empty slot is all-zero; test it first, because +0.0 has key 0
-        if (e[n] == 0ull) x[n] = y;
-        else if ((uint32_t) (e[n] >> 32) == key[n]) x[n] = __uint_as_float((uint32_t) e[n]);
-        else { x[n] = y; pend |= 1u << n; }
-    }
-    for (int p = 1; pend != 0u && p < f.max_probe; ++p) {
-#pragma unroll
-        for (int n = 0; n < N; ++n)
-            if ((pend >> n) & 1u) e[n] = __ldg(f.tab + ((h[n] + (uint32_t) p) & mask));
-#pragma unroll
-        for (int n = 0; n < N; ++n)
-            if ((pend >> n) & 1u) {
-                if (e[n] == 0ull) pend &= ~(1u << n);
-                else if ((uint32_t) (e[n] >> 32) == key[n]) { x[n] = __uint_as_float((uint32_t) e[n]); pend &= ~(1u << n); }
-            }
-    }
+    for (int n = 0; n < N; ++n) x[n] = t3_expf_fix(x[n], t3_expf_core(x[n]), a0[n], a1[n], b0[n], b1[n]);
 }
 
 // Block-wide exclusive scan of doubles (blockDim.x multiple of 32, <= 1024).
@@ -718,16 +707,16 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         float lm = -INFINITY;
         for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
         const float mx = block_max(lm, redf);
-        for (int i0 = 0; i0 < V; i0 += 8 * nth) {
-            float x[8];
+        for (int i0 = 0; i0 < V; i0 += 4 * nth) {
+            float x[4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * nth + tid;
                 x[u] = (i < V && s[i] != -INFINITY) ? __fsub_rn(s[i], mx) : -INFINITY;
             }
-            t3_expf_batch<8>(x, a.fx);
+            t3_expf_batch<4>(x, a.fx);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * nth + tid;
                 if (i < V && s[i] != -INFINITY && x[u] < P.min_p) s[i] = -INFINITY;
             }
@@ -844,16 +833,16 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             __syncthreads();
             SAMP_STAMP(5);
             const float mx = s[(int) (keys[0] & 0xffffffffu)];
-            for (int j0 = 0; j0 < c; j0 += 8 * nth) {
-                float x[8];
+            for (int j0 = 0; j0 < c; j0 += 4 * nth) {
+                float x[4];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 4; ++u) {
                     const int j = j0 + u * nth + tid;
                     x[u] = j < c ? __fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx) : -INFINITY;
                 }
-                t3_expf_batch<8>(x, a.fx);
+                t3_expf_batch<4>(x, a.fx);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 4; ++u) {
                     const int j = j0 + u * nth + tid;
                     if (j < c) e[j] = x[u];
                 }
@@ -905,16 +894,16 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     float lm = -INFINITY;
     for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
     const float mx = block_max(lm, redf);
-    for (int i0 = 0; i0 < V; i0 += 8 * nth) {
-        float x[8];
+    for (int i0 = 0; i0 < V; i0 += 4 * nth) {
+        float x[4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 4; ++u) {
             const int i = i0 + u * nth + tid;
             x[u] = (i < V && s[i] != -INFINITY) ? __fsub_rn(s[i], mx) : -INFINITY;
         }
-        t3_expf_batch<8>(x, a.fx);
+        t3_expf_batch<4>(x, a.fx);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 4; ++u) {
             const int i = i0 + u * nth + tid;
             if (i < V) s[i] = x[u];       // exp(-inf) = 0 for dropped entries
         }

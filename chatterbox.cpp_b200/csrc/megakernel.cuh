@@ -566,7 +566,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 ls = warp_sum(ls);
                 if (lane == 0) rf[32 + w] = ls;
                 __syncthreads();
-                const float lsum = warp_sum(rf[32 + (lane & 15)]);
+                const float lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
                 // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
                 // dims 2l, 2l+1; two accumulators hide the load latency
                 {

@@ -67,7 +67,18 @@ T3_HD float t3_expf_core(float xf) {
     return (float) y;
 }
 
-// Hash of a float's bit pattern into a table of 2^bits slots.
-T3_HD uint32_t t3_expf_hash(uint32_t key, int bits) {
+// The two candidate buckets of a float's bit pattern in a table of 2^bits
+// buckets (two-choice hashing: an entry lives in the emptier of the two, so
+// a lookup reads exactly two buckets).
+T3_HD uint32_t t3_expf_hash1(uint32_t key, int bits) {
     return (key * 2654435761u) >> (32 - bits);
 }
+T3_HD uint32_t t3_expf_hash2(uint32_t key, int bits) {
+    uint32_t h = key ^ (key >> 15);
+    h *= 0x2c1b3c6du;
+    h ^= h >> 12;
+    h *= 0x297a2d39u;
+    h ^= h >> 15;
+    return h >> (32 - bits);
+}
+#define T3_EXPF_SLOTS 4   /* 8-byte slots per bucket: one 32-byte sector */

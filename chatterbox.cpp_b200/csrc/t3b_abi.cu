@@ -44,35 +44,44 @@ void set_err(std::string * dst, const char * fmt, ...) {
 // --------------------------------------------------------------------------
 // exp fix-up hash table (one per device)
 // --------------------------------------------------------------------------
-constexpr int kFixBits = 18;
-struct FixTab { unsigned long long * dev = nullptr; int max_probe = 0; };
+constexpr int kFixBits = 16;   // 2^16 buckets x 4 slots x 8 bytes = 2 MB
+struct FixTab { unsigned long long * dev = nullptr; int bits = kFixBits; };
 std::mutex g_fix_mu;
 std::map<int, FixTab> g_fix;
+
+// Builds the two-choice table: each entry goes to the emptier of its two
+// buckets.  Returns false if a bucket pair is full (never for the shipped
+// fix-up list at this size; the caller then doubles the table).
+bool build_fix_table(int bits, std::vector<unsigned long long> & tab) {
+    const uint32_t nb = 1u << bits;
+    tab.assign((size_t) nb * T3_EXPF_SLOTS, 0ull);
+    std::vector<int> fill(nb, 0);
+    for (uint32_t i = 0; i < t3_expf_fixup_n; ++i) {
+        const uint32_t key = t3_expf_fixup[i][0];
+        const uint32_t h1 = t3_expf_hash1(key, bits), h2 = t3_expf_hash2(key, bits);
+        const uint32_t b = fill[h2] < fill[h1] ? h2 : h1;
+        if (fill[b] >= T3_EXPF_SLOTS) return false;
+        tab[(size_t) b * T3_EXPF_SLOTS + fill[b]++] = ((unsigned long long) key << 32) | t3_expf_fixup[i][1];
+    }
+    return true;
+}
 
 int fix_table(int device, ExpFix * out, std::string * ERRP) {
     std::lock_guard<std::mutex> lk(g_fix_mu);
     auto it = g_fix.find(device);
     if (it == g_fix.end()) {
-        const uint32_t n = 1u << kFixBits, mask = n - 1u;
-        std::vector<unsigned long long> tab(n, 0ull);
-        int maxp = 1;
-        for (uint32_t i = 0; i < t3_expf_fixup_n; ++i) {
-            const uint32_t key = t3_expf_fixup[i][0];
-            uint32_t h = t3_expf_hash(key, kFixBits);
-            int probe = 1;
-            while (tab[h & mask] != 0ull) { ++h; ++probe; }
-            tab[h & mask] = ((unsigned long long) key << 32) | t3_expf_fixup[i][1];
-            maxp = std::max(maxp, probe);
-        }
+        std::vector<unsigned long long> tab;
+        int bits = kFixBits;
+        while (!build_fix_table(bits, tab)) ++bits;
         FixTab ft;
-        ft.max_probe = maxp;
-        CK(cudaMalloc(&ft.dev, n * sizeof(unsigned long long)));
-        CK(cudaMemcpy(ft.dev, tab.data(), n * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+        ft.bits = bits;
+        CK(cudaMalloc(&ft.dev, tab.size() * sizeof(unsigned long long)));
+        CK(cudaMemcpy(ft.dev, tab.data(), tab.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice));
         it = g_fix.emplace(device, ft).first;
     }
     out->tab = it->second.dev;
-    out->bits = kFixBits;
-    out->max_probe = it->second.max_probe;
+    out->bits = it->second.bits;
+    out->max_probe = 0;
     return T3B_OK;
 }
 
