@@ -500,12 +500,26 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32
 // One thread walks them; operands come in as float4 loads, eight at a time,
 // so the only serial dependency left is the add itself.
 __device__ __forceinline__ float seq_sum_f32(const float * a, int n) {
+    // operands for the next 16 adds are loaded while the current 16 run
     float s = 0.0f;
     int j = 0;
-    for (; j + 8 <= n; j += 8) {
-        const float4 u = *(const float4 *) (a + j), v = *(const float4 *) (a + j + 4);
-        s = __fadd_rn(s, u.x); s = __fadd_rn(s, u.y); s = __fadd_rn(s, u.z); s = __fadd_rn(s, u.w);
-        s = __fadd_rn(s, v.x); s = __fadd_rn(s, v.y); s = __fadd_rn(s, v.z); s = __fadd_rn(s, v.w);
+    if (n >= 16) {
+        float4 c0 = *(const float4 *) (a), c1 = *(const float4 *) (a + 4), c2 = *(const float4 *) (a + 8),
+               c3 = *(const float4 *) (a + 12);
+        for (; j + 32 <= n; j += 16) {
+            const float4 n0 = *(const float4 *) (a + j + 16), n1 = *(const float4 *) (a + j + 20);
+            const float4 n2 = *(const float4 *) (a + j + 24), n3 = *(const float4 *) (a + j + 28);
+            s = __fadd_rn(s, c0.x); s = __fadd_rn(s, c0.y); s = __fadd_rn(s, c0.z); s = __fadd_rn(s, c0.w);
+            s = __fadd_rn(s, c1.x); s = __fadd_rn(s, c1.y); s = __fadd_rn(s, c1.z); s = __fadd_rn(s, c1.w);
+            s = __fadd_rn(s, c2.x); s = __fadd_rn(s, c2.y); s = __fadd_rn(s, c2.z); s = __fadd_rn(s, c2.w);
+            s = __fadd_rn(s, c3.x); s = __fadd_rn(s, c3.y); s = __fadd_rn(s, c3.z); s = __fadd_rn(s, c3.w);
+            c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        }
+        s = __fadd_rn(s, c0.x); s = __fadd_rn(s, c0.y); s = __fadd_rn(s, c0.z); s = __fadd_rn(s, c0.w);
+        s = __fadd_rn(s, c1.x); s = __fadd_rn(s, c1.y); s = __fadd_rn(s, c1.z); s = __fadd_rn(s, c1.w);
+        s = __fadd_rn(s, c2.x); s = __fadd_rn(s, c2.y); s = __fadd_rn(s, c2.z); s = __fadd_rn(s, c2.w);
+        s = __fadd_rn(s, c3.x); s = __fadd_rn(s, c3.y); s = __fadd_rn(s, c3.z); s = __fadd_rn(s, c3.w);
+        j += 16;
     }
     for (; j < n; ++j) s = __fadd_rn(s, a[j]);
     return s;

@@ -186,16 +186,34 @@ __device__ __forceinline__ double mk_block_sum_d(double v, double * red) {
     return r;
 }
 
-// LayerNorm of the 1024-vector v in place (two elements per thread).
+// Sum of two doubles over the CTA with a single barrier (see mk_block_sum_d).
+__device__ __forceinline__ double2 mk_block_sum_d2(double a, double b, double * red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) { a += __shfl_xor_sync(0xffffffffu, a, o); b += __shfl_xor_sync(0xffffffffu, b, o); }
+    if (lane == 0) { red[w] = a; red[16 + w] = b; }
+    __syncthreads();
+    double ra = red[lane & 15], rb = red[16 + (lane & 15)];
+#pragma unroll
+    for (int o = 8; o; o >>= 1) { ra += __shfl_xor_sync(0xffffffffu, ra, o); rb += __shfl_xor_sync(0xffffffffu, rb, o); }
+    __syncthreads();
+    return make_double2(ra, rb);
+}
+
+// LayerNorm of the 1024-vector v in place (two elements per thread).  Mean
+// and variance come from one reduction of sum(x) and sum(x^2) in double
+// (var = E[x^2] - mean^2), which differs from ggml's two-pass float form only
+// in the last bits of the statistics.
 __device__ void mk_layernorm(float * v, const MkLn & p, float eps, double * redd) {
     const int tid = threadIdx.x, K = 2 * MK_THREADS;
     const float x0 = v[tid], x1 = v[tid + MK_THREADS];
-    const double s = mk_block_sum_d((double) x0 + (double) x1, redd);
-    const float mean = (float) (s / K);
-    const float t0 = __fsub_rn(x0, mean), t1 = __fsub_rn(x1, mean);
-    const double s2 = mk_block_sum_d((double) __fmul_rn(t0, t0) + (double) __fmul_rn(t1, t1), redd);
-    const float var = (float) (s2 / K);
+    const double d0 = x0, d1 = x1;
+    const double2 m = mk_block_sum_d2(d0 + d1, d0 * d0 + d1 * d1, redd);
+    const double meand = m.x / K;
+    const float mean = (float) meand;
+    const float var = (float) fmax(m.y / K - meand * meand, 0.0);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    const float t0 = __fsub_rn(x0, mean), t1 = __fsub_rn(x1, mean);
     v[tid] = __fadd_rn(__fmul_rn(__fmul_rn(t0, scale), p.g[0]), p.b[0]);
     v[tid + MK_THREADS] = __fadd_rn(__fmul_rn(__fmul_rn(t1, scale), p.g[1]), p.b[1]);
     __syncthreads();
@@ -365,12 +383,6 @@ __device__ void mk_dot(const MkPref<T> & pf, int K, int r0, int r1, const MkAct 
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int mk_r0(int N, int c, int G) { return (int) (((long long) N * c) / G); }
 
-// rows of one GEMV phase: prefetch (before the caller's wait), then dot
-#define MK_GEMV_BEGIN(W, K, N)                                                   \
-    const int r0_ = mk_r0((N), blockIdx.x, gridDim.x), r1_ = mk_r0((N), blockIdx.x + 1, gridDim.x); \
-    MkPref<T> pf_;                                                              \
-    mk_prefetch<T>((W), (K), r0_, r1_, pf_);
-
 // LN_f + speech_head rows of this CTA; the head keeps its own weight type.
 template <int HT>
 __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, const MkAct & act, float * part,
@@ -403,6 +415,19 @@ constexpr size_t mk_smem_bytes() {
     return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 1024) * 4;
 }
 static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
+
+// Bulk prefetch of a CTA's weight slice into L2 (one instruction, no
+// completion to track): issued one phase ahead so the register prefetch of
+// that phase hits L2 instead of HBM.
+__device__ __forceinline__ void mk_l2_prefetch(const MkMat & W, int N) {
+    if (threadIdx.x == 0) {
+        const int r0 = mk_r0(N, blockIdx.x, gridDim.x), r1 = mk_r0(N, blockIdx.x + 1, gridDim.x);
+        const unsigned bytes = (unsigned) ((r1 - r0) * W.rb);
+        if (bytes >= 16u)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(W.w + (size_t) r0 * W.rb), "r"(bytes & ~15u)
+                         : "memory");
+    }
+}
 
 // rows of one GEMV phase: prefetch (before the caller's wait)
 #define MK_GEMV_BEGIN(W, K, N)                                                                      \
@@ -465,6 +490,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
             {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
+                mk_l2_prefetch(Ly.o, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bqkv + r0_ + tid) : 0.0f;
                 MK_STAMP(l * 20 + 0);
@@ -601,6 +627,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P3: proj + bias + residual -----------------------
             {
                 MK_GEMV_BEGIN(Ly.o, D, D)
+                mk_l2_prefetch(Ly.fc, 4 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bo + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) return;
                 MK_STAMP(l * 20 + 5);
@@ -615,6 +642,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P4: LN2 + fc + GELU ------------------------------
             {
                 MK_GEMV_BEGIN(Ly.fc, D, 4 * D)
+                mk_l2_prefetch(Ly.fc2, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
@@ -630,6 +658,8 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P5: fc2 + bias + residual ------------------------
             {
                 MK_GEMV_BEGIN(Ly.fc2, 4 * D, D)
+                if (l + 1 < NL) mk_l2_prefetch(a.layers[l + 1].qkv, 3 * D);
+                else mk_l2_prefetch(a.head, a.V);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
                 MK_STAMP(l * 20 + 7);
