@@ -28,7 +28,7 @@ EXPORTS = [
     "t3b_create", "t3b_destroy", "t3b_last_error", "t3b_stream_alloc", "t3b_prefill", "t3b_step", "t3b_sample",
     "t3b_set_rng", "t3b_set_rng_state", "t3b_get_rng_state", "t3b_set_history", "t3b_decode", "t3b_cancel",
     "t3b_last_device_ms", "t3b_stream_handle", "t3b_trace_logits", "t3b_get_logits_trace", "t3b_op_row_bytes", "t3b_op_repack", "t3b_op_gemv", "t3b_op_attention",
-    "t3b_op_sample_philox", "t3b_expf_fixup_count", "t3b_op_expf",
+    "t3b_op_sample_philox", "t3b_expf_fixup_count", "t3b_op_expf", "t3b_op_attention_noalloc",
 ]
 
 
@@ -97,6 +97,7 @@ def lib():
             "t3b_op_gemv": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, C.c_float, vp, vp, C.c_int,
                                       vp, vp]),
             "t3b_op_attention": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
+            "t3b_op_attention_noalloc": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
             "t3b_op_sample_philox": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, C.c_int, vp, vp, vp, vp, vp]),
             "t3b_expf_fixup_count": (C.c_int, []),
             "t3b_op_expf": (C.c_int, [vp, vp, C.c_int, vp]),

@@ -1184,3 +1184,77 @@ int t3b_op_expf(const float * in_dev, float * out_dev, int n, void * cuda_stream
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode attention (t3b_op_attention_noalloc)
+//
+// For callers that may not allocate device memory on their decode path: the
+// split partials and completion counters of attn_decode_kernel live in fixed
+// static device arrays instead of cudaMalloc'd scratch.  In host code these
+// symbols are host-side stand-ins, never device addresses: their device
+// addresses are resolved once per device with cudaGetSymbolAddress (with that
+// device current) and cached.  Nothing here calls cudaMalloc or cudaFree.
+// ---------------------------------------------------------------------------
+#define T3B_NOALLOC_PART_FLOATS (1u << 20)   // 4 MiB of (m, l, o[64]) split records
+#define T3B_NOALLOC_CNT 4096u                // (row, head) completion counters
+static __device__ __align__(256) float g_noalloc_part[T3B_NOALLOC_PART_FLOATS];
+static __device__ __align__(256) unsigned g_noalloc_cnt[T3B_NOALLOC_CNT + 64];   // + error word
+
+namespace {
+struct NoAllocScratch { float * part = nullptr; unsigned * cnt = nullptr; };
+std::mutex g_noalloc_mu;
+std::map<int, NoAllocScratch> g_noalloc;
+}
+
+extern "C" int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev, const void * v_dev, int M,
+                                        int n_head, int max_ctx, const int32_t * len_dev, float * out_dev,
+                                        void * cuda_stream) {
+    if (!q_dev || !k_dev || !v_dev || !len_dev || !out_dev || M <= 0 || n_head <= 0 || max_ctx <= 0) {
+        set_err(nullptr, "t3b_op_attention_noalloc: bad args");
+        return T3B_ERR_ARG;
+    }
+    const long long s_max = (max_ctx + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;
+    const long long records = (long long) M * n_head * s_max;
+    if (records * (T3B_HD + 2) > (long long) T3B_NOALLOC_PART_FLOATS || (long long) M * n_head > T3B_NOALLOC_CNT) {
+        set_err(nullptr, "t3b_op_attention_noalloc: %d rows x %d heads x %lld splits exceeds the static scratch "
+                "(%u partial records, %u counters)", M, n_head, s_max,
+                T3B_NOALLOC_PART_FLOATS / (T3B_HD + 2), T3B_NOALLOC_CNT);
+        return T3B_ERR_ARG;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { set_err(nullptr, "t3b_op_attention_noalloc: no device"); return T3B_ERR_CUDA; }
+    NoAllocScratch sc;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        auto it = g_noalloc.find(dev);
+        if (it == g_noalloc.end()) {
+            NoAllocScratch n;
+            cudaError_t e1 = cudaGetSymbolAddress((void **) &n.part, g_noalloc_part);
+            cudaError_t e2 = cudaGetSymbolAddress((void **) &n.cnt, g_noalloc_cnt);
+            if (e1 != cudaSuccess || e2 != cudaSuccess) {
+                set_err(nullptr, "t3b_op_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                        cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+                return T3B_ERR_CUDA;
+            }
+            it = g_noalloc.emplace(dev, n).first;
+        }
+        sc = it->second;
+    }
+    cudaStream_t st = (cudaStream_t) cuda_stream;
+    // the counters must start at zero; the arrays keep the previous call's
+    // contents, so clear the ones this call uses (and the error word)
+    cudaError_t e = cudaMemsetAsync(sc.cnt, 0, sizeof(unsigned) * (size_t) M * n_head, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(sc.cnt + T3B_NOALLOC_CNT, 0, sizeof(unsigned), st);
+    if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention_noalloc: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
+    AttnArgs a{};
+    a.q = q_dev; a.ldq = n_head * T3B_HD;
+    a.kv = (const __half *) k_dev; a.row_elems = (size_t) n_head * max_ctx * T3B_HD; a.layer_off = 0;
+    a.v_off = (size_t) ((const __half *) v_dev - (const __half *) k_dev);
+    a.row_of = nullptr; a.len = len_dev; a.len_add = 0; a.max_ctx = max_ctx; a.n_head = n_head;
+    a.out = out_dev; a.ldo = n_head * T3B_HD; a.part = sc.part; a.cnt = sc.cnt; a.s_max = (int) s_max;
+    a.err = sc.cnt + T3B_NOALLOC_CNT;
+    attn_decode_kernel<<<dim3(n_head, M, (unsigned) s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention_noalloc: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
+    return T3B_OK;
+}

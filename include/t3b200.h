@@ -209,6 +209,24 @@ int t3b_op_sample_philox(const float * cond_dev, const float * uncond_dev, int r
                          const uint64_t * counter_dev, int32_t * tokens_out_dev,
                          void * cuda_stream);
 
+/* Allocation-free variant of t3b_op_attention (this entry point has no
+ * counterpart in chatterbox.cpp).  It is for callers that may not allocate
+ * device memory on their decode path: hosts that hand every byte of device
+ * memory to their own pool allocator, and real-time callers that cannot
+ * afford cudaMalloc, which may take allocator locks or synchronise the
+ * device.  The split partials and completion counters live in a fixed
+ * static device array that every GPU loading libt3b200.so keeps until the
+ * process exits (4 MiB of partials + 16 KiB of counters).  Limits: M x n_head
+ * x ceil(max_ctx / 128) <= 15887 partial records and M x n_head <= 4096;
+ * larger calls return T3B_ERR_ARG without launching.  The first call on a
+ * device resolves the array's address (cudaGetSymbolAddress) and should be
+ * made before any stream capture.  All calls share the array: each call
+ * clears the counters it uses on `cuda_stream` first, and calls whose
+ * kernels overlap on the GPU (two streams, or two threads) race on it. */
+int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev, const void * v_dev, int M,
+                             int n_head, int max_ctx, const int32_t * len_dev, float * out_dev,
+                             void * cuda_stream);
+
 /* Host expf fix-up table size (entries where the device exp needed a
  * correction to equal the host libm's expf). */
 int t3b_expf_fixup_count(void);
