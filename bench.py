@@ -234,6 +234,7 @@ def main():
     m.alloc_streams(1, 150 + max(K, W) + 8)
     params = pkg.SampleParams.make(**PARAMS)
 
+    clk = Clocks(local).__enter__()   # sampling starts before the warm-up (nvidia-smi needs ~0.2 s)
     # warm-up: a W-step utterance
     m.prefill(0, text)
     m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
@@ -245,10 +246,11 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local) as clk:
-        toks = m.decode([params], K, ignore_stop=True)[0]
-        dev_ms = m.last_device_ms()
+    toks = m.decode([params], K, ignore_stop=True)[0]
+    dev_ms = m.last_device_ms()
     torch.cuda.synchronize()
+    time.sleep(0.25)
+    clk.__exit__()
     if dist:
         dist.barrier()
     t_dev = torch.tensor([dev_ms], dtype=torch.float64, device="cuda")
@@ -294,13 +296,15 @@ def main():
             "data": "synthetic (random-init T3 Q4_0 weights, seeded prompt)",
             "config": config_block(args),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "decode step (graph of embed + 24 layers + head + sampler)",
+                         "frac": achieved / peak, "traffic": measured_traffic(),
+                         "peak_kind": peak_kind,
+                         "kernel": "t3_decode_megakernel<Q4_0> (persistent; one launch decodes K steps); "
+                                   "achieved/traffic per decode step",
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
             "sampler": sampler_microbench(pkg, torch, peak),
             "e2e": e2e, "clocks": clk.summary(),
-            "gpu_launches": K * (1 + hp["n_layer"] * 9 + 2 + 2) + 1,
+            "gpu_launches": 2,   # first-token sampler + one t3_decode_megakernel launch
             "tokens_head": [int(x) for x in toks[:8]]}
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_reference(args, hp, t, text, "port")
@@ -352,6 +356,18 @@ def sampler_microbench(pkg, torch, peak, reps=200):
     return {"config": "configs[1]: 128x6563, CFG 0.5, min_p 0.05, top_k 1000, top_p 0.95, penalty 1.2, temp 0.8, "
                       "Philox", "us_per_step": med, "us_min": us[0], "target_us": 10.0,
             "achieved_gbs": byts / (med * 1e-6) / 1e9, "peak": peak}
+
+
+def measured_traffic():
+    """DRAM bytes per decode step of the megakernel from the committed ncu
+    summary (profiles/t3_decode_megakernel_q4_0.md), or None."""
+    p = os.path.join(ROOT, "profiles", "t3_decode_megakernel_q4_0.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_step:"):
+            return float(line.split(":")[1])
+    return None
 
 
 def gemv_roofline(pkg, torch, peak):

@@ -64,6 +64,8 @@ struct MegaArgs {
     unsigned * err; int * abort_flag; const int * cancel;
     int * steps_done;
     float * trace;                 // nullable: [n_steps + 1][V] logits, row 0 = prefill
+    float * logits_out;            // nullable: logits of the last step (eval_step)
+    int sample;                    // 0: stop after the head (eval_step without sampling)
     unsigned long long * tl;       // nullable: [G][MK_TL] globaltimer stamps of step tl_step
     int tl_step;
     SampArgs samp;
@@ -404,6 +406,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
         const int n = r0 + tid;
         const float v = __fadd_rn(rowsum[tid], hb);
         if (tr) tr[n] = v;
+        if (a.logits_out) a.logits_out[n] = v;
         lg[n] = v;
     }
     mk_release(a.cnt + MK_C_LOG * MK_C_STRIDE);
@@ -685,6 +688,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             if (!ok) return;
         }
         MK_STAMP(481);
+        if (!a.sample) return;   // eval_step: logits only
         // ---------------- sampler (CTA 0) and token broadcast -------------------
         if (cta == 0) {
             // host cancel flag (mapped memory): read before the wait so the

@@ -785,7 +785,7 @@ int mega_prepare(t3b_ctx * ctx) {
 // One cooperative launch decoding max_steps steps of stream `slot` (row
 // slot).  The first token is already in step_tok (sampled from the prefill
 // logits).  Returns the number of steps run in *steps.
-int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop, int * steps) {
+int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop, int * steps, float * logits_out = nullptr) {
     MegaState & m = ctx->mega;
     cudaStream_t st = ctx->st;
     const int H = ctx->hp.n_head;
@@ -801,7 +801,9 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     a.p0 = p0; a.n_steps = max_steps; a.ignore_stop = ignore_stop; a.stop_token = ctx->hp.stop_speech_token;
     a.buf = m.buf; a.cnt = m.cnt; a.err = ctx->err_word; a.abort_flag = m.abort_flag; a.cancel = m.cancel_dev;
     a.steps_done = m.steps_done;
-    a.trace = ctx->trace_cap >= max_steps ? ctx->trace : nullptr;
+    a.trace = (logits_out == nullptr && ctx->trace_cap >= max_steps) ? ctx->trace : nullptr;
+    a.logits_out = logits_out;
+    a.sample = logits_out == nullptr;
     a.samp = sampler_args(ctx, false);
     a.samp.done = nullptr;
     CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_C_N * MK_C_STRIDE, st));
@@ -823,7 +825,7 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
                     : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0>
                                     : (const void *) t3_decode_megakernel<T3B_F16>;
     CK(cudaLaunchCooperativeKernel(fn, dim3(m.grid), dim3(MK_THREADS), args, m.smem, st));
-    CK(cudaMemcpyAsync(steps, m.steps_done, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (steps) CK(cudaMemcpyAsync(steps, m.steps_done, sizeof(int), cudaMemcpyDeviceToHost, st));
     if (tl) {
         std::vector<unsigned long long> h((size_t) m.grid * MK_TL);
         CK(cudaMemcpyAsync(h.data(), tl, sizeof(unsigned long long) * h.size(), cudaMemcpyDeviceToHost, st));
@@ -867,12 +869,29 @@ int t3b_step(t3b_ctx * ctx, int n, const int32_t * streams, const int32_t * toke
         if (p < 0 || p + 1 > ctx->max_ctx) { set_err(&ctx->err, "t3b_step: position %d outside context %d", p, ctx->max_ctx); return T3B_ERR_ARG; }
         for (int j = 0; j < ctx->rps; ++j) ctx->pos_host[slots[i] * ctx->rps + j] = p;
     }
+    cudaStream_t st = ctx->st;
+    const int p_first = ctx->pos_host[slots[0] * ctx->rps];
+    if (mega_eligible(ctx, n, p_first + 1) && mega_prepare(ctx) == T3B_OK) {
+        // eval_step of one stream: one persistent-kernel step, logits only
+        rc = upload_maps(ctx, slots);
+        if (rc != T3B_OK) return rc;
+        CK(cudaMemcpyAsync(ctx->step_tok + slots[0], tokens, sizeof(int), cudaMemcpyHostToDevice, st));
+        float * dst = ctx->logits + (size_t) slots[0] * V;
+        CK(cudaEventRecord(ctx->ev0, st));
+        rc = mega_decode(ctx, slots[0], p_first, 1, 1, nullptr, dst);
+        if (rc != T3B_OK) return rc;
+        CK(cudaEventRecord(ctx->ev1, st));
+        if (logits_out) CK(cudaMemcpyAsync(logits_out, dst, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1);
+        ctx->pos_host[slots[0]] = p_first + 1;
+        return check_dev_err(ctx);
+    }
     StepGraph * g = nullptr;
     rc = ensure_graph(ctx, n, false, &g);
     if (rc != T3B_OK) return rc;
     rc = upload_maps(ctx, slots);
     if (rc != T3B_OK) return rc;
-    cudaStream_t st = ctx->st;
     // step_tok is indexed by slot, pos by activation row
     std::vector<int> tok(ctx->S, 0);
     CK(cudaMemcpyAsync(tok.data(), ctx->step_tok, sizeof(int) * ctx->S, cudaMemcpyDeviceToHost, st));
