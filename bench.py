@@ -200,15 +200,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["sampler", "gemv"], default=None,
-                    help="run one kernel micro-benchmark alone (for ncu captures)")
+    ap.add_argument("--only", choices=["sampler", "gemv", "timeline"], default=None,
+                    help="run one kernel micro-benchmark alone (ncu captures), or the megakernel phase timeline")
     args = ap.parse_args()
     if args.only:
         import torch
         import __graft_entry__ as ge
         pkg = ge.load_package()
         peak, _ = peaks()
-        r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
+        if args.only == "timeline":
+            r = phase_timeline(pkg)
+        else:
+            r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
         print(json.dumps(r), flush=True)
         return 0
     if args.impl == "reference":
@@ -356,6 +359,51 @@ def sampler_microbench(pkg, torch, peak, reps=200):
     return {"config": "configs[1]: 128x6563, CFG 0.5, min_p 0.05, top_k 1000, top_p 0.95, penalty 1.2, temp 0.8, "
                       "Philox", "us_per_step": med, "us_min": us[0], "target_us": 10.0,
             "achieved_gbs": byts / (med * 1e-6) / 1e9, "peak": peak}
+
+
+def phase_timeline(pkg, step=5):
+    """Per-phase device timestamps (globaltimer) of one decode step of the
+    persistent kernel, every CTA, via the library's T3B_MK_TIMELINE hook.
+    Returns medians over CTAs (us from the step's first stamp) for layers 1
+    and 12, the head, the sampler and its stages."""
+    import tempfile
+    tl_path = os.path.join(tempfile.mkdtemp(), "tl.bin")
+    os.environ["T3B_MK_TIMELINE"] = tl_path
+    os.environ["T3B_MK_TIMELINE_STEP"] = str(step)
+    try:
+        hp, t = make_model(pkg)
+        m = pkg.T3Model(hp, t)
+        m.alloc_streams(1, 512)
+        m.prefill(0, np.random.default_rng(0).integers(0, 50257, PROMPT_TEXT).astype(np.int32))
+        m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
+        m.decode([pkg.SampleParams.make(**PARAMS)], 16, ignore_stop=True)
+        ms = m.last_device_ms()
+        m.close()
+    finally:
+        os.environ.pop("T3B_MK_TIMELINE", None)
+        os.environ.pop("T3B_MK_TIMELINE_STEP", None)
+    tl = np.fromfile(tl_path, dtype=np.uint64).reshape(-1, 512).astype(np.int64)
+    t0 = tl[tl > 0].min()
+    rel = np.where(tl > 0, tl - t0, -1)
+
+    def med(i):
+        c = rel[:, i]
+        c = c[c >= 0]
+        return round(float(np.median(c)) / 1000.0, 2) if c.size else None
+
+    names = {0: "P1 start", 1: "P1 x ready", 13: "P1 LN done", 14: "P1 quant done", 15: "P1 dot done",
+             2: "P1 released", 3: "P2 qkv ready", 4: "P2 released", 5: "P3 att ready", 6: "P4 xm ready",
+             7: "P5 h ready", 10: "P5 quant done", 11: "P5 dot done", 8: "P5 released"}
+    out = {"decode_16_steps_ms": ms, "step": step}
+    for l in (1, 12):
+        out[f"layer{l}"] = {nm: med(l * 20 + i) for i, nm in names.items()}
+    out["head"] = {"start": med(480), "released": med(481), "sampler logits ready": med(482),
+                   "sampled": med(483), "token seen": med(484)}
+    st = tl[0, 490:502]
+    stages = ["start", "min-p", "top-k", "top-p gather", "sort", "exp+psum+cut", "penalty", "final exp",
+              "final psum", "draw", "chains", "end"]
+    out["sampler_stages_us"] = {stages[i]: round((st[i] - st[0]) / 1000.0, 2) for i in range(12) if st[i] > 0}
+    return out
 
 
 def measured_traffic():
