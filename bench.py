@@ -256,11 +256,8 @@ def main():
     clk.__exit__()
     if dist:
         dist.barrier()
-    t_dev = torch.tensor([dev_ms], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t_dev, op=dist.ReduceOp.MAX)
-    ms = float(t_dev.item())
-    value = ws * K / (ms / 1000.0)
+    # every rank decoded K tokens of its own utterance; job time = slowest rank
+    value, ms = pkg.sharding.job_throughput(dist, dev_ms, K, ws)
     ms_per_step = ms / K
 
     # e2e through the per-step drop-in API (host copies every step)
@@ -278,10 +275,8 @@ def main():
         host_logits = m.step([tok])                         # eval_step: token H2D, logits D2H
         tok = int(m.sample([params], logits=host_logits)[0])  # sample_next_token_ex on host logits
     e2e_s = time.perf_counter() - t0
-    t_e2e = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
-    e2e = {"value": ws * e2e_steps / float(t_e2e.item()), "unit": UNIT,
+    e2e_value, _ = pkg.sharding.job_throughput(dist, e2e_s * 1000.0, e2e_steps, ws)
+    e2e = {"value": e2e_value, "unit": UNIT,
            "h2d_bytes_per_step": 4 + 4 + V * 4 + 24 + 4, "d2h_bytes_per_step": V * 4 + 4,
            "steps": e2e_steps, "path": "t3b_step(host token) -> logits D2H -> t3b_sample(host logits) -> token D2H"}
 

@@ -14,7 +14,7 @@ import os
 
 import numpy as np
 
-from . import t3_gguf
+from . import sharding, t3_gguf
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libt3b200.so")

@@ -44,7 +44,29 @@ def build(force=False, verbose_ptxas=False):
         if verbose_ptxas:
             cmd.insert(1, "-Xptxas=-v")
         _run(cmd)
+    build_dropin(force)
     return LIB
+
+
+DROPIN_LIB = os.path.join(HERE, "libt3b200_dropin.so")
+DROPIN_TEST = os.path.join(BUILD, "t3_dropin_main")
+
+
+def build_dropin(force=False):
+    """The C++ mirror of chatterbox.cpp's T3 API (csrc/t3_dropin.cpp) as
+    libt3b200_dropin.so, and the run_t3-style test program linked to it."""
+    inc = os.path.join(HERE, "..", "include")
+    src = os.path.join(CSRC, "t3_dropin.cpp")
+    deps = [src, os.path.join(inc, "t3b200_dropin.hpp"), os.path.join(inc, "t3b200.h"), LIB]
+    gxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
+    if force or not _newer(DROPIN_LIB, deps):
+        _run([gxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-I", inc, src, "-o", DROPIN_LIB,
+              "-L", HERE, "-lt3b200", "-Wl,-rpath,$ORIGIN"])
+    main = os.path.join(HERE, "..", "tests", "cpp", "t3_dropin_main.cpp")
+    if force or not _newer(DROPIN_TEST, [main, DROPIN_LIB]):
+        _run([gxx, "-O2", "-std=c++17", "-I", inc, main, "-o", DROPIN_TEST, "-L", HERE, "-lt3b200_dropin",
+              "-lt3b200", "-Wl,-rpath," + HERE])
+    return DROPIN_LIB
 
 
 if __name__ == "__main__":
