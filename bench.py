@@ -394,10 +394,10 @@ def phase_timeline(pkg, step=5):
         out[f"layer{l}"] = {nm: med(l * 20 + i) for i, nm in names.items()}
     out["head"] = {"start": med(480), "released": med(481), "sampler logits ready": med(482),
                    "sampled": med(483), "token seen": med(484)}
-    st = tl[0, 490:502]
-    stages = ["start", "min-p", "top-k", "top-p gather", "sort", "exp+psum+cut", "penalty", "final exp",
-              "final psum", "draw", "chains", "end"]
-    out["sampler_stages_us"] = {stages[i]: round((st[i] - st[0]) / 1000.0, 2) for i in range(12) if st[i] > 0}
+    st = tl[0, 490:506]
+    stages = ["start", "loaded", "min-p", "top-k", "top-p gathered", "sorted", "top-p exp", "top-p psum",
+              "top-p cut", "penalty", "compacted", "final exp", "final psum", "rng", "dsum", "end"]
+    out["sampler_stages_us"] = {stages[i]: round((st[i] - st[0]) / 1000.0, 2) for i in range(16) if st[i] > 0}
     return out
 
 

@@ -419,10 +419,13 @@ __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a)
 // ---------------------------------------------------------------------------
 // Fused sampler
 // ---------------------------------------------------------------------------
-struct ExpFix { const unsigned long long * tab; int bits; int max_probe; };
+struct ExpFix { const unsigned long long * tab; int bits; int n; };   // n = fix-up entries (0: none)
+
+// 2^(i/32) words of t3_expf_core (device copy)
+__device__ const unsigned long long g_t3_exp2_tab[32] = T3_EXP2_TAB_INIT;
 
 // exp with the host libm's rounding: t3_expf_core + fix-up table lookup
-// (two 32-byte buckets, read together).
+// (two 32-byte buckets, read together) when the build found differences.
 __device__ __forceinline__ float t3_expf_fix(float x, float y, uint4 a0, uint4 a1, uint4 b0, uint4 b1) {
     const uint32_t key = __float_as_uint(x);
     const uint32_t w[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
@@ -432,9 +435,9 @@ __device__ __forceinline__ float t3_expf_fix(float x, float y, uint4 a0, uint4 a
         if ((w[2 * k] | w[2 * k + 1]) != 0u && w[2 * k + 1] == key) y = __uint_as_float(w[2 * k]);
     return y;
 }
-__device__ __forceinline__ float t3_expf_dev(float x, const ExpFix & f) {
-    const float y = t3_expf_core(x);
-    if (!(x >= -104.0f && x <= 0.0f)) return y;
+__device__ __forceinline__ float t3_expf_dev(float x, const ExpFix & f, const unsigned long long * e2) {
+    const float y = t3_expf_core(x, e2);
+    if (f.n == 0 || !(x >= -104.0f && x <= 0.0f)) return y;
     const uint32_t key = __float_as_uint(x);
     const uint4 * b1 = (const uint4 *) (f.tab + (size_t) t3_expf_hash1(key, f.bits) * T3_EXPF_SLOTS);
     const uint4 * b2 = (const uint4 *) (f.tab + (size_t) t3_expf_hash2(key, f.bits) * T3_EXPF_SLOTS);
@@ -572,6 +575,7 @@ struct SampArgs {
     int * done; int stop_token;                       // nullable
     ExpFix fx;
     unsigned long long * tl;                          // nullable: stage stamps of row 0 (debug)
+    int mt_resident;                                  // mt19937 words already in shared memory (persistent kernel)
 };
 
 #define T3B_SAMPLER_THREADS 1024
@@ -583,7 +587,12 @@ struct SampArgs {
 // read is issued before any result is needed, so a batch costs one memory
 // round trip.
 template <int N>
-__device__ __forceinline__ void t3_expf_batch(float (&x)[N], const ExpFix & f) {
+__device__ __forceinline__ void t3_expf_batch(float (&x)[N], const ExpFix & f, const unsigned long long * e2) {
+    if (f.n == 0) {
+#pragma unroll
+        for (int n = 0; n < N; ++n) x[n] = t3_expf_core(x[n], e2);
+        return;
+    }
     uint4 a0[N], a1[N], b0[N], b1[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) {
@@ -597,7 +606,7 @@ __device__ __forceinline__ void t3_expf_batch(float (&x)[N], const ExpFix & f) {
         }
     }
 #pragma unroll
-    for (int n = 0; n < N; ++n) x[n] = t3_expf_fix(x[n], t3_expf_core(x[n]), a0[n], a1[n], b0[n], b1[n]);
+    for (int n = 0; n < N; ++n) x[n] = t3_expf_fix(x[n], t3_expf_core(x[n], e2), a0[n], a1[n], b0[n], b1[n]);
 }
 
 // Block-wide exclusive scan of doubles (blockDim.x multiple of 32, <= 1024).
@@ -689,10 +698,12 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     __shared__ int shi[8];
     __shared__ float shf[4];
     __shared__ uint32_t mtx[625];
+    __shared__ unsigned long long e2tab[32];   // t3_expf_core's table (first use is after several barriers)
 
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31;
     const int slot = a.slot_of ? a.slot_of[r] : r;
     if (a.done && a.done[slot]) return -1;
+    if (tid < 32) e2tab[tid] = g_t3_exp2_tab[tid];
     unsigned long long * tls = (a.tl && r == 0) ? a.tl : nullptr;
 #define SAMP_STAMP(i) do { if (tls && tid == 0) { unsigned long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); tls[i] = t_; } } while (0)
     SAMP_STAMP(0);
@@ -703,59 +714,91 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
     const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
 
-    // (0) CFG mix, (1) temperature  (main.cpp:735-738)
+    // (0) CFG mix, (1) temperature  (main.cpp:735-738).  Each thread issues
+    // its loads four at a time; the max and the count of finite scores are
+    // gathered on the way for min-p and the top-k skip.
     const bool cfg = unc != nullptr && P.cfg_weight != 0.0f;
     const bool use_t = P.temp > 0.0f && P.temp != 1.0f;
     const float inv_t = use_t ? __fdiv_rn(1.0f, P.temp) : 1.0f;
-    for (int i = tid; i < V; i += nth) {
-        float v = cond[i];
-        if (cfg) v = __fadd_rn(v, __fmul_rn(P.cfg_weight, __fsub_rn(v, unc[i])));
-        if (use_t) v = __fmul_rn(v, inv_t);
-        s[i] = v;
-    }
-    __syncthreads();
-
-    SAMP_STAMP(1);
-    // (1b) min-p: drop exp(s - max) < min_p
-    if (P.min_p > 0.0f) {
-        float lm = -INFINITY;
-        for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
-        const float mx = block_max(lm, redf);
-        for (int i0 = 0; i0 < V; i0 += 4 * nth) {
-            float x[4];
+    float lmx = -INFINITY;
+    int lfin = 0;
+    for (int i0 = 0; i0 < V; i0 += 4 * nth) {
+        float cv[4], uv[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = i0 + u * nth + tid;
-                x[u] = (i < V && s[i] != -INFINITY) ? __fsub_rn(s[i], mx) : -INFINITY;
-            }
-            t3_expf_batch<4>(x, a.fx);
+        for (int q = 0; q < 4; ++q) {
+            const int i = i0 + q * nth + tid;
+            cv[q] = i < V ? cond[i] : 0.0f;
+            uv[q] = (cfg && i < V) ? unc[i] : 0.0f;
+        }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = i0 + u * nth + tid;
-                if (i < V && s[i] != -INFINITY && x[u] < P.min_p) s[i] = -INFINITY;
+        for (int q = 0; q < 4; ++q) {
+            const int i = i0 + q * nth + tid;
+            if (i < V) {
+                float v = cv[q];
+                if (cfg) v = __fadd_rn(v, __fmul_rn(P.cfg_weight, __fsub_rn(v, uv[q])));
+                if (use_t) v = __fmul_rn(v, inv_t);
+                s[i] = v;
+                if (v != -INFINITY) { lmx = fmaxf(lmx, v); ++lfin; }
             }
         }
-        __syncthreads();
+    }
+    int nfin = block_sum_i(lfin, redi);
+    const float smax = block_max(lmx, redf);
+
+    SAMP_STAMP(1);
+    // (1b) min-p: drop exp(s - max) < min_p.  The host expf is within one ulp
+    // of exp, so for results in the normal range exp(d) < min_p is decided by
+    // d against log(min_p) except within 1e-5 of it (a relative gap of 1e-5 in
+    // exp, far above one ulp); only that window evaluates expf exactly.
+    if (P.min_p > 0.0f && nfin > 0) {
+        const bool fast = P.min_p >= 1e-30f;
+        const double lg = log((double) P.min_p);
+        const double lo = lg - 1e-5, hi = lg + 1e-5;
+        int kept = 0;
+        for (int i = tid; i < V; i += nth) {
+            const float v = s[i];
+            if (v == -INFINITY) continue;
+            const float d = __fsub_rn(v, smax);
+            bool drop;
+            if (fast && (double) d <= lo) drop = true;
+            else if (fast && (double) d >= hi) drop = false;
+            else drop = t3_expf_dev(d, a.fx, e2tab) < P.min_p;
+            if (drop) s[i] = -INFINITY;
+            else ++kept;
+        }
+        nfin = block_sum_i(kept, redi);
     }
 
     SAMP_STAMP(2);
     // (2) top-k (main.cpp:740-748): radix-select the value at descending
-    // rank k, then keep s > thr (thr nudged by 1e-10f if fewer than k).
-    if (P.top_k > 0 && P.top_k < V) {
+    // rank k, then keep s > thr (thr nudged by 1e-10f if fewer than k).  With
+    // k or fewer finite scores the reference's threshold is -inf and nothing
+    // changes, so the stage is skipped.
+    bool topk_pending = false;   // drop of s <= thr_k not yet applied
+    float thr_k = -INFINITY;
+    if (P.top_k > 0 && P.top_k < V && nfin > P.top_k) {
         // digits of 11, 11 and 10 bits: the first already spreads the scores
         // over their exponent and leading mantissa bits, so few keys share a
         // bin and plain shared-memory atomics stay cheap
-        int * hist = (int *) keys;     // 2048 bins, free until the top-p gather
+        // The first pass runs over all scores; the keys of the bin holding rank
+        // k are then gathered, and the other two passes run over that list only.
+        int * hist = (int *) keys;                    // 2048 bins, free until the top-p gather
+        uint32_t * cand = (uint32_t *) keys + 2048;   // keys of the selected first-digit bin
         uint32_t prefix = 0u, maskb = 0u;
         int rank = P.top_k;
+        int nc = 0;
         for (int pass = 0; pass < 3; ++pass) {
             const int sh = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
             const int nb = pass == 2 ? 1024 : 2048;
             for (int i = tid; i < nb; i += nth) hist[i] = 0;
             __syncthreads();
-            for (int i = tid; i < V; i += nth) {
-                const uint32_t k = desc_key(s[i]);
-                if ((k & maskb) == prefix) atomicAdd(&hist[(k >> sh) & (uint32_t) (nb - 1)], 1);
+            if (pass == 0) {
+                for (int i = tid; i < V; i += nth) atomicAdd(&hist[desc_key(s[i]) >> 21], 1);
+            } else {
+                for (int i = tid; i < nc; i += nth) {
+                    const uint32_t k = cand[i];
+                    if ((k & maskb) == prefix) atomicAdd(&hist[(k >> sh) & (uint32_t) (nb - 1)], 1);
+                }
             }
             __syncthreads();
             // block scan over the bins: thread t owns bins [t*bpt, (t+1)*bpt)
@@ -795,15 +838,37 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             rank -= shi[1];
             prefix |= ((uint32_t) shi[0]) << sh;
             maskb |= ((uint32_t) (nb - 1)) << sh;
+            if (pass == 0) {
+                if (tid == 0) shi[3] = 0;
+                __syncthreads();
+                const uint32_t bsel = (uint32_t) shi[0];
+                for (int i0 = 0; i0 < V; i0 += nth) {      // warp-aggregated gather (order irrelevant)
+                    const int i = i0 + tid;
+                    const uint32_t k = i < V ? desc_key(s[i]) : 0u;
+                    const bool take = i < V && (k >> 21) == bsel;
+                    const unsigned bal = __ballot_sync(0xffffffffu, take);
+                    int base = 0;
+                    if (lane == 0 && bal) base = atomicAdd(&shi[3], __popc(bal));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (take) cand[base + __popc(bal & ((1u << lane) - 1u))] = k;
+                }
+                __syncthreads();
+                nc = shi[3];
+            }
             __syncthreads();
         }
         float thr = desc_key_inv(prefix);
-        int above = 0;
-        for (int i = tid; i < V; i += nth) above += s[i] > thr ? 1 : 0;
-        above = block_sum_i(above, redi);
+        int above;
+        if (thr != 0.0f) {
+            above = P.top_k - rank;   // keys before the selected one = scores strictly above thr
+        } else {                      // +0 and -0 have distinct keys but compare equal
+            int ab = 0;
+            for (int i = tid; i < V; i += nth) ab += s[i] > thr ? 1 : 0;
+            above = block_sum_i(ab, redi);
+        }
         if (above < P.top_k) thr = __fsub_rn(thr, 1e-10f);
-        for (int i = tid; i < V; i += nth) if (s[i] <= thr) s[i] = -INFINITY;
-        __syncthreads();
+        thr_k = thr;
+        topk_pending = true;
     }
 
     SAMP_STAMP(3);
@@ -812,23 +877,26 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     if (P.top_p < 1.0f) {
         if (tid == 0) shi[2] = 0;
         __syncthreads();
-        for (int i0 = 0; i0 < V; i0 += nth) {            // warp-aggregated gather
+        for (int i0 = 0; i0 < V; i0 += nth) {            // warp-aggregated gather (+ top-k drop)
             const int i = i0 + tid;
-            const bool keep = i < V && s[i] != -INFINITY;
+            float v = i < V ? s[i] : -INFINITY;
+            if (topk_pending && i < V && v <= thr_k) { s[i] = -INFINITY; v = -INFINITY; }
+            const bool keep = v != -INFINITY;
             const unsigned b = __ballot_sync(0xffffffffu, keep);
             int base = 0;
             if (lane == 0 && b) base = atomicAdd(&shi[2], __popc(b));
             base = __shfl_sync(0xffffffffu, base, 0);
-            if (keep) keys[base + __popc(b & ((1u << lane) - 1u))] = ((unsigned long long) desc_key(s[i]) << 32) | (unsigned) i;
+            if (keep) keys[base + __popc(b & ((1u << lane) - 1u))] = ((unsigned long long) desc_key(v) << 32) | (unsigned) i;
         }
+        topk_pending = false;
         __syncthreads();
         const int c = shi[2];
+        SAMP_STAMP(4);
         if (c > 0) {
             int n2 = 2;
             while (n2 < c) n2 <<= 1;
             for (int i = c + tid; i < n2; i += nth) keys[i] = ~0ull;
             __syncthreads();
-            SAMP_STAMP(4);
             // bitonic sort on compare-exchange pairs: pair p touches elements of
             // the 64-element segment p/32 whenever the stride j <= 32, so those
             // stages need only a warp barrier
@@ -854,7 +922,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                     const int j = j0 + u * nth + tid;
                     x[u] = j < c ? __fsub_rn(s[(int) (keys[j] & 0xffffffffu)], mx) : -INFINITY;
                 }
-                t3_expf_batch<4>(x, a.fx);
+                t3_expf_batch<4>(x, a.fx, e2tab);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int j = j0 + u * nth + tid;
@@ -862,8 +930,10 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 }
             }
             __syncthreads();
+            SAMP_STAMP(6);
             if (tid == 0) shf[0] = seq_sum_f32(e, c);
             __syncthreads();
+            SAMP_STAMP(7);
             const float psum = shf[0];
             for (int j = tid; j < c; j += nth) e[j] = __fdiv_rn(e[j], psum);
             __syncthreads();
@@ -882,8 +952,12 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             __syncthreads();
         }
     }
+    if (topk_pending) {
+        for (int i = tid; i < V; i += nth) if (s[i] <= thr_k) s[i] = -INFINITY;
+        __syncthreads();
+    }
 
-    SAMP_STAMP(6);
+    SAMP_STAMP(8);
     // (4) repetition penalty over distinct history ids (main.cpp:774-781)
     if (P.repeat_penalty != 1.0f && hl > 0) {
         for (int i = tid; i < (V + 31) / 32; i += nth) seen[i] = 0u;
@@ -901,33 +975,17 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         __syncthreads();
     }
 
-    SAMP_STAMP(7);
-    // (5) softmax over survivors in index order (main.cpp:783-793).  Entries
-    // that were dropped get p = 0, which adds nothing to any later sum, so
-    // they are equivalent to survivors whose exp underflowed.
-    float lm = -INFINITY;
-    for (int i = tid; i < V; i += nth) if (s[i] != -INFINITY) lm = fmaxf(lm, s[i]);
-    const float mx = block_max(lm, redf);
-    for (int i0 = 0; i0 < V; i0 += 4 * nth) {
-        float x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = i0 + u * nth + tid;
-            x[u] = (i < V && s[i] != -INFINITY) ? __fsub_rn(s[i], mx) : -INFINITY;
-        }
-        t3_expf_batch<4>(x, a.fx);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = i0 + u * nth + tid;
-            if (i < V) s[i] = x[u];       // exp(-inf) = 0 for dropped entries
-        }
-    }
-    __syncthreads();
-    // index-ordered compaction of the nonzero p: thread t owns [t*per, (t+1)*per)
+    SAMP_STAMP(9);
+    // (5) softmax over survivors in index order (main.cpp:783-793).  Dropped
+    // entries have p = 0 and add nothing to any later sum, so only the
+    // survivors are compacted (index order: thread t owns [t*per, (t+1)*per))
+    // and exponentiated; one whose exp underflows stays in the list with 0.
     const int per = (V + nth - 1) / nth;
     const int i0 = min(V, tid * per), i1 = min(V, i0 + per);
+    float lm = -INFINITY;
     int cnt = 0;
-    for (int i = i0; i < i1; ++i) cnt += s[i] != 0.0f ? 1 : 0;
+    for (int i = i0; i < i1; ++i) { const float v = s[i]; if (v != -INFINITY) { lm = fmaxf(lm, v); ++cnt; } }
+    const float mx = block_max(lm, redf);
     int incl = cnt;
     const int w = tid >> 5;
 #pragma unroll
@@ -952,14 +1010,30 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     __syncthreads();
     {
         int o = redi[w] + incl - cnt;
-        for (int i = i0; i < i1; ++i)
-            if (s[i] != 0.0f) { lst[o] = i; e[o] = s[i]; ++o; }
+        for (int i = i0; i < i1; ++i) { const float v = s[i]; if (v != -INFINITY) { lst[o] = i; e[o] = v; ++o; } }
     }
     __syncthreads();
     const int cf = shi[4];
-    SAMP_STAMP(8);
+    SAMP_STAMP(10);
+    for (int j0 = 0; j0 < cf; j0 += 4 * nth) {
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = j0 + u * nth + tid;
+            x[u] = j < cf ? __fsub_rn(e[j], mx) : -INFINITY;
+        }
+        t3_expf_batch<4>(x, a.fx, e2tab);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = j0 + u * nth + tid;
+            if (j < cf) e[j] = x[u];
+        }
+    }
+    __syncthreads();
+    SAMP_STAMP(11);
     if (tid == 0) shf[1] = seq_sum_f32(e, cf);
     __syncthreads();
+    SAMP_STAMP(12);
     const float psum = shf[1];
     int tok = 0;
     if (psum != 0.0f) {
@@ -989,21 +1063,23 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             tok = shi[5];
         } else {
             // (7) discrete_distribution draw
-            SAMP_STAMP(9);
             const int mode = a.rng_mode ? a.rng_mode[slot] : T3B_RNG_PHILOX;
             uint32_t x1, x2;
             if (mode == T3B_RNG_MT19937) {
                 uint32_t * st = a.mt + (size_t) slot * 625;
-                for (int i = tid; i < 625; i += nth) mtx[i] = st[i];
-                __syncthreads();
+                if (!a.mt_resident) {        // else mtx still holds this slot's state
+                    for (int i = tid; i < 625; i += nth) mtx[i] = st[i];
+                    __syncthreads();
+                }
                 int idx = (int) mtx[624];
                 bool tw = false;
                 if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
                 x1 = mt_temper(mtx[idx]); ++idx;
                 if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
                 x2 = mt_temper(mtx[idx]); ++idx;
+                __syncthreads();          // every thread has read the index word
                 if (tw) for (int i = tid; i < 624; i += nth) st[i] = mtx[i];
-                if (tid == 0) st[624] = (uint32_t) idx;
+                if (tid == 0) { st[624] = (uint32_t) idx; mtx[624] = (uint32_t) idx; }
             } else {
                 const unsigned long long sd = a.ph_seed[slot];
                 const unsigned long long ct = a.ph_ctr[slot];
@@ -1013,21 +1089,20 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 __syncthreads();
                 if (tid == 0) a.ph_ctr[slot] = ct + 1ull;
             }
-            SAMP_STAMP(10);
+            SAMP_STAMP(13);
             double sum = (double) x1;
             sum += (double) x2 * 4294967296.0;
             double u = sum / 18446744073709551616.0;
             if (u >= 1.0) u = nextafter(1.0, 0.0);
             // dsum = sequential double sum of the p (std::accumulate).  When
-            // every p >= 2^-29 all partial sums (< 2) are exact in double, so
-            // any order gives the same value.
+            // every nonzero p >= 2^-29 all partial sums (< 2) are exact in
+            // double, so any order gives the same value.
             float pmin = INFINITY;
-            for (int j = tid; j < cf; j += nth) pmin = fminf(pmin, e[j]);
+            double ls = 0.0;
+            for (int j = tid; j < cf; j += nth) { const float pj = e[j]; if (pj > 0.0f) pmin = fminf(pmin, pj); ls += (double) pj; }
             pmin = -block_max(-pmin, redf);
             double dsum;
             if (pmin >= 0x1p-29f) {
-                double ls = 0.0;
-                for (int j = tid; j < cf; j += nth) ls += (double) e[j];
                 double tot;
                 block_excl_scan_d(ls, redd, &tot);
                 dsum = tot;
@@ -1037,6 +1112,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 dsum = redd[32];
                 __syncthreads();
             }
+            SAMP_STAMP(14);
             // lower_bound(cp, u) with cp_j = cp_{j-1} + p_j / dsum and the last
             // entry (index V-1) forced to 1
             int pick;
@@ -1064,7 +1140,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             tok = pick;
         }
     }
-    SAMP_STAMP(11);
+    SAMP_STAMP(15);
 #undef SAMP_STAMP
     if (tid == 0) {
         if (a.tok_out) a.tok_out[r] = tok;
@@ -1089,7 +1165,7 @@ __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArg
 // exp test hook
 __global__ void expf_test_kernel(const float * in, float * out, int n, ExpFix fx) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = t3_expf_dev(in[i], fx);
+    if (i < n) out[i] = t3_expf_dev(in[i], fx, g_t3_exp2_tab);
 }
 
 // Advance per-row positions after a decode step (graph-captured loops).

@@ -708,6 +708,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             SampArgs sa = a.samp;
             sa.cond = lg; sa.cond_stride = 0; sa.uncond = nullptr;
             sa.tl = (a.tl && step == a.tl_step) ? a.tl + 490 : nullptr;
+            sa.mt_resident = step > 0;   // this CTA's shared copy of the mt19937 words is current
             MK_STAMP(482);
             const int t = sample_row_block(sa, 0, smem);
             MK_STAMP(483);

@@ -81,7 +81,7 @@ int fix_table(int device, ExpFix * out, std::string * ERRP) {
     }
     out->tab = it->second.dev;
     out->bits = it->second.bits;
-    out->max_probe = 0;
+    out->n = (int) t3_expf_fixup_n;
     return T3B_OK;
 }
 

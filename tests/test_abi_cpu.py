@@ -38,10 +38,12 @@ def test_row_bytes(pkg):
         assert L.t3b_op_row_bytes(ty, 4096) % 16 == 0
 
 
-def test_expf_fixup_table_present(pkg):
+def test_expf_fixup_list_small(pkg):
+    # t3_expf_core restates glibc's expf (FMA build), so the build-time scan of
+    # every float in [-104, 0] finds no or almost no arguments where the host
+    # libm differs; those few would be served from the device fix-up table.
     n = pkg.lib().t3b_expf_fixup_count()
-    # glibc expf is not correctly rounded in ~1e-4 of the [-104, 0] floats
-    assert 10_000 < n < 1_000_000
+    assert 0 <= n < 1000
 
 
 @pytest.mark.skipif(gpu_available(), reason="checks the no-device error path")
