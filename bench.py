@@ -200,7 +200,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["sampler", "gemv", "timeline"], default=None,
+    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched"], default=None,
                     help="run one kernel micro-benchmark alone (ncu captures), or the megakernel phase timeline")
     args = ap.parse_args()
     if args.only:
@@ -210,6 +210,9 @@ def main():
         peak, _ = peaks()
         if args.only == "timeline":
             r = phase_timeline(pkg)
+        elif args.only == "batched":
+            import torch
+            r = batched_cfg(pkg, torch, peak)
         else:
             r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
         print(json.dumps(r), flush=True)
@@ -354,6 +357,45 @@ def sampler_microbench(pkg, torch, peak, reps=200):
     return {"config": "configs[1]: 128x6563, CFG 0.5, min_p 0.05, top_k 1000, top_p 0.95, penalty 1.2, temp 0.8, "
                       "Philox", "us_per_step": med, "us_min": us[0], "target_us": 10.0,
             "achieved_gbs": byts / (med * 1e-6) / 1e9, "peak": peak}
+
+
+def batched_cfg(pkg, torch, peak, steps=256, streams=64, seed=3):
+    """BASELINE configs[3] on one GPU: 64 utterances with CFG (128 rows),
+    random-init Q8_0 weights, prompts of U[100, 400] positions, `steps`
+    decode steps of every stream (stop ignored) through t3b_decode (graph
+    path: batched GEMVs, split-K attention, one sampler CTA per stream).
+    Device time of the decode loop (library CUDA events); unit = one speech
+    token per stream (a CFG pair counts once)."""
+    hp = dict(pkg.t3_gguf.T3_TURBO)
+    hp, t = pkg.t3_gguf.random_t3(hp, quant="q8_0", seed=seed)
+    rng = np.random.default_rng(seed)
+    p_target = rng.integers(100, 401, streams)
+    warm = 4
+    m = pkg.T3Model(hp, t)
+    m.alloc_streams(streams, int(p_target.max()) + warm + steps + 8, cfg=True)
+    lens = []
+    for s in range(streams):
+        n_text = int(p_target[s]) - (hp["cond_prompt_len"] + 2)
+        P, _ = m.prefill(s, rng.integers(0, 50257, n_text).astype(np.int32))
+        m.set_rng(s, pkg.T3B_RNG_PHILOX, seed * 1000 + s)
+        lens.append(P)
+    params = [pkg.SampleParams.make(**PARAMS, cfg_weight=0.5) for _ in range(streams)]
+    m.decode(params, warm, ignore_stop=True)                      # graph capture + warm-up
+    torch.cuda.synchronize()
+    m.decode(params, steps, ignore_stop=True)
+    ms = m.last_device_ms()
+    m.close()
+    wbytes = model_weight_bytes(t)
+    L_mean = float(np.mean(lens)) + warm + (steps + 1) / 2.0
+    kv = 2 * hp["n_layer"] * hp["n_embd"] * 2
+    step_bytes = wbytes + 2 * streams * kv * (L_mean + 1) + 2 * streams * hp["n_speech_vocab"] * 4
+    us = ms * 1000.0 / steps
+    ach = step_bytes / (us * 1e-6) / 1e9
+    return {"config": "configs[3]: 64 streams x CFG (128 rows), Q8_0, prompts U[100,400], "
+                      f"{steps} decode steps per stream, temp 0.8 / top_k 1000 / top_p 0.95 / penalty 1.2 / cfg 0.5",
+            "value": streams * steps / (ms / 1000.0), "unit": UNIT, "us_per_step": us,
+            "mean_L": L_mean, "bytes_per_step": step_bytes, "achieved_gbs": ach, "peak": peak,
+            "frac": ach / peak}
 
 
 def phase_timeline(pkg, step=5):

@@ -6,6 +6,7 @@
 
 #define T3B_HD 64            // head dimension of T3 (n_embd / n_head = 1024 / 16)
 #define T3B_ATTN_CHUNK 128   // keys per attention CTA (one key per thread)
+#define T3B_ATTN_ROWS_MIN 8  // from this many query rows on, one CTA per (row, head) walks all keys
 
 // Device-side error word bits (read back by the host after a launch).
 #define T3B_DEVERR_TOKEN   1u   // token id outside the embedding table

@@ -213,6 +213,183 @@ __global__ __launch_bounds__(256) void gemv_q_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// Quantised skinny GEMM for many activation rows (batched decode, M >= 16):
+// int8 tensor-core MMAs, mma.sync m16n8k32 — one instruction is exactly one
+// 32-element block's integer dot products for a 16 x 8 tile — followed by the
+// same per-block rescale as the GEMV, sumf += ((float) sumi * d_w) * d_x,
+// accumulated in registers in block order.  Per-32 f16 scales force a
+// rescale after every K = 32 step, which is why the accumulators live in
+// registers rather than in tensor memory.
+// CTA = 4 warps (2 x 2), CTA tile 64 activation rows x 32 weight rows, warp
+// tile 32 x 16 (2 x 2 MMA tiles).  K is staged four blocks (128 elements)
+// at a time in two cp.async buffers; smem rows are padded by 16 bytes so
+// the fragment loads of a warp hit 32 distinct banks.
+// grid = (ceil(N / 32), ceil(M / 64)).
+// ---------------------------------------------------------------------------
+#define GQ_BM 64
+#define GQ_BN 32
+#define GQ_KB 4                       // 32-element blocks per stage
+#define GQ_AROW (GQ_KB * 32 + 16)     // bytes per staged activation row
+#define GQ_BROW (GQ_KB * 32 + 16)     // bytes per staged weight row (Q4_0 uses half)
+
+__device__ __forceinline__ void cp_async16(void * smem, const void * gmem, bool pred) {
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    const int sz = pred ? 16 : 0;     // 0: fill with zeros, read nothing
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(sz) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void * smem, const void * gmem, bool pred) {
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    const int sz = pred ? 8 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(s), "l"(gmem), "r"(sz) : "memory");
+}
+
+template <int WT>
+__device__ __forceinline__ void mma_s8(int (&c)[4], const int (&a)[4], int b0, int b1) {
+    if (WT == T3B_Q4_0)   // unsigned nibbles x signed activations
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+template <int WT>
+__global__ __launch_bounds__(128) void gemm_q_mma_kernel(
+        const uint8_t * __restrict__ W, int N, int K, int rb,
+        const int8_t * __restrict__ xq, const float * __restrict__ xd, const int * __restrict__ xs,
+        int M, GemvEpi e) {
+    constexpr int QB = WT == T3B_Q4_0 ? 16 : 32;          // weight bytes per block
+    __shared__ __align__(16) int8_t As[2][GQ_BM][GQ_AROW];
+    __shared__ __align__(16) uint8_t Bs[2][GQ_BN][GQ_BROW];
+    __shared__ __align__(16) float Ds[2][GQ_BM][GQ_KB];   // activation block scales
+    __shared__ __align__(16) int Ss[2][GQ_BM][GQ_KB];     // activation block sums (Q4_0)
+    __shared__ __align__(16) __half Dw[2][GQ_BN][GQ_KB];  // weight block scales
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int wm = warp >> 1, wn = warp & 1;
+    const int m0 = blockIdx.y * GQ_BM, n0 = blockIdx.x * GQ_BN;
+    const int nb = K / 32;
+    const int nstage = nb / GQ_KB;
+
+    auto load_stage = [&](int s, int st) {
+        const int kb = st * GQ_KB;                         // first block of the stage
+        // activations: 64 rows x 128 bytes = 512 chunks of 16 bytes
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = tid + u * 128;
+            const int r = c >> 3, q = c & 7;
+            const bool ok = m0 + r < M;
+            cp_async16(&As[s][r][q * 16], xq + (size_t) (ok ? m0 + r : 0) * K + kb * 32 + q * 16, ok);
+        }
+        // activation scales and sums: 64 rows x 16 bytes each
+        if (tid < 64) {
+            const bool ok = m0 + tid < M;
+            const size_t o = (size_t) (ok ? m0 + tid : 0) * nb + kb;
+            cp_async16(&Ds[s][tid][0], xd + o, ok);
+            if (WT == T3B_Q4_0) cp_async16(&Ss[s][tid][0], xs + o, ok);
+        }
+        // weights: 32 rows x (4 * QB) bytes
+        constexpr int CPR = GQ_KB * QB / 16;              // chunks per row
+#pragma unroll
+        for (int u = 0; u < (GQ_BN * CPR + 127) / 128; ++u) {
+            const int c = tid + u * 128;
+            if (c < GQ_BN * CPR) {
+                const int r = c / CPR, q = c % CPR;
+                const bool ok = n0 + r < N;
+                cp_async16(&Bs[s][r][q * 16], W + (size_t) (ok ? n0 + r : 0) * rb + kb * QB + q * 16, ok);
+            }
+        }
+        if (tid < GQ_BN) {
+            const bool ok = n0 + tid < N;
+            const uint8_t * sc = W + (size_t) (ok ? n0 + tid : 0) * rb + (size_t) nb * QB + kb * 2;
+            cp_async8(&Dw[s][tid][0], sc, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    float acc[2][2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[i][j][k] = 0.0f;
+
+    load_stage(0, 0);
+    for (int st = 0; st < nstage; ++st) {
+        const int s = st & 1;
+        if (st + 1 < nstage) {
+            load_stage(s ^ 1, st + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+#pragma unroll
+        for (int bb = 0; bb < GQ_KB; ++bb) {
+            int a[2][4];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const int r = wm * 32 + mt * 16 + g;
+                a[mt][0] = *(const int *) &As[s][r][bb * 32 + t * 4];
+                a[mt][1] = *(const int *) &As[s][r + 8][bb * 32 + t * 4];
+                a[mt][2] = *(const int *) &As[s][r][bb * 32 + 16 + t * 4];
+                a[mt][3] = *(const int *) &As[s][r + 8][bb * 32 + 16 + t * 4];
+            }
+            int b[2][2];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const int r = wn * 16 + nt * 8 + g;
+                if (WT == T3B_Q4_0) {
+                    // block byte j holds elements j (low nibble) and j + 16 (high)
+                    const unsigned wv = *(const unsigned *) &Bs[s][r][bb * 16 + t * 4];
+                    b[nt][0] = (int) (wv & 0x0F0F0F0Fu);
+                    b[nt][1] = (int) ((wv >> 4) & 0x0F0F0F0Fu);
+                } else {
+                    b[nt][0] = *(const int *) &Bs[s][r][bb * 32 + t * 4];
+                    b[nt][1] = *(const int *) &Bs[s][r][bb * 32 + 16 + t * 4];
+                }
+            }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const int r0 = wm * 32 + mt * 16 + g;
+                const float dx0 = Ds[s][r0][bb], dx1 = Ds[s][r0 + 8][bb];
+                int sx0 = 0, sx1 = 0;
+                if (WT == T3B_Q4_0) { sx0 = 8 * Ss[s][r0][bb]; sx1 = 8 * Ss[s][r0 + 8][bb]; }
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    int c[4];
+                    mma_s8<WT>(c, a[mt], b[nt][0], b[nt][1]);
+                    const int cn = wn * 16 + nt * 8 + 2 * t;
+                    const float dw0 = __half2float(Dw[s][cn][bb]), dw1 = __half2float(Dw[s][cn + 1][bb]);
+                    // c0, c1: row g, columns 2t, 2t+1; c2, c3: row g + 8
+                    acc[mt][nt][0] = __fadd_rn(acc[mt][nt][0], __fmul_rn(__fmul_rn((float) (c[0] - sx0), dw0), dx0));
+                    acc[mt][nt][1] = __fadd_rn(acc[mt][nt][1], __fmul_rn(__fmul_rn((float) (c[1] - sx0), dw1), dx0));
+                    acc[mt][nt][2] = __fadd_rn(acc[mt][nt][2], __fmul_rn(__fmul_rn((float) (c[2] - sx1), dw0), dx1));
+                    acc[mt][nt][3] = __fadd_rn(acc[mt][nt][3], __fmul_rn(__fmul_rn((float) (c[3] - sx1), dw1), dx1));
+                }
+            }
+        }
+        __syncthreads();   // the buffer is refilled by the next stage's load
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            const int m = m0 + wm * 32 + mt * 16 + g;
+            const int n = n0 + wn * 16 + nt * 8 + 2 * t;
+            if (m < M && n < N) epi_store(e, m, n, acc[mt][nt][0]);
+            if (m < M && n + 1 < N) epi_store(e, m, n + 1, acc[mt][nt][1]);
+            if (m + 8 < M && n < N) epi_store(e, m + 8, n, acc[mt][nt][2]);
+            if (m + 8 < M && n + 1 < N) epi_store(e, m + 8, n + 1, acc[mt][nt][3]);
+        }
+}
+
 // F16 weights x f16-rounded activations, f32 accumulation (each f16*f16
 // product is exact in f32).  Lanes stride 8-element chunks.
 template <int MT, int RPW>
@@ -414,6 +591,120 @@ __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a)
         a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = ot / lt;
     }
     if (tid == 0) a.cnt[(size_t) m * a.n_head + h] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention for many rows (batched decode, prefill): one CTA of 4
+// warps per (row, head) walks all L keys.  Lanes form groups of 8; a group
+// holds one key's 64 halves of K and of V (16 bytes per lane), so a warp
+// takes 4 keys and the CTA 16 keys per step, two steps per iteration to
+// keep four 16-byte loads in flight per lane.  Each group keeps an online
+// softmax (running max, sum and 8 output dims per lane); the 16 groups are
+// merged at the end.  Scores are q.k / 8 as in attn_decode_kernel.
+// grid = (n_head, M), 128 threads.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void attn_merge(float & mx, float & l, float (&o)[8], float om, float ol, const float (&oo)[8]) {
+    const float nm = fmaxf(mx, om);
+    const float a1 = mx == -INFINITY ? 0.0f : expf(mx - nm);
+    const float a2 = om == -INFINITY ? 0.0f : expf(om - nm);
+    l = l * a1 + ol * a2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = o[i] * a1 + oo[i] * a2;
+    mx = nm;
+}
+
+__global__ __launch_bounds__(128) void attn_rows_kernel(AttnArgs a) {
+    __shared__ float wmx[4], wl[4];
+    __shared__ float wo[4][T3B_HD];
+    const int h = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+    const int lane = tid & 31, w = tid >> 5, grp = lane >> 3, c = lane & 7;
+    const int L = a.len[m] + a.len_add;
+    if (L <= 0 || L > a.max_ctx) {
+        if (tid == 0) atomicOr(a.err, T3B_DEVERR_POS);
+        return;
+    }
+    const int crow = a.row_of ? a.row_of[m] : m;
+    const __half * kb = a.kv + (size_t) crow * a.row_elems + a.layer_off + (size_t) h * a.max_ctx * T3B_HD + c * 8;
+    const __half * vb = kb + a.v_off;
+    float q[8];
+    {
+        const float * qp = a.q + (size_t) m * a.ldq + h * T3B_HD + c * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = qp[i];
+    }
+    float mx = -INFINITY, l = 0.0f, o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+    // the loop bound is uniform over the warp (every lane reaches every
+    // shuffle); a group whose key is past L contributes nothing
+    for (int jb = w * 4; jb < L; jb += 32) {
+        const int j = jb + grp;
+        const bool one = j < L, two = j + 16 < L;
+        uint4 k0 = make_uint4(0u, 0u, 0u, 0u), v0 = k0, k1 = k0, v1 = k0;
+        if (one) {
+            k0 = __ldg((const uint4 *) (kb + (size_t) j * T3B_HD));
+            v0 = __ldg((const uint4 *) (vb + (size_t) j * T3B_HD));
+        }
+        if (two) {
+            k1 = __ldg((const uint4 *) (kb + (size_t) (j + 16) * T3B_HD));
+            v1 = __ldg((const uint4 *) (vb + (size_t) (j + 16) * T3B_HD));
+        }
+        const __half2 * k0h = (const __half2 *) &k0, * k1h = (const __half2 *) &k1;
+        float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f0 = __half22float2(k0h[i]), f1 = __half22float2(k1h[i]);
+            d0 = fmaf(q[2 * i], f0.x, d0); d0 = fmaf(q[2 * i + 1], f0.y, d0);
+            d1 = fmaf(q[2 * i], f1.x, d1); d1 = fmaf(q[2 * i + 1], f1.y, d1);
+        }
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) {
+            d0 += __shfl_xor_sync(0xffffffffu, d0, off);
+            d1 += __shfl_xor_sync(0xffffffffu, d1, off);
+        }
+        const float s0 = one ? d0 * 0.125f : -INFINITY, s1 = two ? d1 * 0.125f : -INFINITY;
+        const float nm = fmaxf(mx, fmaxf(s0, s1));
+        const float corr = mx == -INFINITY ? 0.0f : expf(mx - nm);
+        const float p0 = one ? expf(s0 - nm) : 0.0f, p1 = two ? expf(s1 - nm) : 0.0f;
+        l = l * corr + p0 + p1;
+        const __half2 * v0h = (const __half2 *) &v0, * v1h = (const __half2 *) &v1;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f0 = __half22float2(v0h[i]), f1 = __half22float2(v1h[i]);
+            o[2 * i] = fmaf(p1, f1.x, fmaf(p0, f0.x, o[2 * i] * corr));
+            o[2 * i + 1] = fmaf(p1, f1.y, fmaf(p0, f0.y, o[2 * i + 1] * corr));
+        }
+        mx = nm;
+    }
+    // merge the four groups of the warp (lanes c, c+8, c+16, c+24 hold the same dims)
+#pragma unroll
+    for (int off = 8; off <= 16; off <<= 1) {
+        float oo[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) oo[i] = __shfl_xor_sync(0xffffffffu, o[i], off);
+        const float om = __shfl_xor_sync(0xffffffffu, mx, off), ol = __shfl_xor_sync(0xffffffffu, l, off);
+        attn_merge(mx, l, o, om, ol, oo);
+    }
+    if (grp == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wo[w][c * 8 + i] = o[i];
+        if (c == 0) { wmx[w] = mx; wl[w] = l; }
+    }
+    __syncthreads();
+    if (tid < T3B_HD) {
+        float gm = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) gm = fmaxf(gm, wmx[u]);
+        float lt = 0.0f, ot = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (wmx[u] == -INFINITY) continue;
+            const float f = expf(wmx[u] - gm);
+            lt = fmaf(wl[u], f, lt);
+            ot = fmaf(wo[u][tid], f, ot);
+        }
+        a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = ot / lt;
+    }
 }
 
 // ---------------------------------------------------------------------------

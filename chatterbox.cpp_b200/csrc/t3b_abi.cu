@@ -259,6 +259,11 @@ void launch_gemv_h_t(const Mat & W, const __half * xh, int M, const GemvEpi & e,
 template <int WT>
 void launch_gemv_q(const Mat & W, const int8_t * xq, const float * xd, const int * xs, int M, const GemvEpi & e,
                    cudaStream_t st) {
+    if (M >= 16 && W.K % (32 * GQ_KB) == 0) {   // many rows: int8 tensor-core GEMM
+        dim3 grid((W.N + GQ_BN - 1) / GQ_BN, (M + GQ_BM - 1) / GQ_BM);
+        gemm_q_mma_kernel<WT><<<grid, 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd, xs, M, e);
+        return;
+    }
     if (M <= 1) launch_gemv_q_t<WT, 1>(W, xq, xd, xs, M, e, st);
     else if (M <= 2) launch_gemv_q_t<WT, 2>(W, xq, xd, xs, M, e, st);
     else if (M <= 4) launch_gemv_q_t<WT, 4>(W, xq, xd, xs, M, e, st);
@@ -305,7 +310,8 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         a.kv = ctx->kv; a.row_elems = ctx->row_elems; a.layer_off = e.layer_off; a.v_off = e.v_off;
         a.row_of = row_of; a.len = pos; a.len_add = 1; a.max_ctx = ctx->max_ctx; a.n_head = H;
         a.out = ctx->attn; a.ldo = D; a.part = ctx->part; a.cnt = ctx->cnt; a.s_max = ctx->s_max; a.err = ctx->err_word;
-        attn_decode_kernel<<<dim3(H, M, ctx->s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
+        if (M >= T3B_ATTN_ROWS_MIN) attn_rows_kernel<<<dim3(H, M), 128, 0, st>>>(a);
+        else attn_decode_kernel<<<dim3(H, M, ctx->s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
         // proj + bias + residual
         launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
         launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_RESID, ctx->x, D, Ly.proj_b, ctx->x, D), st);
@@ -1147,7 +1153,8 @@ int t3b_op_attention(const float * q_dev, const void * k_dev, const void * v_dev
     a.v_off = (size_t) ((const __half *) v_dev - (const __half *) k_dev);
     a.row_of = nullptr; a.len = len_dev; a.len_add = 0; a.max_ctx = max_ctx; a.n_head = n_head;
     a.out = out_dev; a.ldo = n_head * T3B_HD; a.part = sc->part; a.cnt = sc->cnt; a.s_max = s_max; a.err = errw;
-    attn_decode_kernel<<<dim3(n_head, M, s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
+    if (M >= T3B_ATTN_ROWS_MIN) attn_rows_kernel<<<dim3(n_head, M), 128, 0, st>>>(a);
+    else attn_decode_kernel<<<dim3(n_head, M, s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
     return T3B_OK;
