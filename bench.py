@@ -304,6 +304,7 @@ def main():
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
             "sampler": sampler_microbench(pkg, torch, peak),
+            "batched_cfg": batched_cfg(pkg, torch, peak) if rank == 0 else None,
             "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": 2,   # first-token sampler + one t3_decode_megakernel launch
             "tokens_head": [int(x) for x in toks[:8]]}

@@ -16,9 +16,12 @@
 //
 // Phases per layer (rows split evenly over the G CTAs):
 //   P1 LN1 + QKV GEMV (+ K/V append to the f16 cache)        -> q,k,v slots
-//   P2 attention, CTA h < n_head owns head h                  -> attn slots
-//   P3 proj GEMV + bias + residual                            -> x_mid slots
-//   P4 LN2 + fc GEMV + bias + GELU                            -> h slots
+//   P2 attention, CTA h < n_head owns head h; for Q4_0/Q8_0 weights the same
+//      CTA also quantises its 64 outputs (Q8_0 blocks 2h, 2h+1) and forms the
+//      out-projection over them for all 1024 rows       -> per-head partials
+//   P3 (F16 weights only) proj GEMV + bias + residual        -> x_mid slots
+//   P4 x_mid = sum of the 16 head partials + bias + residual (every CTA),
+//      LN2 + fc GEMV + bias + GELU                            -> h slots
 //   P5 fc2 GEMV + bias + residual                             -> x slots
 // then LN_f + head GEMV -> logit slots, CTA 0 runs the sampler, publishes
 // the token slot, and every CTA builds the next step's embedding itself.
@@ -42,7 +45,8 @@
 #define MK_B_X (MK_B_H + 4096)
 #define MK_B_LOG (MK_B_X + 1024)
 #define MK_B_TOK (MK_B_LOG + T3B_SAMPLER_VMAX)
-#define MK_B_TOTAL (MK_B_TOK + 32)
+#define MK_B_PART (MK_B_TOK + 32)          // [16 heads][1024] out-projection partials
+#define MK_B_TOTAL (MK_B_PART + 16 * 1024)
 enum { MK_C_QKV, MK_C_ATT, MK_C_XM, MK_C_H, MK_C_X, MK_C_LOG, MK_C_TOK, MK_C_N };
 #define MK_C_STRIDE 32   // counters 128 bytes apart
 
@@ -415,7 +419,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
 
 // Dynamic shared memory the megakernel needs.
 constexpr size_t mk_smem_bytes() {
-    return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 1024) * 4;
+    return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 1024 + 128) * 4;   // + head outputs and their Q8_0
 }
 static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
 
@@ -467,17 +471,19 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // attention stage (and, in CTA 0, the sampler) reuse the same bytes
     __half * kst = (__half *) smem;
     __half * vst = kst + MK_MAX_POS * T3B_HD;
-    float * att_s = (float *) (smem + 2 * MK_MAX_POS * T3B_HD * 2);   // qkv[192] | p[MK_MAX_POS] | o[8][64]
+    float * att_s = (float *) (smem + 2 * MK_MAX_POS * T3B_HD * 2);   // qkv[192] | p[MK_MAX_POS] | o[16][64] | head out[64] + Q8_0
 
     const int tid = threadIdx.x, cta = blockIdx.x, G = gridDim.x;
     const int NL = a.n_layer;
     const int Hn = 16;
+    constexpr bool FUSE = T != T3B_F16;   // out-projection folded into the attention CTAs
     unsigned * cQKV = a.cnt + MK_C_QKV * MK_C_STRIDE, * cATT = a.cnt + MK_C_ATT * MK_C_STRIDE;
     unsigned * cXM = a.cnt + MK_C_XM * MK_C_STRIDE, * cH = a.cnt + MK_C_H * MK_C_STRIDE;
     unsigned * cX = a.cnt + MK_C_X * MK_C_STRIDE, * cLOG = a.cnt + MK_C_LOG * MK_C_STRIDE;
     unsigned * cTOK = a.cnt + MK_C_TOK * MK_C_STRIDE;
     float * bQKV = a.buf + MK_B_QKV, * bATT = a.buf + MK_B_ATT, * bXM = a.buf + MK_B_XM;
     float * bH = a.buf + MK_B_H, * bX = a.buf + MK_B_X, * bLOG = a.buf + MK_B_LOG;
+    float * bPART = a.buf + MK_B_PART;
     int * bTOK = (int *) (a.buf + MK_B_TOK);
 
     int tok = a.samp.step_tok[a.samp.slot_of ? a.samp.slot_of[0] : 0];
@@ -493,7 +499,8 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
             {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
-                mk_l2_prefetch(Ly.o, D);
+                if (FUSE) mk_l2_prefetch(Ly.fc, 4 * D);   // the next GEMV this CTA runs is P4's
+                else mk_l2_prefetch(Ly.o, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bqkv + r0_ + tid) : 0.0f;
                 MK_STAMP(l * 20 + 0);
@@ -537,6 +544,20 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sv), "l"(vb + i * 8) : "memory");
                 }
                 asm volatile("cp.async.commit_group;" ::: "memory");
+                // out-projection weights of this head: blocks 2h, 2h+1 of rows
+                // tid and tid + 512 (quants and the two block scales)
+                uint4 ow[2][MkW<T>::QW * 2];
+                unsigned ows[2] = {0u, 0u};
+                if (FUSE) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint8_t * wr = Ly.o.w + (size_t) (tid + u * MK_THREADS) * Ly.o.rb;
+                        constexpr int QB = T == T3B_Q4_0 ? 16 : 32;
+#pragma unroll
+                        for (int c = 0; c < MkW<T>::QW * 2; ++c) ow[u][c] = ldg_v4(wr + 2 * h * QB + c * 16);
+                        ows[u] = ld_nc_u32(wr + (size_t) (D / 32) * QB + 4 * h);
+                    }
+                }
                 float * qkvh = att_s;   // [192]
                 const bool ok = mk_acquire(cQKV, k * G, a);
                 if (tid < 192) qkvh[tid] = __ldcg(bQKV + (tid / 64) * D + h * 64 + (tid & 63));
@@ -617,18 +638,82 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     og[w * 64 + 2 * lane] = o0.x + o1.x;
                     og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
                     __syncthreads();
+                    float * ho = og + 16 * 64;   // this head's 64 outputs
                     if (tid < 64) {
                         float t = 0.0f;
 #pragma unroll
                         for (int gg = 0; gg < 16; ++gg) t += og[gg * 64 + tid];
-                        bATT[h * 64 + tid] = t / lsum;
+                        t = t / lsum;
+                        if (FUSE) ho[tid] = t;
+                        else bATT[h * 64 + tid] = t;
+                    }
+                    if (FUSE) {
+                        // Q8_0 of the two blocks (what the proj GEMV's activation
+                        // prep does to blocks 2h, 2h+1 of the attention vector),
+                        // by warp 0 with every lane in every shuffle
+                        int8_t * hq = (int8_t *) (ho + 64);
+                        float * hd = ho + 64 + 16;
+                        int * hs = (int *) (ho + 64 + 18);
+                        __syncthreads();
+                        if (tid < 32) {
+                            const float v0 = ho[lane], v1 = ho[32 + lane];
+                            const float m0 = warp_max(fabsf(v0)), m1 = warp_max(fabsf(v1));
+                            const float d0 = __fdiv_rn(m0, 127.0f), d1 = __fdiv_rn(m1, 127.0f);
+                            const float i0 = d0 != 0.0f ? __fdiv_rn(1.0f, d0) : 0.0f;
+                            const float i1 = d1 != 0.0f ? __fdiv_rn(1.0f, d1) : 0.0f;
+                            const int q0 = (int) roundf(__fmul_rn(v0, i0)), q1 = (int) roundf(__fmul_rn(v1, i1));
+                            hq[lane] = (int8_t) q0;
+                            hq[32 + lane] = (int8_t) q1;
+                            const int s0 = warp_sum_i(q0), s1 = warp_sum_i(q1);
+                            if (lane == 0) {
+                                hd[0] = __half2float(__float2half_rn(d0)); hd[1] = __half2float(__float2half_rn(d1));
+                                hs[0] = s0; hs[1] = s1;
+                            }
+                        }
+                        __syncthreads();
+                        const int4 xa = *(const int4 *) hq, xb = *(const int4 *) (hq + 16);
+                        const int4 xc = *(const int4 *) (hq + 32), xe = *(const int4 *) (hq + 48);
+                        const float dx0 = hd[0], dx1 = hd[1];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            int s0 = 0, s1 = 0;
+                            if (T == T3B_Q4_0) {
+                                const uint4 w0 = ow[u][0], w1 = ow[u][1];
+                                s0 = __dp4a((int) (w0.x & 0x0F0F0F0Fu), xa.x, s0); s0 = __dp4a((int) ((w0.x >> 4) & 0x0F0F0F0Fu), xb.x, s0);
+                                s0 = __dp4a((int) (w0.y & 0x0F0F0F0Fu), xa.y, s0); s0 = __dp4a((int) ((w0.y >> 4) & 0x0F0F0F0Fu), xb.y, s0);
+                                s0 = __dp4a((int) (w0.z & 0x0F0F0F0Fu), xa.z, s0); s0 = __dp4a((int) ((w0.z >> 4) & 0x0F0F0F0Fu), xb.z, s0);
+                                s0 = __dp4a((int) (w0.w & 0x0F0F0F0Fu), xa.w, s0); s0 = __dp4a((int) ((w0.w >> 4) & 0x0F0F0F0Fu), xb.w, s0);
+                                s1 = __dp4a((int) (w1.x & 0x0F0F0F0Fu), xc.x, s1); s1 = __dp4a((int) ((w1.x >> 4) & 0x0F0F0F0Fu), xe.x, s1);
+                                s1 = __dp4a((int) (w1.y & 0x0F0F0F0Fu), xc.y, s1); s1 = __dp4a((int) ((w1.y >> 4) & 0x0F0F0F0Fu), xe.y, s1);
+                                s1 = __dp4a((int) (w1.z & 0x0F0F0F0Fu), xc.z, s1); s1 = __dp4a((int) ((w1.z >> 4) & 0x0F0F0F0Fu), xe.z, s1);
+                                s1 = __dp4a((int) (w1.w & 0x0F0F0F0Fu), xc.w, s1); s1 = __dp4a((int) ((w1.w >> 4) & 0x0F0F0F0Fu), xe.w, s1);
+                                s0 -= 8 * hs[0];
+                                s1 -= 8 * hs[1];
+                            } else {
+                                const uint4 w0 = ow[u][0], w1 = ow[u][1 % (MkW<T>::QW * 2)];
+                                const uint4 w2 = ow[u][2 % (MkW<T>::QW * 2)], w3 = ow[u][3 % (MkW<T>::QW * 2)];
+                                s0 = __dp4a((int) w0.x, xa.x, s0); s0 = __dp4a((int) w0.y, xa.y, s0);
+                                s0 = __dp4a((int) w0.z, xa.z, s0); s0 = __dp4a((int) w0.w, xa.w, s0);
+                                s0 = __dp4a((int) w1.x, xb.x, s0); s0 = __dp4a((int) w1.y, xb.y, s0);
+                                s0 = __dp4a((int) w1.z, xb.z, s0); s0 = __dp4a((int) w1.w, xb.w, s0);
+                                s1 = __dp4a((int) w2.x, xc.x, s1); s1 = __dp4a((int) w2.y, xc.y, s1);
+                                s1 = __dp4a((int) w2.z, xc.z, s1); s1 = __dp4a((int) w2.w, xc.w, s1);
+                                s1 = __dp4a((int) w3.x, xe.x, s1); s1 = __dp4a((int) w3.y, xe.y, s1);
+                                s1 = __dp4a((int) w3.z, xe.z, s1); s1 = __dp4a((int) w3.w, xe.w, s1);
+                            }
+                            const float dw0 = __half2float(__ushort_as_half((unsigned short) (ows[u] & 0xffffu)));
+                            const float dw1 = __half2float(__ushort_as_half((unsigned short) (ows[u] >> 16)));
+                            const float t0 = __fmul_rn(__fmul_rn((float) s0, dw0), dx0);
+                            const float t1 = __fmul_rn(__fmul_rn((float) s1, dw1), dx1);
+                            bPART[h * D + tid + u * MK_THREADS] = __fadd_rn(t0, t1);
+                        }
                     }
                 }
                 mk_release(cATT);
                 MK_STAMP(l * 20 + 4);
             }
-            // ---------------- P3: proj + bias + residual -----------------------
-            {
+            // ---------------- P3: proj + bias + residual (F16 weights) --------
+            if (!FUSE) {
                 MK_GEMV_BEGIN(Ly.o, D, D)
                 mk_l2_prefetch(Ly.fc, 4 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bo + r0_ + tid) : 0.0f;
@@ -648,10 +733,31 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 mk_l2_prefetch(Ly.fc2, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
-                if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
+                if (FUSE) {
+                    // x_mid = (sum over heads of the partials) + proj bias + x,
+                    // heads added in order 0..15
+                    const float bo0 = __ldg(Ly.bo + tid), bo1 = __ldg(Ly.bo + tid + MK_THREADS);
+                    if (!mk_acquire(cATT, k * Hn, a)) return;
+                    float p0[16], p1[16];
+#pragma unroll
+                    for (int hh = 0; hh < 16; ++hh) {
+                        p0[hh] = __ldcg(bPART + hh * D + tid);
+                        p1[hh] = __ldcg(bPART + hh * D + tid + MK_THREADS);
+                    }
+                    float s0 = p0[0], s1 = p1[0];
+#pragma unroll
+                    for (int hh = 1; hh < 16; ++hh) { s0 = __fadd_rn(s0, p0[hh]); s1 = __fadd_rn(s1, p1[hh]); }
+                    s0 = __fadd_rn(__fadd_rn(s0, bo0), xres[tid]);
+                    s1 = __fadd_rn(__fadd_rn(s1, bo1), xres[tid + MK_THREADS]);
+                    xmid[tid] = s0; xmid[tid + MK_THREADS] = s1;
+                    vec[tid] = s0; vec[tid + MK_THREADS] = s1;
+                    __syncthreads();
+                } else {
+                    if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
+                    for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
+                    __syncthreads();
+                }
                 MK_STAMP(l * 20 + 6);
-                for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
-                __syncthreads();
                 mk_layernorm(vec, lp, a.eps, redd);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
