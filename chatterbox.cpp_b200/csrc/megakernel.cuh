@@ -389,6 +389,14 @@ __device__ void mk_dot(const MkPref<T> & pf, int K, int r0, int r1, const MkAct 
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int mk_r0(int N, int c, int G) { return (int) (((long long) N * c) / G); }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// phase timeline (debug): stamp point `i` of the traced step
+#define MK_STAMP(i) do { if (a.tl && step == a.tl_step && tid == 0) a.tl[(size_t) cta * MK_TL + (i)] = globaltimer_ns(); } while (0)
+
 // LN_f + speech_head rows of this CTA; the head keeps its own weight type.
 template <int HT>
 __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, const MkAct & act, float * part,
@@ -401,9 +409,12 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
     const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
     if (!mk_wait_vec(a.cnt + MK_C_X * MK_C_STRIDE, kx * G, a.buf + MK_B_X, D, vec, a)) return false;
+    const int cta = blockIdx.x;
+    MK_STAMP(487);
     mk_layernorm(vec, lp, a.eps, redd);
     mk_quantize(act, D, HT == T3B_F16);
     mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
+    MK_STAMP(488);
     float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
     float * lg = a.buf + MK_B_LOG;
     if (tid < r1 - r0) {
@@ -442,13 +453,6 @@ __device__ __forceinline__ void mk_l2_prefetch(const MkMat & W, int N) {
     MkPref<T> pf_;                                                                                 \
     mk_prefetch<T>((W), (K), r0_, r1_, pf_);
 
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-// phase timeline (debug): stamp point `i` of the traced step
-#define MK_STAMP(i) do { if (a.tl && step == a.tl_step && tid == 0) a.tl[(size_t) cta * MK_TL + (i)] = globaltimer_ns(); } while (0)
 
 template <int T>
 __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a) {
@@ -488,6 +492,11 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
 
     int tok = a.samp.step_tok[a.samp.slot_of ? a.samp.slot_of[0] : 0];
     for (int step = 0; step < a.n_steps; ++step) {
+        // host cancel flag (mapped memory, a PCIe round trip): one thread of
+        // CTA 0 reads it at the start of the step; the value is needed only
+        // after the sampler, so the read overlaps the whole step
+        int cancelled = 0;
+        if (cta == 0 && tid == 0 && a.cancel) cancelled = *(volatile const int *) a.cancel;
         const int pos = a.p0 + step;
         // embedding: x = speech_emb[tok] + wpe[pos]
         for (int i = tid; i < D; i += MK_THREADS)
@@ -797,9 +806,6 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         if (!a.sample) return;   // eval_step: logits only
         // ---------------- sampler (CTA 0) and token broadcast -------------------
         if (cta == 0) {
-            // host cancel flag (mapped memory): read before the wait so the
-            // PCIe round trip overlaps it
-            const int cancelled = a.cancel ? *(volatile const int *) a.cancel : 0;
             float * lg = (float *) (smem + T3B_SAMPLER_SMEM);   // logits staged after the sampler's arrays
             if (!mk_acquire(cLOG, (unsigned) (step + 1) * G, a)) return;
             {
