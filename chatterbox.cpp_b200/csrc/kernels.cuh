@@ -967,6 +967,46 @@ __device__ int block_first_crossing(int n, double target, double eps, LoadF load
     return idx;
 }
 
+// Block-wide exclusive scan of ints in thread order (blockDim.x a multiple
+// of 32); *total receives the sum.
+__device__ __forceinline__ int block_excl_scan_i(int v, int * red, int * total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    __syncthreads();
+    if (lane == 31) red[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        const int x = lane < nw ? red[lane] : 0;
+        int xi = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, xi, o);
+            if (lane >= o) xi += n;
+        }
+        if (lane < nw) red[lane] = xi - x;
+        if (lane == 31) red[32] = xi;
+    }
+    __syncthreads();
+    const int r = red[w] + incl - v;
+    *total = red[32];
+    return r;
+}
+
+// Linear value bins of the sampler's fast top-k/top-p path, highest score
+// first: floor((v - smin) * scale) never decreases as v grows.
+#define SAMP_NBIN 2048
+#define SAMP_BIN_MAX 32
+__device__ __forceinline__ int samp_dbin(float v, float smin, float scale) {
+    int b = (int) __fmul_rn(__fsub_rn(v, smin), scale);
+    b = min(max(b, 0), SAMP_NBIN - 1);
+    return SAMP_NBIN - 1 - b;
+}
+
 // One row of sample_next_token_ex by the whole block (any blockDim.x that
 // is a multiple of 32 and >= 256).  smraw: T3B_SAMPLER_SMEM bytes of shared
 // memory.  Returns the token (every thread), or -1 for a finished stream.
@@ -983,7 +1023,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     float * e = (float *) (smraw + T3B_SAMPLER_VMAX * 12);
     int * lst = (int *) keys;   // index list, reused after the sort
     __shared__ float redf[32];
-    __shared__ int redi[32];
+    __shared__ int redi[33];
     __shared__ double redd[33];
     __shared__ unsigned seen[T3B_SAMPLER_VMAX / 32];
     __shared__ int shi[8];
@@ -1011,7 +1051,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const bool cfg = unc != nullptr && P.cfg_weight != 0.0f;
     const bool use_t = P.temp > 0.0f && P.temp != 1.0f;
     const float inv_t = use_t ? __fdiv_rn(1.0f, P.temp) : 1.0f;
-    float lmx = -INFINITY;
+    float lmx = -INFINITY, lmn = INFINITY;
     int lfin = 0;
     for (int i0 = 0; i0 < V; i0 += 4 * nth) {
         float cv[4], uv[4];
@@ -1029,12 +1069,13 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 if (cfg) v = __fadd_rn(v, __fmul_rn(P.cfg_weight, __fsub_rn(v, uv[q])));
                 if (use_t) v = __fmul_rn(v, inv_t);
                 s[i] = v;
-                if (v != -INFINITY) { lmx = fmaxf(lmx, v); ++lfin; }
+                if (v != -INFINITY) { lmx = fmaxf(lmx, v); lmn = fminf(lmn, v); ++lfin; }
             }
         }
     }
     int nfin = block_sum_i(lfin, redi);
     const float smax = block_max(lmx, redf);
+    const float smin = -block_max(-lmn, redf);
 
     SAMP_STAMP(1);
     // (1b) min-p: drop exp(s - max) < min_p.  The host expf is within one ulp
@@ -1067,7 +1108,106 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     // changes, so the stage is skipped.
     bool topk_pending = false;   // drop of s <= thr_k not yet applied
     float thr_k = -INFINITY;
-    if (P.top_k > 0 && P.top_k < V && nfin > P.top_k) {
+    // Fast path of (2) and (3): linear value bins order the scores, so a
+    // histogram finds the bin of rank k; the scores of that bin and above are
+    // scattered into their bins and each bin (at most SAMP_BIN_MAX scores) is
+    // insertion-sorted by (value desc, index asc), which is the order top-p
+    // needs.  fastc = number of sorted survivors in keys[] (-1: not taken;
+    // the radix path below then runs on the untouched scores).
+    int fastc = -1;
+    {
+        const bool need_k = P.top_k > 0 && P.top_k < V && nfin > P.top_k;
+        const bool need_p = P.top_p < 1.0f;
+        const float span = __fsub_rn(smax, smin);
+        if ((need_k || need_p) && nfin > 256 && span > 0.0f && span < INFINITY) {   // few scores: gather + bitonic is cheaper
+            const float scale = __fdiv_rn((float) SAMP_NBIN, span);
+            int * hist = (int *) e;            // e[] is free until the top-p exps
+            int * start = hist + SAMP_NBIN;
+            int * cur = start + SAMP_NBIN;
+            for (int d = tid; d < SAMP_NBIN; d += nth) { hist[d] = 0; cur[d] = 0; }
+            __syncthreads();
+            for (int i = tid; i < V; i += nth) {
+                const float v = s[i];
+                if (v != -INFINITY) atomicAdd(&hist[samp_dbin(v, smin, scale)], 1);
+            }
+            __syncthreads();
+            const int bpt = (SAMP_NBIN + nth - 1) / nth;
+            const int b0 = min(SAMP_NBIN, tid * bpt), b1 = min(SAMP_NBIN, b0 + bpt);
+            int tot = 0;
+            for (int d = b0; d < b1; ++d) tot += hist[d];
+            int total;
+            const int excl = block_excl_scan_i(tot, redi, &total);
+            {
+                int run = excl;
+                for (int d = b0; d < b1; ++d) { start[d] = run; run += hist[d]; }
+            }
+            if (tid == 0) shi[0] = SAMP_NBIN - 1;
+            __syncthreads();
+            if (need_k && excl <= P.top_k && P.top_k < excl + tot) {
+                for (int d = b0; d < b1; ++d)
+                    if (P.top_k < start[d] + hist[d]) { shi[0] = d; break; }
+            }
+            __syncthreads();
+            const int dsel = shi[0];
+            int lmaxb = 0;
+            for (int d = b0; d < b1 && d <= dsel; ++d) lmaxb = max(lmaxb, hist[d]);
+            const int maxb = (int) block_max((float) lmaxb, redf);
+            if (maxb <= SAMP_BIN_MAX) {
+                for (int i = tid; i < V; i += nth) {
+                    const float v = s[i];
+                    if (v == -INFINITY) continue;
+                    const int d = samp_dbin(v, smin, scale);
+                    if (d > dsel) continue;
+                    const int pos = start[d] + atomicAdd(&cur[d], 1);
+                    keys[pos] = ((unsigned long long) desc_key(v) << 32) | (unsigned) i;
+                }
+                __syncthreads();
+                for (int d = tid; d <= dsel; d += nth) {
+                    unsigned long long * kp = keys + start[d];
+                    const int n = hist[d];
+                    for (int x = 1; x < n; ++x) {
+                        const unsigned long long t = kp[x];
+                        int y = x - 1;
+                        while (y >= 0 && kp[y] > t) { kp[y + 1] = kp[y]; --y; }
+                        kp[y + 1] = t;
+                    }
+                }
+                __syncthreads();
+                const int ns = start[dsel] + hist[dsel];
+                if (need_k) {
+                    // threshold = the score at descending rank k; scores in
+                    // higher bins are strictly above it, equal scores share its bin
+                    if (tid == 0) {
+                        const float thr = desc_key_inv((uint32_t) (keys[P.top_k] >> 32));
+                        int above = start[dsel];
+                        for (int j = start[dsel]; j < ns; ++j) {
+                            if (desc_key_inv((uint32_t) (keys[j] >> 32)) > thr) ++above;
+                            else break;
+                        }
+                        const float thr2 = above < P.top_k ? __fsub_rn(thr, 1e-10f) : thr;
+                        shf[2] = thr;
+                        shi[5] = above;
+                        shi[6] = thr2 == thr;   // a nudge that moves thr can admit scores below this bin
+                    }
+                    __syncthreads();
+                    if (shi[6]) {
+                        thr_k = shf[2];
+                        topk_pending = true;      // applied by the pass below
+                        fastc = shi[5];
+                    }
+                } else {
+                    fastc = ns;
+                }
+                __syncthreads();
+            }
+        }
+    }
+    if (fastc >= 0 && topk_pending) {
+        for (int i = tid; i < V; i += nth) if (s[i] <= thr_k) s[i] = -INFINITY;
+        topk_pending = false;
+        __syncthreads();
+    }
+    if (fastc < 0 && P.top_k > 0 && P.top_k < V && nfin > P.top_k) {
         // digits of 11, 11 and 10 bits: the first already spreads the scores
         // over their exponent and leading mantissa bits, so few keys share a
         // bin and plain shared-memory atomics stay cheap
@@ -1166,9 +1306,9 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     // (3) top-p (main.cpp:750-772): survivors sorted by score descending
     // (ties by ascending index), sequential float sums in that order.
     if (P.top_p < 1.0f) {
-        if (tid == 0) shi[2] = 0;
+        if (tid == 0) shi[2] = fastc >= 0 ? fastc : 0;
         __syncthreads();
-        for (int i0 = 0; i0 < V; i0 += nth) {            // warp-aggregated gather (+ top-k drop)
+        for (int i0 = 0; fastc < 0 && i0 < V; i0 += nth) {   // warp-aggregated gather (+ top-k drop)
             const int i = i0 + tid;
             float v = i < V ? s[i] : -INFINITY;
             if (topk_pending && i < V && v <= thr_k) { s[i] = -INFINITY; v = -INFINITY; }
@@ -1183,7 +1323,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         __syncthreads();
         const int c = shi[2];
         SAMP_STAMP(4);
-        if (c > 0) {
+        if (c > 0 && fastc < 0) {
             int n2 = 2;
             while (n2 < c) n2 <<= 1;
             for (int i = c + tid; i < n2; i += nth) keys[i] = ~0ull;
@@ -1203,6 +1343,8 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                     if (j >= 64 || (jn >= 64 && k < n2)) __syncthreads();
                     else __syncwarp();
                 }
+        }
+        if (c > 0) {
             __syncthreads();
             SAMP_STAMP(5);
             const float mx = s[(int) (keys[0] & 0xffffffffu)];

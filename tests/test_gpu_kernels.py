@@ -138,6 +138,48 @@ def test_attention_matches_fp64(pkg, L_, M):
             assert rel_err(out[m, h * 64:(h + 1) * 64], ref) < 1e-5, (m, h, n)
 
 
+@pytest.mark.parametrize("kind", ["narrow", "rounded"])
+def test_sampler_bucket_and_radix_paths(pkg, orc, kind):
+    """Top-k 1000 / top-p 0.95 without min-p on narrow logits (value bins
+    hold few scores: the bucketed top-k + sort path) and on logits rounded to
+    0.1 (thousands of exact ties: the radix-select + bitonic path): device
+    tokens == oracle tokens."""
+    L = pkg.lib()
+    rows, V, HL = 128, 6563, 256
+    rng = np.random.default_rng(11)
+    if kind == "narrow":
+        cond = np.stack([synth_logits(700 + r, scale=0.6) for r in range(rows)])
+    else:
+        cond = np.stack([synth_logits(700 + r, kind="rounded") for r in range(rows)])
+    unc = np.zeros_like(cond)
+    hist = rng.integers(0, V, (rows, HL)).astype(np.int32)
+    hlen = np.full(rows, HL, np.int32)
+    params = [dict(top_k=int(rng.choice([50, 1000])), top_p=float(rng.choice([0.8, 0.95, 1.0])), temp=0.8,
+                   repeat_penalty=1.2, min_p=0.0, cfg_weight=0.0) for _ in range(rows)]
+    seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
+    ctrs = rng.integers(0, 2 ** 40, rows, dtype=np.uint64)
+    P = (pkg.SampleParams * rows)(*[pkg.SampleParams.make(**p) for p in params])
+    pd = torch.frombuffer(bytearray(bytes(P)), dtype=torch.uint8).cuda()
+    cd, ud = torch.from_numpy(cond).cuda(), torch.from_numpy(unc).cuda()
+    hd, hld = torch.from_numpy(hist).cuda(), torch.from_numpy(hlen).cuda()
+    sd = torch.from_numpy(seeds.view(np.int64)).cuda()
+    ctd = torch.from_numpy(ctrs.view(np.int64)).cuda()
+    td = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    pkg.check(L.t3b_op_sample_philox(_p(cd), _p(ud), rows, V, _p(hd), _p(hld), HL, _p(pd), _p(sd), _p(ctd),
+                                     _p(td), _stream()))
+    torch.cuda.synchronize()
+    got = td.cpu().numpy()
+    checked = 0
+    for r in range(rows):
+        x1, x2 = _philox_words(orc, int(seeds[r]), int(ctrs[r]), r)
+        t, aux = orc.sample(cond[r], params[r], x1, x2, uncond=unc[r], hist=hist[r])
+        if aux[2]:
+            continue
+        assert got[r] == t, (kind, r, params[r])
+        checked += 1
+    assert checked > rows // 2
+
+
 def _philox_words(orc, seed, ctr, row):
     w = orc.philox([ctr & 0xFFFFFFFF, ctr >> 32, row, 0], [seed & 0xFFFFFFFF, seed >> 32])
     return int(w[0]), int(w[1])
