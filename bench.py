@@ -200,7 +200,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched"], default=None,
+    ap.add_argument("--no-batched", action="store_true", help="leave out the batched CFG run (profiling commands)")
+    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels"], default=None,
                     help="run one kernel micro-benchmark alone (ncu captures), or the megakernel phase timeline")
     args = ap.parse_args()
     if args.only:
@@ -213,6 +214,9 @@ def main():
         elif args.only == "batched":
             import torch
             r = batched_cfg(pkg, torch, peak)
+        elif args.only == "kernels":
+            import torch
+            r = batched_kernels(pkg, torch, peak)
         else:
             r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
         print(json.dumps(r), flush=True)
@@ -304,7 +308,8 @@ def main():
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
             "sampler": sampler_microbench(pkg, torch, peak),
-            "batched_cfg": batched_cfg(pkg, torch, peak) if rank == 0 else None,
+            "batched_cfg": batched_cfg(pkg, torch, peak) if rank == 0 and not args.no_batched else None,
+            "batched_kernels": batched_kernels(pkg, torch, peak),
             "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": 2,   # first-token sampler + one t3_decode_megakernel launch
             "tokens_head": [int(x) for x in toks[:8]]}
@@ -397,6 +402,58 @@ def batched_cfg(pkg, torch, peak, steps=256, streams=64, seed=3):
             "value": streams * steps / (ms / 1000.0), "unit": UNIT, "us_per_step": us,
             "mean_L": L_mean, "bytes_per_step": step_bytes, "achieved_gbs": ach, "peak": peak,
             "frac": ach / peak}
+
+
+def batched_kernels(pkg, torch, peak, reps=50):
+    """The two kernels of the batched decode step alone, 128 rows: the Q8_0
+    fc GEMV of T3 (1024 -> 4096) through t3b_op_gemv (activation prep +
+    int8 tensor-core GEMM), and decode attention over 16 heads x 400 f16
+    positions per row through t3b_op_attention (one CTA per (row, head)).
+    CUDA events on the launching stream; the attention's K/V (268 MB)
+    exceed L2, the GEMM's weights (4.4 MB) stay in it (compute-bound)."""
+    import ctypes as C
+    import gguf
+    L = pkg.lib()
+    s = torch.cuda.current_stream()
+    sp = C.c_void_p(s.cuda_stream)
+    M, K, N = 128, 1024, 4096
+    w = (np.random.default_rng(2).standard_normal((N, K)) * 0.02).astype(np.float32)
+    q = np.ascontiguousarray(gguf.quants.quantize(w, gguf.GGMLQuantizationType.Q8_0))
+    rb = L.t3b_op_row_bytes(8, K)
+    wd = torch.empty(N * rb, dtype=torch.uint8, device="cuda")
+    pkg.check(L.t3b_op_repack(8, q.ctypes.data, N, K, C.c_void_p(wd.data_ptr())))
+    x = torch.randn(M, K, device="cuda")
+    y = torch.empty(M, N, device="cuda")
+    gemm_args = (8, C.c_void_p(wd.data_ptr()), N, K, C.c_void_p(x.data_ptr()), M, None, None, 1e-5, None, None, 0,
+                 C.c_void_p(y.data_ptr()), sp)
+    H, T, Lk = 16, 512, 400
+    kv = torch.randn(2, M, H, T, 64, device="cuda").half()
+    qa = torch.randn(M, H * 64, device="cuda")
+    ln = torch.full((M,), Lk, dtype=torch.int32, device="cuda")
+    out = torch.empty(M, H * 64, device="cuda")
+    attn_args = (C.c_void_p(qa.data_ptr()), C.c_void_p(kv[0].data_ptr()), C.c_void_p(kv[1].data_ptr()), M, H, T,
+                 C.c_void_p(ln.data_ptr()), C.c_void_p(out.data_ptr()), sp)
+
+    def timed(fn, args):
+        for _ in range(5):
+            pkg.check(fn(*args))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            pkg.check(fn(*args))
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1000.0 / reps
+
+    g_us = timed(L.t3b_op_gemv, gemm_args)
+    a_us = timed(L.t3b_op_attention, attn_args)
+    a_bytes = M * H * Lk * 64 * 2 * 2 + M * H * 64 * 8
+    return {"gemm_q8_0_m128": {"shape": f"M={M} K={K} N={N}", "us_per_call": g_us,
+                               "int8_tops": 2.0 * M * N * K / (g_us * 1e-6) / 1e12,
+                               "note": "t3b_op_gemv = prep_act + gemm_q_mma_kernel"},
+            "attn_rows_m128": {"shape": f"M={M} heads={H} L={Lk}", "us_per_call": a_us, "bytes": a_bytes,
+                               "achieved_gbs": a_bytes / (a_us * 1e-6) / 1e9, "peak": peak,
+                               "frac": a_bytes / (a_us * 1e-6) / 1e9 / peak}}
 
 
 def phase_timeline(pkg, step=5):
