@@ -201,7 +201,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="leave out the batched CFG run (profiling commands)")
-    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels"], default=None,
+    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels", "sweep"], default=None,
                     help="run one kernel micro-benchmark alone (ncu captures), or the megakernel phase timeline")
     args = ap.parse_args()
     if args.only:
@@ -217,6 +217,9 @@ def main():
         elif args.only == "kernels":
             import torch
             r = batched_kernels(pkg, torch, peak)
+        elif args.only == "sweep":
+            import torch
+            r = gemv_sweep(pkg, torch, peak)
         else:
             r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
         print(json.dumps(r), flush=True)
@@ -310,6 +313,7 @@ def main():
             "sampler": sampler_microbench(pkg, torch, peak),
             "batched_cfg": batched_cfg(pkg, torch, peak) if rank == 0 and not args.no_batched else None,
             "batched_kernels": batched_kernels(pkg, torch, peak),
+            "gemv_sweep": gemv_sweep(pkg, torch, peak) if not args.no_batched else None,
             "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": 2,   # first-token sampler + one t3_decode_megakernel launch
             "tokens_head": [int(x) for x in toks[:8]]}
@@ -454,6 +458,55 @@ def batched_kernels(pkg, torch, peak, reps=50):
             "attn_rows_m128": {"shape": f"M={M} heads={H} L={Lk}", "us_per_call": a_us, "bytes": a_bytes,
                                "achieved_gbs": a_bytes / (a_us * 1e-6) / 1e9, "peak": peak,
                                "frac": a_bytes / (a_us * 1e-6) / 1e9 / peak}}
+
+
+def gemv_sweep(pkg, torch, peak, reps=20):
+    """the four T3 layer shapes x {Q4_0, Q8_0, F16} x
+    M in {1, 2, 8, 32, 128} through t3b_op_gemv (activation prep + GEMV for
+    M < 16, int8 tensor-core GEMM for M >= 16).  Device time per call (CUDA
+    events, weights cycled over enough copies to exceed L2), algorithmic
+    bytes N*K*{0.5625, 1.0625, 2} + M*K*4 + M*N*4."""
+    import ctypes as C
+    import gguf
+    L = pkg.lib()
+    s = torch.cuda.current_stream()
+    sp = C.c_void_p(s.cuda_stream)
+    out = []
+    for ty, name in ((2, "q4_0"), (8, "q8_0"), (1, "f16")):
+        for K, N in ((1024, 3072), (1024, 1024), (1024, 4096), (4096, 1024)):
+            w = (np.random.default_rng(K + N).standard_normal((N, K)) * 0.02).astype(np.float32)
+            if ty == 1:
+                q = np.ascontiguousarray(w.astype(np.float16))
+            else:
+                qt = {2: gguf.GGMLQuantizationType.Q4_0, 8: gguf.GGMLQuantizationType.Q8_0}[ty]
+                q = np.ascontiguousarray(gguf.quants.quantize(w, qt))
+            rb = L.t3b_op_row_bytes(ty, K)
+            copies = max(2, int(160e6 // (N * rb)) + 1)
+            wd = torch.empty((copies, N * rb), dtype=torch.uint8, device="cuda")
+            pkg.check(L.t3b_op_repack(ty, q.ctypes.data, N, K, C.c_void_p(wd[0].data_ptr())))
+            wd[1:] = wd[0]
+            for M in (1, 2, 8, 32, 128):
+                x = torch.randn(M, K, device="cuda")
+                y = torch.empty(M, N, device="cuda")
+
+                def call(i):
+                    pkg.check(L.t3b_op_gemv(ty, C.c_void_p(wd[i % copies].data_ptr()), N, K, C.c_void_p(x.data_ptr()),
+                                            M, None, None, 1e-5, None, None, 0, C.c_void_p(y.data_ptr()), sp))
+                for i in range(3):
+                    call(i)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for i in range(reps):
+                    call(i)
+                e1.record(s)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1000.0 / reps
+                byts = N * rb + M * K * 4 + M * N * 4
+                out.append([name, K, N, M, round(us, 2), round(byts / (us * 1e-6) / 1e9, 1),
+                            round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)])
+            del wd
+    return {"columns": ["type", "K", "N", "M", "us_per_call", "GB/s", "TOP/s"], "rows": out, "peak": peak,
+            "note": "t3b_op_gemv: activation prep (LN off) + GEMV (M < 16) or int8 tensor-core GEMM (M >= 16)"}
 
 
 def phase_timeline(pkg, step=5):

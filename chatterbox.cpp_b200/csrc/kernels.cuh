@@ -33,6 +33,9 @@ struct GemvEpi {
     const int * y_row;   // nullable: activation row -> output row of y
     int max_ctx; int D;
     unsigned * err;
+    // gemm_q_mma_kernel with EPI_GELU only (nullable): write the output rows
+    // re-quantised to Q8_0 (the next GEMM's activation prep) instead of y
+    int8_t * qx; float * qd; int * qs; int qK;
 };
 
 __device__ __forceinline__ void epi_store(const GemvEpi & e, int m, int n, float acc) {
@@ -377,6 +380,40 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         }
         __syncthreads();   // the buffer is refilled by the next stage's load
     }
+    if (e.qx) {
+        // bias + GELU, then Q8_0 of each row's 32-wide block (this CTA's
+        // columns are exactly one block): the tile goes through shared memory
+        float (*Tt)[GQ_BN + 1] = (float (*)[GQ_BN + 1]) & As[0][0][0];   // 64 x 33 floats fit in As[0]
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int ml = wm * 32 + mt * 16 + g + (i >> 1) * 8;
+                    const int nl = wn * 16 + nt * 8 + 2 * t + (i & 1);
+                    const float b = e.bias ? e.bias[n0 + nl] : 0.0f;
+                    Tt[ml][nl] = gelu_ggml(e.bias ? __fadd_rn(acc[mt][nt][i], b) : acc[mt][nt][i]);
+                }
+        __syncthreads();
+        const int nbk = e.qK / 32;
+        for (int ml = warp * 16; ml < warp * 16 + 16; ++ml) {
+            const int m = m0 + ml;
+            if (m >= M) break;   // uniform over the warp
+            const float v = Tt[ml][lane];
+            const float amax = warp_max(fabsf(v));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q = (int) roundf(__fmul_rn(v, id));
+            e.qx[(size_t) m * e.qK + n0 + lane] = (int8_t) q;
+            const int sq = warp_sum_i(q);
+            if (lane == 0) {
+                e.qd[(size_t) m * nbk + n0 / 32] = __half2float(__float2half_rn(d));
+                e.qs[(size_t) m * nbk + n0 / 32] = sq;
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -509,6 +546,9 @@ struct AttnArgs {
     float * out; int ldo;
     float * part; unsigned * cnt; int s_max;
     unsigned * err;
+    // attn_rows_kernel only (nullable): also write the output re-quantised
+    // to Q8_0 blocks (the out-projection's activation prep), row stride ldo
+    int8_t * qx; float * qd; int * qs;
 };
 
 __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a) {
@@ -636,43 +676,63 @@ __global__ __launch_bounds__(128) void attn_rows_kernel(AttnArgs a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = 0.0f;
     // the loop bound is uniform over the warp (every lane reaches every
-    // shuffle); a group whose key is past L contributes nothing
-    for (int jb = w * 4; jb < L; jb += 32) {
+    // shuffle); a group whose key is past L contributes nothing.  Each group
+    // takes keys j, j+16, j+32, j+48: eight 16-byte loads in flight per lane.
+    constexpr int U = 4;
+    for (int jb = w * 4; jb < L; jb += 16 * U) {
         const int j = jb + grp;
-        const bool one = j < L, two = j + 16 < L;
-        uint4 k0 = make_uint4(0u, 0u, 0u, 0u), v0 = k0, k1 = k0, v1 = k0;
-        if (one) {
-            k0 = __ldg((const uint4 *) (kb + (size_t) j * T3B_HD));
-            v0 = __ldg((const uint4 *) (vb + (size_t) j * T3B_HD));
-        }
-        if (two) {
-            k1 = __ldg((const uint4 *) (kb + (size_t) (j + 16) * T3B_HD));
-            v1 = __ldg((const uint4 *) (vb + (size_t) (j + 16) * T3B_HD));
-        }
-        const __half2 * k0h = (const __half2 *) &k0, * k1h = (const __half2 *) &k1;
-        float d0 = 0.0f, d1 = 0.0f;
+        uint4 kk[U], vv[U];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f0 = __half22float2(k0h[i]), f1 = __half22float2(k1h[i]);
-            d0 = fmaf(q[2 * i], f0.x, d0); d0 = fmaf(q[2 * i + 1], f0.y, d0);
-            d1 = fmaf(q[2 * i], f1.x, d1); d1 = fmaf(q[2 * i + 1], f1.y, d1);
+        for (int u = 0; u < U; ++u) {
+            kk[u] = make_uint4(0u, 0u, 0u, 0u);
+            vv[u] = kk[u];
+            if (j + 16 * u < L) {
+                kk[u] = __ldg((const uint4 *) (kb + (size_t) (j + 16 * u) * T3B_HD));
+                vv[u] = __ldg((const uint4 *) (vb + (size_t) (j + 16 * u) * T3B_HD));
+            }
+        }
+        float d[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const __half2 * kh = (const __half2 *) &kk[u];
+            float t = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(kh[i]);
+                t = fmaf(q[2 * i], f.x, t);
+                t = fmaf(q[2 * i + 1], f.y, t);
+            }
+            d[u] = t;
         }
 #pragma unroll
-        for (int off = 1; off < 8; off <<= 1) {
-            d0 += __shfl_xor_sync(0xffffffffu, d0, off);
-            d1 += __shfl_xor_sync(0xffffffffu, d1, off);
+        for (int off = 1; off < 8; off <<= 1)
+#pragma unroll
+            for (int u = 0; u < U; ++u) d[u] += __shfl_xor_sync(0xffffffffu, d[u], off);
+        float sc[U], nm = mx;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            sc[u] = j + 16 * u < L ? d[u] * 0.125f : -INFINITY;
+            nm = fmaxf(nm, sc[u]);
         }
-        const float s0 = one ? d0 * 0.125f : -INFINITY, s1 = two ? d1 * 0.125f : -INFINITY;
-        const float nm = fmaxf(mx, fmaxf(s0, s1));
         const float corr = mx == -INFINITY ? 0.0f : expf(mx - nm);
-        const float p0 = one ? expf(s0 - nm) : 0.0f, p1 = two ? expf(s1 - nm) : 0.0f;
-        l = l * corr + p0 + p1;
-        const __half2 * v0h = (const __half2 *) &v0, * v1h = (const __half2 *) &v1;
+        float p[U], ps = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f0 = __half22float2(v0h[i]), f1 = __half22float2(v1h[i]);
-            o[2 * i] = fmaf(p1, f1.x, fmaf(p0, f0.x, o[2 * i] * corr));
-            o[2 * i + 1] = fmaf(p1, f1.y, fmaf(p0, f0.y, o[2 * i + 1] * corr));
+        for (int u = 0; u < U; ++u) {
+            p[u] = j + 16 * u < L ? expf(sc[u] - nm) : 0.0f;
+            ps += p[u];
+        }
+        l = l * corr + ps;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] *= corr;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const __half2 * vh = (const __half2 *) &vv[u];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(vh[i]);
+                o[2 * i] = fmaf(p[u], f.x, o[2 * i]);
+                o[2 * i + 1] = fmaf(p[u], f.y, o[2 * i + 1]);
+            }
         }
         mx = nm;
     }
@@ -703,7 +763,21 @@ __global__ __launch_bounds__(128) void attn_rows_kernel(AttnArgs a) {
             lt = fmaf(wl[u], f, lt);
             ot = fmaf(wo[u][tid], f, ot);
         }
-        a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = ot / lt;
+        const float v = ot / lt;
+        a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = v;
+        if (a.qx) {   // warps 0 and 1: Q8_0 blocks 2h and 2h + 1 of row m
+            const float amax = warp_max(fabsf(v));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q = (int) roundf(__fmul_rn(v, id));
+            a.qx[(size_t) m * a.ldo + h * T3B_HD + tid] = (int8_t) q;
+            const int sq = warp_sum_i(q);
+            if (lane == 0) {
+                const int blk = (size_t) m * (a.ldo / 32) + h * 2 + w;
+                a.qd[blk] = __half2float(__float2half_rn(d));
+                a.qs[blk] = sq;
+            }
+        }
     }
 }
 

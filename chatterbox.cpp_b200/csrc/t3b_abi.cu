@@ -175,6 +175,7 @@ struct t3b_ctx {
     float * x = nullptr, * qkv = nullptr, * attn = nullptr, * h = nullptr, * logits = nullptr, * part = nullptr;
     float * spk = nullptr;
     int8_t * xq = nullptr; float * xd = nullptr; int * xs = nullptr; __half * xh = nullptr;
+    int8_t * xq2 = nullptr; float * xd2 = nullptr; int * xs2 = nullptr;   // fc2 input written by the fc GEMM
     unsigned * cnt = nullptr;
     int * row_slot = nullptr, * pos = nullptr, * row_of = nullptr, * y_row = nullptr;
     int * pk_kind = nullptr, * pk_id = nullptr, * slot_list = nullptr;
@@ -310,17 +311,26 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         a.kv = ctx->kv; a.row_elems = ctx->row_elems; a.layer_off = e.layer_off; a.v_off = e.v_off;
         a.row_of = row_of; a.len = pos; a.len_add = 1; a.max_ctx = ctx->max_ctx; a.n_head = H;
         a.out = ctx->attn; a.ldo = D; a.part = ctx->part; a.cnt = ctx->cnt; a.s_max = ctx->s_max; a.err = ctx->err_word;
+        // many rows: the attention kernel writes the proj GEMM's Q8_0 input itself
+        const bool q_attn = M >= T3B_ATTN_ROWS_MIN && Ly.proj.type != T3B_F16;
+        if (q_attn) { a.qx = ctx->xq; a.qd = ctx->xd; a.qs = ctx->xs; }
         if (M >= T3B_ATTN_ROWS_MIN) attn_rows_kernel<<<dim3(H, M), 128, 0, st>>>(a);
         else attn_decode_kernel<<<dim3(H, M, ctx->s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
         // proj + bias + residual
-        launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
+        if (!q_attn) launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
         launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_RESID, ctx->x, D, Ly.proj_b, ctx->x, D), st);
-        // LN2 + fc + GELU
+        // LN2 + fc + GELU; with the tensor-core GEMM (M >= 16) its epilogue
+        // writes fc2's Q8_0 input (separate buffers: fc is still reading xq)
         launch_prep(ctx, ctx->x, D, M, D, Ly.ln2g, Ly.ln2b, Ly.fc.type, st);
-        launch_gemv(Ly.fc, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_GELU, ctx->h, 4 * D, Ly.fc_b, nullptr, 0), st);
+        GemvEpi ef = epi_plain(EPI_GELU, ctx->h, 4 * D, Ly.fc_b, nullptr, 0);
+        const bool q_fc = M >= 16 && Ly.fc.type != T3B_F16 && Ly.fc2.type != T3B_F16 &&
+                          Ly.fc.K % (32 * GQ_KB) == 0 && (4 * D) % GQ_BN == 0;
+        if (q_fc) { ef.qx = ctx->xq2; ef.qd = ctx->xd2; ef.qs = ctx->xs2; ef.qK = 4 * D; }
+        launch_gemv(Ly.fc, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ef, st);
         // fc2 + bias + residual
-        launch_prep(ctx, ctx->h, 4 * D, M, 4 * D, nullptr, nullptr, Ly.fc2.type, st);
-        launch_gemv(Ly.fc2, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D), st);
+        if (!q_fc) launch_prep(ctx, ctx->h, 4 * D, M, 4 * D, nullptr, nullptr, Ly.fc2.type, st);
+        launch_gemv(Ly.fc2, q_fc ? ctx->xq2 : ctx->xq, q_fc ? ctx->xd2 : ctx->xd, q_fc ? ctx->xs2 : ctx->xs, ctx->xh, M,
+                    epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D), st);
     }
     if (head_rows > 0) {
         launch_prep(ctx, ctx->x + (size_t) head_first * D, D, head_rows, D, ctx->lnf_g, ctx->lnf_b, ctx->head.type, st);
@@ -526,6 +536,7 @@ int t3b_stream_alloc(t3b_ctx * ctx, int n_streams, int max_ctx, int cfg) {
     A(&ctx->x, (size_t) R * D); A(&ctx->qkv, (size_t) R * 3 * D); A(&ctx->attn, (size_t) R * D); A(&ctx->h, (size_t) R * 4 * D);
     A(&ctx->logits, (size_t) rows * V); A(&ctx->spk, D);
     A(&ctx->xq, (size_t) R * 4 * D); A(&ctx->xd, (size_t) R * 4 * D / 32); A(&ctx->xs, (size_t) R * 4 * D / 32); A(&ctx->xh, (size_t) R * 4 * D);
+    A(&ctx->xq2, (size_t) R * 4 * D); A(&ctx->xd2, (size_t) R * 4 * D / 32); A(&ctx->xs2, (size_t) R * 4 * D / 32);
     A(&ctx->part, (size_t) R * H * ctx->s_max * (T3B_HD + 2)); A(&ctx->cnt, (size_t) R * H);
     A(&ctx->row_slot, R); A(&ctx->pos, R); A(&ctx->row_of, R); A(&ctx->y_row, R);
     A(&ctx->pk_kind, R); A(&ctx->pk_id, R);
