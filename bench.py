@@ -136,7 +136,7 @@ def cpu_reference(args, hp, t, text, label_impl):
     as fit in ~12 s (at least 4), after an untimed prefill."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
-    cores = os.cpu_count() or 1
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     oracle.set_threads(cores)
     m = oracle.Model(hp, t, max_ctx=150 + max(args.steps, 64) + 8, gemv_mode=1, gelu_f16=1, kv_f16=0)
     P, lg = m.prompt(text)
@@ -317,7 +317,7 @@ def main():
             "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": 2,   # first-token sampler + one t3_decode_megakernel launch
             "tokens_head": [int(x) for x in toks[:8]]}
-    if rank == 0 and not args.no_cpu_baseline:
+    if ws == 1 and not args.no_cpu_baseline:   # the CPU baseline is measured at N = 1 only
         line["cpu_baseline"] = cpu_reference(args, hp, t, text, "port")
     if rank == 0:
         print(json.dumps(line), flush=True)
