@@ -49,6 +49,7 @@
 #define MK_B_TOTAL (MK_B_PART + 16 * 1024)
 enum { MK_C_QKV, MK_C_ATT, MK_C_XM, MK_C_H, MK_C_X, MK_C_LOG, MK_C_TOK, MK_C_N };
 #define MK_C_STRIDE 32   // counters 128 bytes apart
+#define MK_CTL_WORDS ((MK_C_N + 2) * MK_C_STRIDE)   // counters, abort flag, steps done
 
 struct MkMat { const uint8_t * w; int type; int rb; };
 struct MkLayer {
@@ -72,6 +73,7 @@ struct MegaArgs {
     int sample;                    // 0: stop after the head (eval_step without sampling)
     unsigned long long * tl;       // nullable: [G][MK_TL] globaltimer stamps of step tl_step
     int tl_step;
+    int first_tok;                 // token of the first step (< 0: the stream's step_tok)
     SampArgs samp;
 };
 #define MK_TL 512
@@ -91,9 +93,7 @@ struct MegaState {
 inline void mega_free(MegaState & m) {
     if (m.layers) cudaFree(m.layers);
     if (m.buf) cudaFree(m.buf);
-    if (m.cnt) cudaFree(m.cnt);
-    if (m.abort_flag) cudaFree(m.abort_flag);
-    if (m.steps_done) cudaFree(m.steps_done);
+    if (m.cnt) cudaFree(m.cnt);   // abort_flag and steps_done live in the same block
     if (m.cancel_host) cudaFreeHost(m.cancel_host);
     m = MegaState();
 }
@@ -490,7 +490,16 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     float * bPART = a.buf + MK_B_PART;
     int * bTOK = (int *) (a.buf + MK_B_TOK);
 
-    int tok = a.samp.step_tok[a.samp.slot_of ? a.samp.slot_of[0] : 0];
+    int tok;
+    {
+        const int slot0 = a.samp.slot_of ? a.samp.slot_of[0] : 0;
+        if (a.first_tok >= 0) {
+            tok = a.first_tok;
+            if (cta == 0 && tid == 0) a.samp.step_tok[slot0] = tok;   // the stream's last input token
+        } else {
+            tok = a.samp.step_tok[slot0];
+        }
+    }
     for (int step = 0; step < a.n_steps; ++step) {
         // host cancel flag (mapped memory, a PCIe round trip): one thread of
         // CTA 0 reads it at the start of the step; the value is needed only

@@ -155,6 +155,7 @@ struct t3b_ctx {
     std::vector<int32_t> builtin_cond;
     ExpFix fx{};
     unsigned * err_word = nullptr;
+    unsigned * err_pin = nullptr;   // pinned host copy of err_word (read in the same synchronize as results)
     volatile int cancel = 0;
     float last_ms = 0.0f;
 
@@ -179,6 +180,7 @@ struct t3b_ctx {
     unsigned * cnt = nullptr;
     int * row_slot = nullptr, * pos = nullptr, * row_of = nullptr, * y_row = nullptr;
     int * pk_kind = nullptr, * pk_id = nullptr, * slot_list = nullptr;
+    std::vector<int> maps_slots;    // slot list row_slot/row_of/slot_list hold (empty: unknown)
     // captured step graphs keyed by the slot list (+ whether sampling)
     std::map<std::vector<int>, StepGraph> graphs;
     // persistent batch-1 decode kernel state
@@ -226,6 +228,7 @@ void free_streams(t3b_ctx * ctx) {
         if (kv.second.g) cudaGraphDestroy(kv.second.g);
     }
     ctx->graphs.clear();
+    ctx->maps_slots.clear();
     for (void * p : ctx->sallocs) cudaFree(p);
     ctx->sallocs.clear();
     ctx->S = 0; ctx->R = 0; ctx->kv = nullptr;
@@ -380,6 +383,8 @@ t3b_ctx * t3b_create(int device, const t3b_model_desc * desc) {
         return fail("sampler shared memory attribute");
     if (dalloc(ctx, ctx->allocs, &ctx->err_word, 1) != T3B_OK) return fail("alloc");
     cudaMemset(ctx->err_word, 0, sizeof(unsigned));
+    if (cudaHostAlloc((void **) &ctx->err_pin, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess) return fail("alloc");
+    *ctx->err_pin = 0u;
 
     const int D = hp.n_embd;
     auto upload = [&](const t3b_tensor & t, size_t bytes, void ** dst) -> int {
@@ -478,6 +483,7 @@ void t3b_destroy(t3b_ctx * ctx) {
     for (void * p : ctx->allocs) cudaFree(p);
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
+    if (ctx->err_pin) cudaFreeHost(ctx->err_pin);
     if (ctx->st) cudaStreamDestroy(ctx->st);
     delete ctx;
 }
@@ -648,6 +654,7 @@ int t3b_prefill(t3b_ctx * ctx, int stream, const int32_t * text, int n_text, con
             for (int i = 0; i < n; ++i) pos[i] = c0 + i;
             CK(cudaMemcpyAsync(ctx->pk_kind, kj.data() + c0, sizeof(int) * n, cudaMemcpyHostToDevice, st));
             CK(cudaMemcpyAsync(ctx->pk_id, id.data() + c0, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+            ctx->maps_slots.clear();
             CK(cudaMemcpyAsync(ctx->row_of, rowof.data(), sizeof(int) * n, cudaMemcpyHostToDevice, st));
             CK(cudaMemcpyAsync(ctx->pos, pos.data(), sizeof(int) * n, cudaMemcpyHostToDevice, st));
             embed_prompt_kernel<<<n, 256, 0, st>>>(ctx->semb, ctx->temb, ctx->wpe, ctx->spk, ctx->pk_kind, ctx->pk_id, c0, D, ctx->x);
@@ -680,6 +687,7 @@ namespace {
 // positions from device buffers, so one graph serves any n streams;
 // upload_maps() fills the maps before a launch.
 int upload_maps(t3b_ctx * ctx, const std::vector<int> & slots) {
+    if (!ctx->maps_slots.empty() && ctx->maps_slots == slots) return T3B_OK;   // already on the device
     const int n = (int) slots.size(), M = n * ctx->rps;
     std::vector<int> row_slot(M), row_of(M);
     for (int i = 0; i < n; ++i)
@@ -691,6 +699,7 @@ int upload_maps(t3b_ctx * ctx, const std::vector<int> & slots) {
     CK(cudaMemcpyAsync(ctx->row_of, row_of.data(), sizeof(int) * M, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemcpyAsync(ctx->slot_list, slots.data(), sizeof(int) * n, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaStreamSynchronize(ctx->st));
+    ctx->maps_slots = slots;
     return T3B_OK;
 }
 
@@ -779,9 +788,10 @@ int mega_prepare(t3b_ctx * ctx) {
     CK(cudaMalloc(&m.layers, sizeof(MkLayer) * hl.size()));
     CK(cudaMemcpy(m.layers, hl.data(), sizeof(MkLayer) * hl.size(), cudaMemcpyHostToDevice));
     CK(cudaMalloc(&m.buf, sizeof(float) * MK_B_TOTAL));
-    CK(cudaMalloc(&m.cnt, sizeof(unsigned) * MK_C_N * MK_C_STRIDE));
-    CK(cudaMalloc(&m.abort_flag, sizeof(int)));
-    CK(cudaMalloc(&m.steps_done, sizeof(int)));
+    // counters | abort flag | steps done, each on its own 128-byte line: one memset per launch
+    CK(cudaMalloc(&m.cnt, sizeof(unsigned) * MK_CTL_WORDS));
+    m.abort_flag = (int *) (m.cnt + MK_C_N * MK_C_STRIDE);
+    m.steps_done = (int *) (m.cnt + (MK_C_N + 1) * MK_C_STRIDE);
     CK(cudaHostAlloc(&m.cancel_host, sizeof(int), cudaHostAllocMapped));
     *m.cancel_host = 0;
     CK(cudaHostGetDevicePointer(&m.cancel_dev, m.cancel_host, 0));
@@ -802,7 +812,8 @@ int mega_prepare(t3b_ctx * ctx) {
 // One cooperative launch decoding max_steps steps of stream `slot` (row
 // slot).  The first token is already in step_tok (sampled from the prefill
 // logits).  Returns the number of steps run in *steps.
-int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop, int * steps, float * logits_out = nullptr) {
+int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop, int * steps, float * logits_out = nullptr,
+                int first_tok = -1) {
     MegaState & m = ctx->mega;
     cudaStream_t st = ctx->st;
     const int H = ctx->hp.n_head;
@@ -823,9 +834,8 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     a.sample = logits_out == nullptr;
     a.samp = sampler_args(ctx, false);
     a.samp.done = nullptr;
-    CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_C_N * MK_C_STRIDE, st));
-    CK(cudaMemsetAsync(m.abort_flag, 0, sizeof(int), st));
-    CK(cudaMemsetAsync(m.steps_done, 0, sizeof(int), st));
+    a.first_tok = first_tok;
+    CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_CTL_WORDS, st));
     // debug: T3B_MK_TIMELINE=<file> stamps every phase boundary of step
     // T3B_MK_TIMELINE_STEP (default 2) per CTA and writes [G][256] u64 ns
     const char * tl_file = getenv("T3B_MK_TIMELINE");
@@ -892,17 +902,17 @@ int t3b_step(t3b_ctx * ctx, int n, const int32_t * streams, const int32_t * toke
         // eval_step of one stream: one persistent-kernel step, logits only
         rc = upload_maps(ctx, slots);
         if (rc != T3B_OK) return rc;
-        CK(cudaMemcpyAsync(ctx->step_tok + slots[0], tokens, sizeof(int), cudaMemcpyHostToDevice, st));
         float * dst = ctx->logits + (size_t) slots[0] * V;
         CK(cudaEventRecord(ctx->ev0, st));
-        rc = mega_decode(ctx, slots[0], p_first, 1, 1, nullptr, dst);
+        rc = mega_decode(ctx, slots[0], p_first, 1, 1, nullptr, dst, tokens[0]);
         if (rc != T3B_OK) return rc;
         CK(cudaEventRecord(ctx->ev1, st));
         if (logits_out) CK(cudaMemcpyAsync(logits_out, dst, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(ctx->err_pin, ctx->err_word, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
         cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1);
         ctx->pos_host[slots[0]] = p_first + 1;
-        return check_dev_err(ctx);
+        return *ctx->err_pin ? check_dev_err(ctx) : T3B_OK;
     }
     StepGraph * g = nullptr;
     rc = ensure_graph(ctx, n, false, &g);
@@ -946,6 +956,7 @@ int t3b_sample(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
             CK(cudaMemcpyAsync(ctx->logits + (size_t) slots[i] * ctx->rps * V, logits + (size_t) i * ctx->rps * V,
                                sizeof(float) * ctx->rps * V, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(ctx->params, params, sizeof(t3b_sample_params) * n, cudaMemcpyHostToDevice, st));
+    ctx->maps_slots.clear();
     CK(cudaMemcpyAsync(ctx->slot_list, slots.data(), sizeof(int) * n, cudaMemcpyHostToDevice, st));
     SampArgs a = sampler_args(ctx, false);
     CK(cudaEventRecord(ctx->ev0, st));
