@@ -46,7 +46,10 @@
 #define MK_B_LOG (MK_B_X + 1024)
 #define MK_B_TOK (MK_B_LOG + T3B_SAMPLER_VMAX)
 #define MK_B_PART (MK_B_TOK + 32)          // [16 heads][1024] out-projection partials
-#define MK_B_TOTAL (MK_B_PART + 16 * 1024)
+#define MK_B_HQ (MK_B_PART + 16 * 1024)     // fc output h in Q8_0: quants [4096] i8
+#define MK_B_HD (MK_B_HQ + 1024)            //   block scales [128]
+#define MK_B_HS (MK_B_HD + 128)             //   block sums [128]
+#define MK_B_TOTAL (MK_B_HS + 128)
 enum { MK_C_QKV, MK_C_ATT, MK_C_XM, MK_C_H, MK_C_X, MK_C_LOG, MK_C_TOK, MK_C_N };
 #define MK_C_STRIDE 32   // counters 128 bytes apart
 #define MK_CTL_WORDS ((MK_C_N + 2) * MK_C_STRIDE)   // counters, abort flag, steps done
@@ -154,15 +157,13 @@ __device__ __forceinline__ bool mk_wait_vec(const unsigned * c, unsigned target,
     return true;
 }
 
-// LayerNorm parameters of this thread's two elements, loaded before a wait
-struct MkLn { float g[2], b[2]; };
+// LayerNorm parameters of this thread's two elements (2*tid, 2*tid+1),
+// loaded before a wait
+struct MkLn { float2 g, b; };
 __device__ __forceinline__ MkLn mk_ln_prefetch(const float * g, const float * b) {
     MkLn p;
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        p.g[u] = __ldg(g + threadIdx.x + u * MK_THREADS);
-        p.b[u] = __ldg(b + threadIdx.x + u * MK_THREADS);
-    }
+    p.g = __ldg((const float2 *) g + threadIdx.x);
+    p.b = __ldg((const float2 *) b + threadIdx.x);
     return p;
 }
 
@@ -206,22 +207,38 @@ __device__ __forceinline__ double2 mk_block_sum_d2(double a, double b, double * 
     return make_double2(ra, rb);
 }
 
-// LayerNorm of the 1024-vector v in place (two elements per thread).  Mean
-// and variance come from one reduction of sum(x) and sum(x^2) in double
-// (var = E[x^2] - mean^2), which differs from ggml's two-pass float form only
-// in the last bits of the statistics.
-__device__ void mk_layernorm(float * v, const MkLn & p, float eps, double * redd) {
+// LayerNorm of a 1024-vector followed by its Q8_0 re-quantisation (or f16
+// rounding for F16 weights), x0/x1 = elements 2*tid and 2*tid+1 held in
+// registers.  Mean and variance come from one reduction of sum(x) and
+// sum(x^2) in double (var = E[x^2] - mean^2), which differs from ggml's
+// two-pass float form only in the last bits of the statistics.  Each thread
+// quantises the two elements it normalised: 16 lanes share a 32-element
+// block, so the normalised vector never goes through shared memory.
+__device__ void mk_ln_quant(float x0, float x1, const MkLn & p, float eps, double * redd, const MkAct & x, bool f16) {
     const int tid = threadIdx.x, K = 2 * MK_THREADS;
-    const float x0 = v[tid], x1 = v[tid + MK_THREADS];
     const double d0 = x0, d1 = x1;
     const double2 m = mk_block_sum_d2(d0 + d1, d0 * d0 + d1 * d1, redd);
     const double meand = m.x / K;
     const float mean = (float) meand;
     const float var = (float) fmax(m.y / K - meand * meand, 0.0);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-    const float t0 = __fsub_rn(x0, mean), t1 = __fsub_rn(x1, mean);
-    v[tid] = __fadd_rn(__fmul_rn(__fmul_rn(t0, scale), p.g[0]), p.b[0]);
-    v[tid + MK_THREADS] = __fadd_rn(__fmul_rn(__fmul_rn(t1, scale), p.g[1]), p.b[1]);
+    const float y0 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x0, mean), scale), p.g.x), p.b.x);
+    const float y1 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x1, mean), scale), p.g.y), p.b.y);
+    if (f16) {
+        *(__half2 *) (x.h + 2 * tid) = __halves2half2(__float2half_rn(y0), __float2half_rn(y1));
+    } else {
+        float mx = fmaxf(fabsf(y0), fabsf(y1));
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float d = __fdiv_rn(mx, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const int q0 = (int) roundf(__fmul_rn(y0, id)), q1 = (int) roundf(__fmul_rn(y1, id));
+        *(short *) (x.q + 2 * tid) = (short) ((q0 & 0xff) | ((q1 & 0xff) << 8));
+        int s = q0 + q1;
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if ((tid & 15) == 0) { x.d[tid >> 4] = __half2float(__float2half_rn(d)); x.s[tid >> 4] = s; }
+    }
     __syncthreads();
 }
 
@@ -408,11 +425,11 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
     const MkLn lp = mk_ln_prefetch(a.lnfg, a.lnfb);
     const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
-    if (!mk_wait_vec(a.cnt + MK_C_X * MK_C_STRIDE, kx * G, a.buf + MK_B_X, D, vec, a)) return false;
+    if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * G, a)) return false;
+    const float2 xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
     const int cta = blockIdx.x;
     MK_STAMP(487);
-    mk_layernorm(vec, lp, a.eps, redd);
-    mk_quantize(act, D, HT == T3B_F16);
+    mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, HT == T3B_F16);
     mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
     MK_STAMP(488);
     float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
@@ -433,18 +450,25 @@ constexpr size_t mk_smem_bytes() {
     return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 1024 + 128) * 4;   // + head outputs and their Q8_0
 }
 static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
+static_assert(MK_THREADS == 512, "LayerNorm and the h hand-off assume two elements of a 1024-vector per thread");
 
 // Bulk prefetch of a CTA's weight slice into L2 (one instruction, no
 // completion to track): issued one phase ahead so the register prefetch of
 // that phase hits L2 instead of HBM.
-__device__ __forceinline__ void mk_l2_prefetch(const MkMat & W, int N) {
+__device__ __forceinline__ void mk_l2_prefetch_rows(const MkMat & W, int r0, int r1) {
     if (threadIdx.x == 0) {
-        const int r0 = mk_r0(N, blockIdx.x, gridDim.x), r1 = mk_r0(N, blockIdx.x + 1, gridDim.x);
         const unsigned bytes = (unsigned) ((r1 - r0) * W.rb);
         if (bytes >= 16u)
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(W.w + (size_t) r0 * W.rb), "r"(bytes & ~15u)
                          : "memory");
     }
+}
+__device__ __forceinline__ void mk_l2_prefetch(const MkMat & W, int N) {
+    mk_l2_prefetch_rows(W, mk_r0(N, blockIdx.x, gridDim.x), mk_r0(N, blockIdx.x + 1, gridDim.x));
+}
+// fc rows of a CTA: whole 32-row blocks when the CTA publishes h in Q8_0
+__device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
+    return blocks ? mk_r0(128, c, G) * 32 : mk_r0(4096, c, G);
 }
 
 // rows of one GEMV phase: prefetch (before the caller's wait)
@@ -488,6 +512,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     float * bQKV = a.buf + MK_B_QKV, * bATT = a.buf + MK_B_ATT, * bXM = a.buf + MK_B_XM;
     float * bH = a.buf + MK_B_H, * bX = a.buf + MK_B_X, * bLOG = a.buf + MK_B_LOG;
     float * bPART = a.buf + MK_B_PART;
+    int8_t * bHQ = (int8_t *) (a.buf + MK_B_HQ);
+    float * bHD = a.buf + MK_B_HD;
+    int * bHS = (int *) (a.buf + MK_B_HS);
     int * bTOK = (int *) (a.buf + MK_B_TOK);
 
     int tok;
@@ -517,19 +544,23 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
             {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
-                if (FUSE) mk_l2_prefetch(Ly.fc, 4 * D);   // the next GEMV this CTA runs is P4's
+                if (FUSE) mk_l2_prefetch_rows(Ly.fc, mk_fc_r0(cta, G, true), mk_fc_r0(cta + 1, G, true));   // P4's rows
                 else mk_l2_prefetch(Ly.o, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bqkv + r0_ + tid) : 0.0f;
                 MK_STAMP(l * 20 + 0);
-                if (l > 0 && !mk_wait_vec(cX, (k - 1u) * G, bX, D, xres, a)) return;
+                // layer input: this thread's elements 2*tid, 2*tid+1 (the
+                // embedding of layer 0 is already in xres)
+                float2 xv;
+                if (l > 0) {
+                    if (!mk_acquire(cX, (k - 1u) * G, a)) return;
+                    xv = __ldcg((const float2 *) bX + tid);
+                    *(float2 *) (xres + 2 * tid) = xv;
+                } else {
+                    xv = *(const float2 *) (xres + 2 * tid);
+                }
                 MK_STAMP(l * 20 + 1);
-                for (int i = tid; i < D; i += MK_THREADS) vec[i] = xres[i];
-                __syncthreads();
-                MK_STAMP(l * 20 + 12);
-                mk_layernorm(vec, lp, a.eps, redd);
-                MK_STAMP(l * 20 + 13);
-                mk_quantize(act, D, T == T3B_F16);
+                mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, T == T3B_F16);
                 MK_STAMP(l * 20 + 14);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
                 MK_STAMP(l * 20 + 15);
@@ -747,39 +778,66 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             }
             // ---------------- P4: LN2 + fc + GELU ------------------------------
             {
-                MK_GEMV_BEGIN(Ly.fc, D, 4 * D)
+                // with the fused out-projection each CTA owns whole 32-row
+                // blocks of fc (128 blocks: on 148 SMs, one block or none)
+                // and publishes its slice of h already in Q8_0, which is
+                // fc2's input; the F16 path publishes h as floats
+                const int r0_ = mk_fc_r0(cta, G, FUSE), r1_ = mk_fc_r0(cta + 1, G, FUSE);
+                MkPref<T> pf_;
+                mk_prefetch<T>(Ly.fc, D, r0_, r1_, pf_);
                 mk_l2_prefetch(Ly.fc2, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
+                float x0, x1;   // x_mid elements 2*tid, 2*tid+1
                 if (FUSE) {
                     // x_mid = (sum over heads of the partials) + proj bias + x,
                     // heads added in order 0..15
-                    const float bo0 = __ldg(Ly.bo + tid), bo1 = __ldg(Ly.bo + tid + MK_THREADS);
+                    const float2 bo = __ldg((const float2 *) Ly.bo + tid);
                     if (!mk_acquire(cATT, k * Hn, a)) return;
-                    float p0[16], p1[16];
+                    float2 p[16];
 #pragma unroll
-                    for (int hh = 0; hh < 16; ++hh) {
-                        p0[hh] = __ldcg(bPART + hh * D + tid);
-                        p1[hh] = __ldcg(bPART + hh * D + tid + MK_THREADS);
-                    }
-                    float s0 = p0[0], s1 = p1[0];
+                    for (int hh = 0; hh < 16; ++hh) p[hh] = __ldcg((const float2 *) (bPART + hh * D) + tid);
+                    x0 = p[0].x; x1 = p[0].y;
 #pragma unroll
-                    for (int hh = 1; hh < 16; ++hh) { s0 = __fadd_rn(s0, p0[hh]); s1 = __fadd_rn(s1, p1[hh]); }
-                    s0 = __fadd_rn(__fadd_rn(s0, bo0), xres[tid]);
-                    s1 = __fadd_rn(__fadd_rn(s1, bo1), xres[tid + MK_THREADS]);
-                    xmid[tid] = s0; xmid[tid + MK_THREADS] = s1;
-                    vec[tid] = s0; vec[tid + MK_THREADS] = s1;
-                    __syncthreads();
+                    for (int hh = 1; hh < 16; ++hh) { x0 = __fadd_rn(x0, p[hh].x); x1 = __fadd_rn(x1, p[hh].y); }
+                    const float2 xr = *(const float2 *) (xres + 2 * tid);
+                    x0 = __fadd_rn(__fadd_rn(x0, bo.x), xr.x);
+                    x1 = __fadd_rn(__fadd_rn(x1, bo.y), xr.y);
                 } else {
-                    if (!mk_wait_vec(cXM, k * G, bXM, D, xmid, a)) return;
-                    for (int i = tid; i < D; i += MK_THREADS) vec[i] = xmid[i];
-                    __syncthreads();
+                    if (!mk_acquire(cXM, k * G, a)) return;
+                    const float2 xm = __ldcg((const float2 *) bXM + tid);
+                    x0 = xm.x; x1 = xm.y;
                 }
+                *(float2 *) (xmid + 2 * tid) = make_float2(x0, x1);   // P5's residual (read after barriers)
                 MK_STAMP(l * 20 + 6);
-                mk_layernorm(vec, lp, a.eps, redd);
-                mk_quantize(act, D, T == T3B_F16);
-                mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
-                if (tid < r1_ - r0_) bH[r0_ + tid] = gelu_ggml(__fadd_rn(rowsum[tid], bias));
+                if (r1_ > r0_) {   // CTA-uniform
+                    mk_ln_quant(x0, x1, lp, a.eps, redd, act, T == T3B_F16);
+                    mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                    if (FUSE) {
+                        // warp w: GELU of block w of this CTA's rows, then
+                        // Q8_0 with the arithmetic of mk_quant_block
+                        const int w = tid >> 5, lane = tid & 31;
+                        if (w < (r1_ - r0_) / 32) {
+                            const float v = gelu_ggml(__fadd_rn(rowsum[tid], bias));
+                            float mx = fabsf(v);
+#pragma unroll
+                            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                            const float d = __fdiv_rn(mx, 127.0f);
+                            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                            const int q = (int) roundf(__fmul_rn(v, id));
+                            int sq = q;
+#pragma unroll
+                            for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                            bHQ[r0_ + tid] = (int8_t) q;
+                            if (lane == 0) {
+                                bHD[(r0_ >> 5) + w] = __half2float(__float2half_rn(d));
+                                bHS[(r0_ >> 5) + w] = sq;
+                            }
+                        }
+                    } else if (tid < r1_ - r0_) {
+                        bH[r0_ + tid] = gelu_ggml(__fadd_rn(rowsum[tid], bias));
+                    }
+                }
                 mk_release(cH);
             }
             // ---------------- P5: fc2 + bias + residual ------------------------
@@ -788,9 +846,19 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 if (l + 1 < NL) mk_l2_prefetch(a.layers[l + 1].qkv, 3 * D);
                 else mk_l2_prefetch(a.head, a.V);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
-                if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
-                MK_STAMP(l * 20 + 7);
-                mk_quantize(act, 4 * D, T == T3B_F16);
+                if (FUSE) {
+                    // h arrives in Q8_0: 4096 quants, 128 scales, 128 sums
+                    if (!mk_acquire(cH, k * G, a)) return;
+                    if (tid < 256) *(int4 *) (act.q + 16 * tid) = __ldcg((const int4 *) bHQ + tid);
+                    else if (tid < 384) act.d[tid - 256] = __ldcg(bHD + tid - 256);
+                    else act.s[tid - 384] = __ldcg(bHS + tid - 384);
+                    __syncthreads();
+                    MK_STAMP(l * 20 + 7);
+                } else {
+                    if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
+                    MK_STAMP(l * 20 + 7);
+                    mk_quantize(act, 4 * D, true);
+                }
                 MK_STAMP(l * 20 + 10);
                 mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
                 MK_STAMP(l * 20 + 11);

@@ -771,7 +771,8 @@ int mega_prepare(t3b_ctx * ctx) {
     // per thread) and of the row scratch
     if (cdiv(3 * 1024, G) * 32 > MK_MAXI * MK_THREADS || cdiv(4 * 1024, G) * 32 > MK_MAXI * MK_THREADS ||
         cdiv(1024, G) * 128 > MK_MAXI * MK_THREADS || cdiv(ctx->hp.n_speech_vocab, G) * 32 > MK_MAXI * MK_THREADS ||
-        cdiv(ctx->hp.n_speech_vocab, G) > 128 || G < 16) {
+        cdiv(ctx->hp.n_speech_vocab, G) > 128 || G < 16 ||
+        (ctx->L[0].fc.type != T3B_F16 && cdiv(128, G) * 32 * 32 > MK_MAXI * MK_THREADS)) {   // fc in 32-row blocks
         set_err(&ctx->err, "megakernel: %d SMs too few for the row split", G);
         return T3B_ERR_STATE;
     }
