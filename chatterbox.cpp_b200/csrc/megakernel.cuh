@@ -416,7 +416,7 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 
 // LN_f + speech_head rows of this CTA; the head keeps its own weight type.
 template <int HT>
-__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, const MkAct & act, float * part,
+__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const MkAct & act, float * part,
                                      float * rowsum, double * redd) {
     const int D = 1024, tid = threadIdx.x, G = gridDim.x;
     const int r0 = mk_r0(a.V, blockIdx.x, G), r1 = mk_r0(a.V, blockIdx.x + 1, G);
@@ -425,7 +425,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
     const MkLn lp = mk_ln_prefetch(a.lnfg, a.lnfb);
     const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
-    if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * G, a)) return false;
+    if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
     const float2 xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
     const int cta = blockIdx.x;
     MK_STAMP(487);
@@ -445,12 +445,116 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, float * vec, 
     return true;
 }
 
-// Dynamic shared memory the megakernel needs.
+// Dynamic shared memory.  Q4_0 layers (the attention CTAs compute their
+// head's q/k/v rows from weights staged in shared memory):
+//   attention scratch | GEMV scratch | K rows | q/k/v weights, then V rows.
+// Q8_0 / F16 layers: K rows | V rows | attention scratch, the GEMV scratch
+// overlapping the K rows.
+#define MK_ATT_BYTES ((256 + MK_MAX_POS + 1024 + 128) * 4)   // q/k/v[192] | p[MK_MAX_POS] | o[16][64] | head out[64] + Q8_0
+#define MK_SCR_BYTES 8192                                     // Q8_0 of a 4096-vector, f16 copy of a 1024-vector, dot partials
+#define MK_KV_BYTES (MK_MAX_POS * T3B_HD * 2)
+#define MK_QKVW_ROW 576                                       // Q4_0 row of K = 1024: 512 quant bytes + 32 f16 scales
+#define MK_QKVW_BYTES (3 * T3B_HD * MK_QKVW_ROW)
 constexpr size_t mk_smem_bytes() {
-    return (size_t) 2 * MK_MAX_POS * T3B_HD * 2 + (256 + MK_MAX_POS + 1024 + 128) * 4;   // + head outputs and their Q8_0
+    return (size_t) MK_ATT_BYTES + MK_SCR_BYTES + MK_KV_BYTES + (MK_QKVW_BYTES > MK_KV_BYTES ? MK_QKVW_BYTES : MK_KV_BYTES);
 }
-static_assert(mk_smem_bytes() >= T3B_SAMPLER_SMEM + T3B_SAMPLER_VMAX * 4, "sampler staging must fit");
-static_assert(MK_THREADS == 512, "LayerNorm and the h hand-off assume two elements of a 1024-vector per thread");
+static_assert(mk_smem_bytes() >= 2 * MK_KV_BYTES + MK_ATT_BYTES, "K/V stage layout must fit");
+static_assert(4096 + 1024 + 2048 + MK_MAXI * MK_THREADS / 32 * 4 <= MK_SCR_BYTES, "GEMV scratch must fit");
+
+// cp.async of n K or V rows (64 f16 each) into shared memory
+__device__ __forceinline__ void mk_stage_kv(__half * dst, const __half * src, int n) {
+    const int nchunk = n * (T3B_HD * 2 / 16);
+    const unsigned d0 = (unsigned) __cvta_generic_to_shared(dst);
+    for (int i = threadIdx.x; i < nchunk; i += MK_THREADS)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + i * 16), "l"(src + i * 8) : "memory");
+}
+__device__ __forceinline__ void mk_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// --- bulk copies (TMA engine, no multicast) completing on an mbarrier -------
+__device__ __forceinline__ unsigned mk_saddr(const void * p) { return (unsigned) __cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mk_mbar_init(unsigned long long * mb) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mk_saddr(mb)) : "memory");
+}
+// the phase's single arrival, announcing `bytes` of copies that complete on mb
+__device__ __forceinline__ void mk_mbar_expect(unsigned long long * mb, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mk_saddr(mb)), "r"(bytes) : "memory");
+}
+// bytes: multiple of 16; both addresses 16-byte aligned
+__device__ __forceinline__ void mk_bulk_g2s(void * dst, const void * src, unsigned bytes, unsigned long long * mb) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(mk_saddr(dst)), "l"(src), "r"(bytes), "r"(mk_saddr(mb)) : "memory");
+}
+// wait for phase `parity` of mb; false after MK_SPIN polls
+__device__ __forceinline__ bool mk_mbar_wait(unsigned long long * mb, unsigned parity) {
+    const unsigned ad = mk_saddr(mb);
+    for (unsigned spins = 0;; ++spins) {
+        unsigned done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(ad), "r"(parity) : "memory");
+        if (done) return true;
+        if (spins >= MK_SPIN) return false;
+        __nanosleep(20);
+    }
+}
+__device__ __forceinline__ void mk_fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// head h's q, k and v rows (64 each) of a Q4_0 q/k/v matrix (K = 1024):
+// three contiguous sections, one bulk copy each
+#define MK_QKVW_SEC (T3B_HD * MK_QKVW_ROW)
+__device__ __forceinline__ void mk_bulk_qkvw(unsigned char * dst, const MkMat & W, int h, unsigned long long * mb) {
+    for (int sec = 0; sec < 3; ++sec)
+        mk_bulk_g2s(dst + sec * MK_QKVW_SEC, W.w + (size_t) (sec * 1024 + h * T3B_HD) * MK_QKVW_ROW, MK_QKVW_SEC, mb);
+}
+
+// q/k/v of one head from the staged Q4_0 rows.  Lane = 8 * g + c: row group
+// g of the warp's four rows, blocks c, c+8, c+16, c+24 summed in that order,
+// then a butterfly over the eight lanes.  Warp w takes rows 12w .. 12w+11.
+// Raw row sums (no bias) go to out[192].
+__device__ __forceinline__ void mk_qkv_own(const unsigned char * wst, const MkAct & x, float * out) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, g = lane >> 3, c = lane & 7;
+    int4 xa[4], xb[4];
+    float dx[4];
+    int sx8[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int b = c + 8 * j;
+        xa[j] = *(const int4 *) (x.q + b * 32);
+        xb[j] = *(const int4 *) (x.q + b * 32 + 16);
+        dx[j] = x.d[b];
+        sx8[j] = 8 * x.s[b];
+    }
+    float acc[3];
+#pragma unroll
+    for (int it = 0; it < 3; ++it) {
+        const unsigned char * rp = wst + (size_t) (w * 12 + it * 4 + g) * MK_QKVW_ROW;
+        float t = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int b = c + 8 * j;
+            const uint4 qv = *(const uint4 *) (rp + b * 16);
+            const float dw = __half2float(*(const __half *) (rp + 512 + b * 2));
+            int si = 0;
+            si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), xa[j].x, si);
+            si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), xb[j].x, si);
+            si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), xa[j].y, si);
+            si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), xb[j].y, si);
+            si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), xa[j].z, si);
+            si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), xb[j].z, si);
+            si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), xa[j].w, si);
+            si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), xb[j].w, si);
+            si -= sx8[j];
+            t = __fadd_rn(t, __fmul_rn(__fmul_rn((float) si, dw), dx[j]));
+        }
+        acc[it] = t;
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1)
+#pragma unroll
+        for (int it = 0; it < 3; ++it) acc[it] = __fadd_rn(acc[it], __shfl_xor_sync(0xffffffffu, acc[it], o));
+    if (c == 0) {
+#pragma unroll
+        for (int it = 0; it < 3; ++it) out[w * 12 + it * 4 + g] = acc[it];
+    }
+}
 
 // Bulk prefetch of a CTA's weight slice into L2 (one instruction, no
 // completion to track): issued one phase ahead so the register prefetch of
@@ -478,6 +582,16 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
     mk_prefetch<T>((W), (K), r0_, r1_, pf_);
 
 
+// every exit first waits (bounded) for this CTA's copies still in flight
+#define MK_BAIL do {                                                                  \
+        asm volatile("cp.async.wait_all;" ::: "memory");                              \
+        if (OWN && att && tid == 0) {                                                 \
+            if (kw_out >= 0) mk_mbar_wait(&mbar[0], (unsigned) kw_out & 1u);          \
+            if (v_out >= 0) mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u);            \
+        }                                                                             \
+        return;                                                                       \
+    } while (0)
+
 template <int T>
 __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -488,23 +602,76 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     __shared__ float rowsum[128];
     __shared__ int tokv;
     // scratch (reused by every phase): vec[4096] f32 | q[4096] i8 | d,s [128] | h[4096] f16 | part
-    float * vec = (float *) smem;
+    constexpr bool FUSE = T != T3B_F16;   // out-projection folded into the attention CTAs
+    constexpr bool OWN = T == T3B_Q4_0;   // attention CTAs compute their head's q/k/v themselves
+    float * vec = (float *) smem;         // (Q8_0 / F16 layout only)
     MkAct act;
-    act.v = vec;
-    act.q = (int8_t *) (smem + 16384);
-    act.d = (float *) (smem + 16384 + 4096);
-    act.s = (int *) (smem + 16384 + 4096 + 512);
-    act.h = (__half *) (smem + 16384 + 4096 + 1024);
-    float * part = (float *) (smem + 16384 + 4096 + 1024 + 8192);
-    // attention stage (and, in CTA 0, the sampler) reuse the same bytes
-    __half * kst = (__half *) smem;
-    __half * vst = kst + MK_MAX_POS * T3B_HD;
-    float * att_s = (float *) (smem + 2 * MK_MAX_POS * T3B_HD * 2);   // qkv[192] | p[MK_MAX_POS] | o[16][64] | head out[64] + Q8_0
+    float * part;
+    __half * kst, * vst;
+    float * att_s;
+    if (OWN) {
+        unsigned char * scr = smem + MK_ATT_BYTES;
+        act.v = nullptr;
+        act.q = (int8_t *) scr;
+        act.d = (float *) (scr + 4096);
+        act.s = (int *) (scr + 4096 + 512);
+        act.h = (__half *) (scr + 4096 + 1024);
+        part = (float *) (scr + 4096 + 1024 + 2048);
+        att_s = (float *) smem;
+        kst = (__half *) (smem + MK_ATT_BYTES + MK_SCR_BYTES);
+        vst = (__half *) (smem + MK_ATT_BYTES + MK_SCR_BYTES + MK_KV_BYTES);   // after the q/k/v weights are used
+    } else {
+        act.v = vec;
+        act.q = (int8_t *) (smem + 16384);
+        act.d = (float *) (smem + 16384 + 4096);
+        act.s = (int *) (smem + 16384 + 4096 + 512);
+        act.h = (__half *) (smem + 16384 + 4096 + 1024);
+        part = (float *) (smem + 16384 + 4096 + 1024 + 8192);
+        kst = (__half *) smem;   // the attention stage (and, in CTA 0, the sampler) reuse the scratch bytes
+        vst = kst + MK_MAX_POS * T3B_HD;
+        att_s = (float *) (smem + 2 * MK_KV_BYTES);
+    }
+    unsigned char * const qkvw = (unsigned char *) vst;   // OWN: staged q/k/v weights of this CTA's head
 
     const int tid = threadIdx.x, cta = blockIdx.x, G = gridDim.x;
     const int NL = a.n_layer;
     const int Hn = 16;
-    constexpr bool FUSE = T != T3B_F16;   // out-projection folded into the attention CTAs
+    // attention CTAs: 1..16 when they stage weights (CTA 0 runs the sampler,
+    // whose arrays would overwrite the staged rows), else 0..15
+    const bool att = OWN ? (cta >= 1 && cta <= Hn) : cta < Hn;
+    const int hh_ = OWN ? cta - 1 : cta;
+    // fc / fc2 workers: with OWN the attention CTAs sit out P4 and P5 (their
+    // bulk copies for the next layer are in flight then, and a release fence
+    // in those CTAs would wait for them); worker wi of GW takes the rows
+    const bool worker = !OWN || !att;
+    const int GW = OWN ? G - Hn : G;
+    const int wi = OWN ? (cta == 0 ? 0 : cta - Hn) : cta;
+    // OWN staging: mbar[0] = this use's K rows + q/k/v weights, mbar[1] =
+    // its V rows; use u = step * n_layer + layer completes phase u of each.
+    // kw_out / v_out: use index of a copy issued and not yet waited for.
+    __shared__ __align__(8) unsigned long long mbar[2];
+    __shared__ int okf;
+    int kw_out = -1, v_out = -1;
+    if (OWN && att && tid == 0) {
+        mk_mbar_init(&mbar[0]);
+        mk_mbar_init(&mbar[1]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // OWN attention CTAs: bulk copies of use u's K rows [0, npos) of layer nl
+    // and of that layer's q/k/v weights for this head, issued by the last
+    // warp's first thread (not the hand-off poller)
+    auto issue_kw = [&](int u, int nl, int npos) {
+        if (tid == MK_THREADS - 32) {
+            mk_fence_proxy_async();   // K/V rows this CTA stored (generic proxy) are read by the bulk copy
+            mk_mbar_expect(&mbar[0], (unsigned) npos * T3B_HD * 2 + MK_QKVW_BYTES);
+            if (npos > 0)
+                mk_bulk_g2s(kst, a.kv + (size_t) nl * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD,
+                            (unsigned) npos * T3B_HD * 2, &mbar[0]);
+            mk_bulk_qkvw(qkvw, a.layers[nl].qkv, hh_, &mbar[0]);
+        }
+        kw_out = u;
+    };
     unsigned * cQKV = a.cnt + MK_C_QKV * MK_C_STRIDE, * cATT = a.cnt + MK_C_ATT * MK_C_STRIDE;
     unsigned * cXM = a.cnt + MK_C_XM * MK_C_STRIDE, * cH = a.cnt + MK_C_H * MK_C_STRIDE;
     unsigned * cX = a.cnt + MK_C_X * MK_C_STRIDE, * cLOG = a.cnt + MK_C_LOG * MK_C_STRIDE;
@@ -527,6 +694,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             tok = a.samp.step_tok[slot0];
         }
     }
+    if (OWN && att) issue_kw(0, 0, a.p0);   // use 0: layer 0 of the first step
     for (int step = 0; step < a.n_steps; ++step) {
         // host cancel flag (mapped memory, a PCIe round trip): one thread of
         // CTA 0 reads it at the start of the step; the value is needed only
@@ -541,8 +709,82 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         for (int l = 0; l < NL; ++l) {
             const MkLayer & Ly = a.layers[l];
             const unsigned k = (unsigned) (step * NL + l) + 1u;   // occurrence of this layer's phases
+            // out-projection weights of this CTA's head (FUSE): blocks 2h, 2h+1
+            // of rows tid and tid + 512 (quants and the two block scales).
+            // OWN loads them before the layer-input wait, the others before
+            // the q/k/v wait, so they arrive while the CTA waits.
+            uint4 ow[2][MkW<T>::QW * 2];
+            unsigned ows[2] = {0u, 0u};
+            auto load_ow = [&]() {
+                if (FUSE) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint8_t * wr = Ly.o.w + (size_t) (tid + u * MK_THREADS) * Ly.o.rb;
+                        constexpr int QB = T == T3B_Q4_0 ? 16 : 32;
+#pragma unroll
+                        for (int c = 0; c < MkW<T>::QW * 2; ++c) ow[u][c] = ldg_v4(wr + 2 * hh_ * QB + c * 16);
+                        ows[u] = ld_nc_u32(wr + (size_t) (D / 32) * QB + 4 * hh_);
+                    }
+                }
+            };
             // ---------------- P1: LN1 + QKV (+ K/V append) ----------------
-            {
+            if (OWN) {
+                if (att) load_ow();
+                // every CTA takes the layer input (P4's residual); the
+                // attention CTAs normalise it and compute their head's q/k/v
+                // rows from the staged weights, then append K/V at pos
+                if (worker) mk_l2_prefetch_rows(Ly.fc, mk_fc_r0(wi, GW, true), mk_fc_r0(wi + 1, GW, true));   // P4's rows
+                const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
+                const float bq = att && tid < 3 * T3B_HD ? __ldg(Ly.bqkv + (tid >> 6) * D + hh_ * T3B_HD + (tid & 63)) : 0.0f;
+                MK_STAMP(l * 20 + 0);
+                float2 xv;
+                if (l > 0) {
+                    if (!mk_acquire(cX, (k - 1u) * GW, a)) MK_BAIL;
+                    xv = __ldcg((const float2 *) bX + tid);
+                    *(float2 *) (xres + 2 * tid) = xv;
+                } else {
+                    xv = *(const float2 *) (xres + 2 * tid);
+                }
+                MK_STAMP(l * 20 + 1);
+                if (att) {
+                    float * qkvh = att_s;   // [192]
+                    const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
+                    mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, false);
+                    if (tid == 0) {   // K rows and q/k/v weights of this use
+                        const bool ok = mk_mbar_wait(&mbar[0], (unsigned) (k - 1u) & 1u);
+                        if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                        okf = ok;
+                    }
+                    __syncthreads();
+                    if (!okf) MK_BAIL;
+                    kw_out = -1;
+                    MK_STAMP(l * 20 + 14);
+                    mk_qkv_own(qkvw, act, qkvh);
+                    __syncthreads();
+                    MK_STAMP(l * 20 + 15);
+                    // V rows [0, pos) replace the weights (every read of them
+                    // finished before the barrier above).  Issued by the last
+                    // warp, which has no part in the K/V append below.
+                    if (tid == MK_THREADS - 32) {
+                        mk_mbar_expect(&mbar[1], (unsigned) pos * T3B_HD * 2);
+                        if (pos > 0) mk_bulk_g2s(vst, kb + a.v_off, (unsigned) pos * T3B_HD * 2, &mbar[1]);
+                    }
+                    MK_STAMP(l * 20 + 16);
+                    v_out = (int) (k - 1u);
+                    if (tid < 3 * T3B_HD) {
+                        const float v = __fadd_rn(__fadd_rn(0.0f, qkvh[tid]), bq);   // mk_dot's row sum + bias
+                        qkvh[tid] = v;
+                        if (tid >= T3B_HD) {
+                            const int vv = tid >= 2 * T3B_HD, c = tid & 63;
+                            const __half hv = __float2half_rn(v);
+                            (vv ? (__half *) (kb + a.v_off) : (__half *) kb)[(size_t) pos * T3B_HD + c] = hv;
+                            (vv ? vst : kst)[(size_t) pos * T3B_HD + c] = hv;
+                        }
+                    }
+                    __syncthreads();
+                    MK_STAMP(l * 20 + 13);
+                }
+            } else {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
                 if (FUSE) mk_l2_prefetch_rows(Ly.fc, mk_fc_r0(cta, G, true), mk_fc_r0(cta + 1, G, true));   // P4's rows
                 else mk_l2_prefetch(Ly.o, D);
@@ -553,7 +795,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 // embedding of layer 0 is already in xres)
                 float2 xv;
                 if (l > 0) {
-                    if (!mk_acquire(cX, (k - 1u) * G, a)) return;
+                    if (!mk_acquire(cX, (k - 1u) * G, a)) MK_BAIL;
                     xv = __ldcg((const float2 *) bX + tid);
                     *(float2 *) (xres + 2 * tid) = xv;
                 } else {
@@ -579,46 +821,34 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 mk_release(cQKV);
                 MK_STAMP(l * 20 + 2);
             }
-            // ---------------- P2: attention (CTA h < 16 owns head h) ----------
-            if (cta < Hn) {
-                const int h = cta;
+            // ---------------- P2: attention (one CTA per head) ----------------
+            if (att) {
+                const int h = hh_;
                 const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) h * a.max_ctx * T3B_HD;
                 const __half * vb = kb + a.v_off;
-                // stage K/V of positions [0, pos) while q/k/v are computed
-                const int nchunk = pos * (T3B_HD * 2 / 16);     // 16-byte chunks per tensor
-                for (int i = tid; i < nchunk; i += MK_THREADS) {
-                    const unsigned sk = (unsigned) __cvta_generic_to_shared(kst) + i * 16;
-                    const unsigned sv = (unsigned) __cvta_generic_to_shared(vst) + i * 16;
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sk), "l"(kb + i * 8) : "memory");
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sv), "l"(vb + i * 8) : "memory");
+                if (!OWN) {
+                    // stage K/V of positions [0, pos) while q/k/v are computed
+                    mk_stage_kv(kst, kb, pos);
+                    mk_stage_kv(vst, vb, pos);
+                    mk_cp_commit();
                 }
-                asm volatile("cp.async.commit_group;" ::: "memory");
-                // out-projection weights of this head: blocks 2h, 2h+1 of rows
-                // tid and tid + 512 (quants and the two block scales)
-                uint4 ow[2][MkW<T>::QW * 2];
-                unsigned ows[2] = {0u, 0u};
-                if (FUSE) {
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const uint8_t * wr = Ly.o.w + (size_t) (tid + u * MK_THREADS) * Ly.o.rb;
-                        constexpr int QB = T == T3B_Q4_0 ? 16 : 32;
-#pragma unroll
-                        for (int c = 0; c < MkW<T>::QW * 2; ++c) ow[u][c] = ldg_v4(wr + 2 * h * QB + c * 16);
-                        ows[u] = ld_nc_u32(wr + (size_t) (D / 32) * QB + 4 * h);
-                    }
-                }
+                if (!OWN) load_ow();
                 float * qkvh = att_s;   // [192]
-                const bool ok = mk_acquire(cQKV, k * G, a);
-                if (tid < 192) qkvh[tid] = __ldcg(bQKV + (tid / 64) * D + h * 64 + (tid & 63));
-                asm volatile("cp.async.wait_all;" ::: "memory");
-                __syncthreads();
-                if (!ok) return;
-                MK_STAMP(l * 20 + 3);
-                if (tid < T3B_HD) {
-                    kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
-                    vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
+                if (!OWN) {
+                    const bool ok = mk_acquire(cQKV, k * G, a);
+                    MK_STAMP(l * 20 + 12);
+                    if (tid < 192) qkvh[tid] = __ldcg(bQKV + (tid / 64) * D + h * 64 + (tid & 63));
+                    asm volatile("cp.async.wait_all;" ::: "memory");
+                    __syncthreads();
+                    if (!ok) MK_BAIL;
+                    MK_STAMP(l * 20 + 3);
+                    if (tid < T3B_HD) {
+                        kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
+                        vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
+                    }
+                    __syncthreads();
+                    MK_STAMP(l * 20 + 13);
                 }
-                __syncthreads();
                 const int L = pos + 1;
                 const int lane = tid & 31, w = tid >> 5;
                 // scores: thread t owns keys t and t + 512; each thread walks the
@@ -654,6 +884,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 lm = warp_max(lm);
                 if (lane == 0) rf[w] = lm;
                 __syncthreads();
+                if (OWN) MK_STAMP(l * 20 + 12);
                 const float mx = warp_max(rf[lane & 15]);
                 float * pw = att_s + 256;      // [L] weights
                 float ls = 0.0f;
@@ -664,8 +895,19 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 }
                 ls = warp_sum(ls);
                 if (lane == 0) rf[32 + w] = ls;
+                if (OWN && tid == 0) {   // this layer's V rows
+                    const bool ok = mk_mbar_wait(&mbar[1], (unsigned) (k - 1u) & 1u);
+                    if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                    okf = ok;
+                    MK_STAMP(l * 20 + 3);
+                }
                 __syncthreads();
+                if (OWN) {
+                    if (!okf) MK_BAIL;
+                    v_out = -1;
+                }
                 const float lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
+                MK_STAMP(l * 20 + 9);
                 // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
                 // dims 2l, 2l+1; two accumulators hide the load latency
                 {
@@ -687,6 +929,8 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     og[w * 64 + 2 * lane] = o0.x + o1.x;
                     og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
                     __syncthreads();
+                    MK_STAMP(l * 20 + 17);
+
                     float * ho = og + 16 * 64;   // this head's 64 outputs
                     if (tid < 64) {
                         float t = 0.0f;
@@ -720,6 +964,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             }
                         }
                         __syncthreads();
+                        MK_STAMP(l * 20 + 18);
                         const int4 xa = *(const int4 *) hq, xb = *(const int4 *) (hq + 16);
                         const int4 xc = *(const int4 *) (hq + 32), xe = *(const int4 *) (hq + 48);
                         const float dx0 = hd[0], dx1 = hd[1];
@@ -758,7 +1003,20 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         }
                     }
                 }
+                MK_STAMP(l * 20 + 19);
+                __syncthreads();
+                MK_STAMP(l * 20 + 2);
                 mk_release(cATT);
+                MK_STAMP(l * 20 + 5);
+                // K and V rows are consumed (the release's barrier): stage the
+                // next layer's (use k); layer 0 of the next step is staged
+                // after the head, whose release would otherwise wait for it
+                if (OWN && l + 1 < NL) {
+                    // only once every head has released: bulk traffic in
+                    // flight slows the release of the CTAs still storing
+                    if (!mk_acquire(cATT, k * Hn, a)) MK_BAIL;
+                    issue_kw((int) k, l + 1, pos);
+                }
                 MK_STAMP(l * 20 + 4);
             }
             // ---------------- P3: proj + bias + residual (F16 weights) --------
@@ -766,7 +1024,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 MK_GEMV_BEGIN(Ly.o, D, D)
                 mk_l2_prefetch(Ly.fc, 4 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bo + r0_ + tid) : 0.0f;
-                if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) return;
+                if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) MK_BAIL;
                 MK_STAMP(l * 20 + 5);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
@@ -776,16 +1034,17 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 }
                 mk_release(cXM);
             }
+            if (l + 1 == NL) mk_l2_prefetch(a.head, a.V);   // every CTA has head rows
             // ---------------- P4: LN2 + fc + GELU ------------------------------
-            {
-                // with the fused out-projection each CTA owns whole 32-row
-                // blocks of fc (128 blocks: on 148 SMs, one block or none)
-                // and publishes its slice of h already in Q8_0, which is
-                // fc2's input; the F16 path publishes h as floats
-                const int r0_ = mk_fc_r0(cta, G, FUSE), r1_ = mk_fc_r0(cta + 1, G, FUSE);
+            if (worker) {
+                // with the fused out-projection each worker owns whole 32-row
+                // blocks of fc (128 blocks: one block or none per worker) and
+                // publishes its slice of h already in Q8_0, which is fc2's
+                // input; the F16 path publishes h as floats
+                const int r0_ = mk_fc_r0(wi, GW, FUSE), r1_ = mk_fc_r0(wi + 1, GW, FUSE);
                 MkPref<T> pf_;
                 mk_prefetch<T>(Ly.fc, D, r0_, r1_, pf_);
-                mk_l2_prefetch(Ly.fc2, D);
+                mk_l2_prefetch_rows(Ly.fc2, mk_r0(D, wi, GW), mk_r0(D, wi + 1, GW));
                 const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
                 float x0, x1;   // x_mid elements 2*tid, 2*tid+1
@@ -793,7 +1052,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     // x_mid = (sum over heads of the partials) + proj bias + x,
                     // heads added in order 0..15
                     const float2 bo = __ldg((const float2 *) Ly.bo + tid);
-                    if (!mk_acquire(cATT, k * Hn, a)) return;
+                    if (!mk_acquire(cATT, k * Hn, a)) MK_BAIL;
                     float2 p[16];
 #pragma unroll
                     for (int hh = 0; hh < 16; ++hh) p[hh] = __ldcg((const float2 *) (bPART + hh * D) + tid);
@@ -804,7 +1063,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     x0 = __fadd_rn(__fadd_rn(x0, bo.x), xr.x);
                     x1 = __fadd_rn(__fadd_rn(x1, bo.y), xr.y);
                 } else {
-                    if (!mk_acquire(cXM, k * G, a)) return;
+                    if (!mk_acquire(cXM, k * G, a)) MK_BAIL;
                     const float2 xm = __ldcg((const float2 *) bXM + tid);
                     x0 = xm.x; x1 = xm.y;
                 }
@@ -841,21 +1100,22 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 mk_release(cH);
             }
             // ---------------- P5: fc2 + bias + residual ------------------------
-            {
-                MK_GEMV_BEGIN(Ly.fc2, 4 * D, D)
-                if (l + 1 < NL) mk_l2_prefetch(a.layers[l + 1].qkv, 3 * D);
-                else mk_l2_prefetch(a.head, a.V);
+            if (worker) {
+                const int r0_ = mk_r0(D, wi, GW), r1_ = mk_r0(D, wi + 1, GW);
+                MkPref<T> pf_;
+                mk_prefetch<T>(Ly.fc2, 4 * D, r0_, r1_, pf_);
+                if (l + 1 < NL && !OWN) mk_l2_prefetch(a.layers[l + 1].qkv, 3 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
                 if (FUSE) {
                     // h arrives in Q8_0: 4096 quants, 128 scales, 128 sums
-                    if (!mk_acquire(cH, k * G, a)) return;
+                    if (!mk_acquire(cH, k * GW, a)) MK_BAIL;
                     if (tid < 256) *(int4 *) (act.q + 16 * tid) = __ldcg((const int4 *) bHQ + tid);
                     else if (tid < 384) act.d[tid - 256] = __ldcg(bHD + tid - 256);
                     else act.s[tid - 384] = __ldcg(bHS + tid - 384);
                     __syncthreads();
                     MK_STAMP(l * 20 + 7);
                 } else {
-                    if (!mk_wait_vec(cH, k * G, bH, 4 * D, vec, a)) return;
+                    if (!mk_wait_vec(cH, k * GW, bH, 4 * D, vec, a)) MK_BAIL;
                     MK_STAMP(l * 20 + 7);
                     mk_quantize(act, 4 * D, true);
                 }
@@ -874,17 +1134,19 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         MK_STAMP(480);
         {
             bool ok;
-            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, vec, act, part, rowsum, redd);
-            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, vec, act, part, rowsum, redd);
-            else ok = mk_head<T3B_Q4_0>(a, step, vec, act, part, rowsum, redd);
-            if (!ok) return;
+            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, GW, act, part, rowsum, redd);
+            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, GW, act, part, rowsum, redd);
+            else ok = mk_head<T3B_Q4_0>(a, step, GW, act, part, rowsum, redd);
+            if (!ok) MK_BAIL;
         }
+        // OWN: layer 0 of the next step (K rows up to this step's position)
+        if (OWN && att && step + 1 < a.n_steps) issue_kw((step + 1) * NL, 0, pos + 1);
         MK_STAMP(481);
-        if (!a.sample) return;   // eval_step: logits only
+        if (!a.sample) MK_BAIL;   // eval_step: logits only
         // ---------------- sampler (CTA 0) and token broadcast -------------------
         if (cta == 0) {
             float * lg = (float *) (smem + T3B_SAMPLER_SMEM);   // logits staged after the sampler's arrays
-            if (!mk_acquire(cLOG, (unsigned) (step + 1) * G, a)) return;
+            if (!mk_acquire(cLOG, (unsigned) (step + 1) * G, a)) MK_BAIL;
             {
                 constexpr int E = (T3B_SAMPLER_VMAX + MK_THREADS - 1) / MK_THREADS;
                 float v[E];
@@ -909,13 +1171,14 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             mk_release(cTOK);
         }
         {
-            if (!mk_acquire(cTOK, (unsigned) (step + 1), a)) return;
+            if (!mk_acquire(cTOK, (unsigned) (step + 1), a)) MK_BAIL;
             MK_STAMP(484);
             if (tid == 0) tokv = __ldcg(bTOK);
             __syncthreads();
             const int tv = tokv;
-            if (tv & 0x10000) return;
+            if (tv & 0x10000) MK_BAIL;
             tok = tv & 0xffff;
         }
     }
+    MK_BAIL;
 }

@@ -768,11 +768,15 @@ int mega_prepare(t3b_ctx * ctx) {
     const int G = sms;
     auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
     // per-CTA limits of the register prefetch (MK_MAXI items of 32 elements
-    // per thread) and of the row scratch
-    if (cdiv(3 * 1024, G) * 32 > MK_MAXI * MK_THREADS || cdiv(4 * 1024, G) * 32 > MK_MAXI * MK_THREADS ||
-        cdiv(1024, G) * 128 > MK_MAXI * MK_THREADS || cdiv(ctx->hp.n_speech_vocab, G) * 32 > MK_MAXI * MK_THREADS ||
-        cdiv(ctx->hp.n_speech_vocab, G) > 128 || G < 16 ||
-        (ctx->L[0].fc.type != T3B_F16 && cdiv(128, G) * 32 * 32 > MK_MAXI * MK_THREADS)) {   // fc in 32-row blocks
+    // per thread) and of the row scratch.  Q4_0 layers: CTAs 1..16 run the
+    // attention and the other GW = G - 16 share fc and fc2 (fc in whole
+    // 32-row blocks); Q8_0: fc in blocks over all G; F16: plain row split.
+    const int LT = ctx->L[0].fc.type;
+    const int GW = LT == T3B_Q4_0 ? G - 16 : G;
+    const int fc_items = LT == T3B_F16 ? cdiv(4 * 1024, GW) * 32 : cdiv(128, GW) * 32 * 32;
+    if (G < 17 || GW < 1 || cdiv(3 * 1024, G) * 32 > MK_MAXI * MK_THREADS || fc_items > MK_MAXI * MK_THREADS ||
+        cdiv(1024, GW) * 128 > MK_MAXI * MK_THREADS || cdiv(ctx->hp.n_speech_vocab, G) * 32 > MK_MAXI * MK_THREADS ||
+        cdiv(ctx->hp.n_speech_vocab, G) > 128) {
         set_err(&ctx->err, "megakernel: %d SMs too few for the row split", G);
         return T3B_ERR_STATE;
     }
