@@ -944,6 +944,7 @@ struct SampArgs {
 };
 
 #define T3B_SAMPLER_THREADS 1024
+#define T3B_SAMPLER_TL 22   // debug stage stamps of row 0
 #define T3B_SAMPLER_VMAX 8192
 // dynamic smem: s[VMAX] f32 | keys[VMAX] u64 | e[VMAX] f32
 #define T3B_SAMPLER_SMEM (T3B_SAMPLER_VMAX * (4 + 8 + 4))
@@ -1205,6 +1206,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 if (v != -INFINITY) atomicAdd(&hist[samp_dbin(v, smin, scale)], 1);
             }
             __syncthreads();
+            SAMP_STAMP(16);
             const int bpt = (SAMP_NBIN + nth - 1) / nth;
             const int b0 = min(SAMP_NBIN, tid * bpt), b1 = min(SAMP_NBIN, b0 + bpt);
             int tot = 0;
@@ -1222,6 +1224,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                     if (P.top_k < start[d] + hist[d]) { shi[0] = d; break; }
             }
             __syncthreads();
+            SAMP_STAMP(17);
             const int dsel = shi[0];
             int lmaxb = 0;
             for (int d = b0; d < b1 && d <= dsel; ++d) lmaxb = max(lmaxb, hist[d]);
@@ -1236,6 +1239,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                     keys[pos] = ((unsigned long long) desc_key(v) << 32) | (unsigned) i;
                 }
                 __syncthreads();
+                SAMP_STAMP(18);
                 for (int d = tid; d <= dsel; d += nth) {
                     unsigned long long * kp = keys + start[d];
                     const int n = hist[d];
@@ -1247,6 +1251,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                     }
                 }
                 __syncthreads();
+                SAMP_STAMP(19);
                 const int ns = start[dsel] + hist[dsel];
                 if (need_k) {
                     // threshold = the score at descending rank k; scores in
@@ -1448,12 +1453,14 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             bool ok;
             const double eps = (double) (c + 2) * 0x1p-24 * 1.01 + 1e-12;
             int j = block_first_crossing(c, (double) P.top_p, eps, [&](int q) { return (double) e[q]; }, redd, shi, &ok);
+            SAMP_STAMP(20);
             if (!ok) {
                 if (tid == 0) shi[3] = seq_cut_f32(e, c, P.top_p);
                 __syncthreads();
                 j = shi[3];
                 __syncthreads();
             }
+            SAMP_STAMP(21);
             const int cut = j < c ? j + 1 : c;
             for (int q = cut + tid; q < c; q += nth) s[(int) (keys[q] & 0xffffffffu)] = -INFINITY;
             __syncthreads();

@@ -1209,15 +1209,15 @@ int t3b_op_sample_philox(const float * cond_dev, const float * uncond_dev, int r
     a.params = params_dev; a.params_per_row = 1; a.rng_mode = nullptr; a.mt = nullptr;
     a.ph_seed = (const unsigned long long *) seed_dev; a.ph_ctr = (unsigned long long *) counter_dev;
     a.tok_out = tokens_out_dev; a.step_tok = nullptr; a.done = nullptr; a.stop_token = -1; a.fx = fx;
-    // debug: T3B_SAMPLER_TIMELINE=<file> writes stage stamps of row 0 (16 u64 ns)
+    // debug: T3B_SAMPLER_TIMELINE=<file> writes stage stamps of row 0 (T3B_SAMPLER_TL u64 ns)
     const char * tl_file = getenv("T3B_SAMPLER_TIMELINE");
-    if (tl_file) { cudaMalloc(&a.tl, 16 * 8); cudaMemsetAsync(a.tl, 0, 16 * 8, (cudaStream_t) cuda_stream); }
+    if (tl_file) { cudaMalloc(&a.tl, T3B_SAMPLER_TL * 8); cudaMemsetAsync(a.tl, 0, T3B_SAMPLER_TL * 8, (cudaStream_t) cuda_stream); }
     sampler_kernel<<<rows, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, (cudaStream_t) cuda_stream>>>(a);
     if (tl_file) {
-        unsigned long long h[16];
+        unsigned long long h[T3B_SAMPLER_TL];
         cudaMemcpyAsync(h, a.tl, sizeof h, cudaMemcpyDeviceToHost, (cudaStream_t) cuda_stream);
         cudaStreamSynchronize((cudaStream_t) cuda_stream);
-        if (FILE * f = fopen(tl_file, "wb")) { fwrite(h, 8, 16, f); fclose(f); }
+        if (FILE * f = fopen(tl_file, "wb")) { fwrite(h, 8, T3B_SAMPLER_TL, f); fclose(f); }
         cudaFree(a.tl);
     }
     cudaError_t e = cudaGetLastError();
