@@ -425,9 +425,10 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const
     const MkLn lp = mk_ln_prefetch(a.lnfg, a.lnfb);
     const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
+    const int cta = blockIdx.x;
+    MK_STAMP(489);
     if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
     const float2 xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
-    const int cta = blockIdx.x;
     MK_STAMP(487);
     mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, HT == T3B_F16);
     mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
@@ -646,12 +647,15 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     const bool worker = !OWN || !att;
     const int GW = OWN ? G - Hn : G;
     const int wi = OWN ? (cta == 0 ? 0 : cta - Hn) : cta;
-    // OWN staging: mbar[0] = this use's K rows + q/k/v weights, mbar[1] =
-    // its V rows; use u = step * n_layer + layer completes phase u of each.
-    // kw_out / v_out: use index of a copy issued and not yet waited for.
+    // OWN staging: mbar[0] = a use's K rows + q/k/v weights (use u = step *
+    // n_layer + layer completes phase u), plus its V rows when K and V of
+    // positions [0, pos] fit the K stage together ("packed": V at row pos+1);
+    // otherwise mbar[1] = the V rows, loaded into the weight stage after the
+    // q/k/v rows are computed (vph counts its phases).  kw_out / v_out: phase
+    // of a copy issued and not yet waited for.
     __shared__ __align__(8) unsigned long long mbar[2];
     __shared__ int okf;
-    int kw_out = -1, v_out = -1;
+    int kw_out = -1, v_out = -1, vph = 0;
     if (OWN && att && tid == 0) {
         mk_mbar_init(&mbar[0]);
         mk_mbar_init(&mbar[1]);
@@ -661,13 +665,18 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // OWN attention CTAs: bulk copies of use u's K rows [0, npos) of layer nl
     // and of that layer's q/k/v weights for this head, issued by the last
     // warp's first thread (not the hand-off poller)
+    auto packed = [](int p) { return 2 * (p + 1) <= MK_MAX_POS; };
     auto issue_kw = [&](int u, int nl, int npos) {
         if (tid == MK_THREADS - 32) {
+            const bool pk = packed(npos);
+            const unsigned rb = (unsigned) npos * T3B_HD * 2;
+            const __half * kb = a.kv + (size_t) nl * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
             mk_fence_proxy_async();   // K/V rows this CTA stored (generic proxy) are read by the bulk copy
-            mk_mbar_expect(&mbar[0], (unsigned) npos * T3B_HD * 2 + MK_QKVW_BYTES);
-            if (npos > 0)
-                mk_bulk_g2s(kst, a.kv + (size_t) nl * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD,
-                            (unsigned) npos * T3B_HD * 2, &mbar[0]);
+            mk_mbar_expect(&mbar[0], (pk ? 2u : 1u) * rb + MK_QKVW_BYTES);
+            if (npos > 0) {
+                mk_bulk_g2s(kst, kb, rb, &mbar[0]);
+                if (pk) mk_bulk_g2s(kst + (size_t) (npos + 1) * T3B_HD, kb + a.v_off, rb, &mbar[0]);
+            }
             mk_bulk_qkvw(qkvw, a.layers[nl].qkv, hh_, &mbar[0]);
         }
         kw_out = u;
@@ -750,6 +759,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     float * qkvh = att_s;   // [192]
                     const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
                     mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, false);
+                    MK_STAMP(l * 20 + 12);
                     if (tid == 0) {   // K rows and q/k/v weights of this use
                         const bool ok = mk_mbar_wait(&mbar[0], (unsigned) (k - 1u) & 1u);
                         if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
@@ -762,15 +772,19 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     mk_qkv_own(qkvw, act, qkvh);
                     __syncthreads();
                     MK_STAMP(l * 20 + 15);
-                    // V rows [0, pos) replace the weights (every read of them
-                    // finished before the barrier above).  Issued by the last
-                    // warp, which has no part in the K/V append below.
-                    if (tid == MK_THREADS - 32) {
-                        mk_mbar_expect(&mbar[1], (unsigned) pos * T3B_HD * 2);
-                        if (pos > 0) mk_bulk_g2s(vst, kb + a.v_off, (unsigned) pos * T3B_HD * 2, &mbar[1]);
+                    const bool pk = packed(pos);
+                    __half * vrow = pk ? kst + (size_t) (pos + 1) * T3B_HD : vst;
+                    if (!pk) {
+                        // V rows [0, pos) replace the weights (every read of
+                        // them finished before the barrier above).  Issued by
+                        // the last warp, which has no part in the K/V append.
+                        if (tid == MK_THREADS - 32) {
+                            mk_mbar_expect(&mbar[1], (unsigned) pos * T3B_HD * 2);
+                            if (pos > 0) mk_bulk_g2s(vst, kb + a.v_off, (unsigned) pos * T3B_HD * 2, &mbar[1]);
+                        }
+                        v_out = vph++;
                     }
                     MK_STAMP(l * 20 + 16);
-                    v_out = (int) (k - 1u);
                     if (tid < 3 * T3B_HD) {
                         const float v = __fadd_rn(__fadd_rn(0.0f, qkvh[tid]), bq);   // mk_dot's row sum + bias
                         qkvh[tid] = v;
@@ -778,7 +792,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             const int vv = tid >= 2 * T3B_HD, c = tid & 63;
                             const __half hv = __float2half_rn(v);
                             (vv ? (__half *) (kb + a.v_off) : (__half *) kb)[(size_t) pos * T3B_HD + c] = hv;
-                            (vv ? vst : kst)[(size_t) pos * T3B_HD + c] = hv;
+                            (vv ? vrow : kst)[(size_t) pos * T3B_HD + c] = hv;
                         }
                     }
                     __syncthreads();
@@ -884,7 +898,6 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 lm = warp_max(lm);
                 if (lane == 0) rf[w] = lm;
                 __syncthreads();
-                if (OWN) MK_STAMP(l * 20 + 12);
                 const float mx = warp_max(rf[lane & 15]);
                 float * pw = att_s + 256;      // [L] weights
                 float ls = 0.0f;
@@ -895,17 +908,19 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 }
                 ls = warp_sum(ls);
                 if (lane == 0) rf[32 + w] = ls;
-                if (OWN && tid == 0) {   // this layer's V rows
-                    const bool ok = mk_mbar_wait(&mbar[1], (unsigned) (k - 1u) & 1u);
+                const bool vwait = OWN && v_out >= 0;   // V rows loaded separately (not packed)
+                if (vwait && tid == 0) {   // this layer's V rows
+                    const bool ok = mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u);
                     if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                     okf = ok;
                     MK_STAMP(l * 20 + 3);
                 }
                 __syncthreads();
-                if (OWN) {
+                if (vwait) {
                     if (!okf) MK_BAIL;
                     v_out = -1;
                 }
+                const __half * vsrc = (OWN && packed(pos)) ? kst + (size_t) (pos + 1) * T3B_HD : vst;
                 const float lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
                 MK_STAMP(l * 20 + 9);
                 // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
@@ -914,14 +929,14 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
                     int j = w;
                     for (; j + 16 < L; j += 32) {
-                        const float2 v0 = __half22float2(*(const __half2 *) (vst + (size_t) j * T3B_HD + 2 * lane));
-                        const float2 v1 = __half22float2(*(const __half2 *) (vst + (size_t) (j + 16) * T3B_HD + 2 * lane));
+                        const float2 v0 = __half22float2(*(const __half2 *) (vsrc + (size_t) j * T3B_HD + 2 * lane));
+                        const float2 v1 = __half22float2(*(const __half2 *) (vsrc + (size_t) (j + 16) * T3B_HD + 2 * lane));
                         const float p0 = pw[j], p1 = pw[j + 16];
                         o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
                         o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
                     }
                     if (j < L) {
-                        const float2 v0 = __half22float2(*(const __half2 *) (vst + (size_t) j * T3B_HD + 2 * lane));
+                        const float2 v0 = __half22float2(*(const __half2 *) (vsrc + (size_t) j * T3B_HD + 2 * lane));
                         const float p0 = pw[j];
                         o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
                     }
