@@ -1101,6 +1101,8 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     __shared__ int redi[33];
     __shared__ double redd[33];
     __shared__ unsigned seen[T3B_SAMPLER_VMAX / 32];
+    __shared__ unsigned surv[T3B_SAMPLER_VMAX / 32];   // survivor bit set (list mode)
+    __shared__ float redf2[32];
     __shared__ int shi[8];
     __shared__ float shf[4];
     __shared__ uint32_t mtx[625];
@@ -1148,9 +1150,16 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             }
         }
     }
-    int nfin = block_sum_i(lfin, redi);
-    const float smax = block_max(lmx, redf);
-    const float smin = -block_max(-lmn, redf);
+    // count, max and min in one exchange
+    const int nw = nth >> 5, w = tid >> 5;
+    lfin = warp_sum_i(lfin);
+    lmx = warp_max(lmx);
+    lmn = -warp_max(-lmn);
+    if (lane == 0) { redi[w] = lfin; redf[w] = lmx; redf2[w] = lmn; }
+    __syncthreads();
+    int nfin = warp_sum_i(lane < nw ? redi[lane] : 0);
+    const float smax = warp_max(lane < nw ? redf[lane] : -INFINITY);
+    const float smin = -warp_max(lane < nw ? -redf2[lane] : -INFINITY);
 
     SAMP_STAMP(1);
     // (1b) min-p: drop exp(s - max) < min_p.  The host expf is within one ulp
@@ -1207,28 +1216,45 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             }
             __syncthreads();
             SAMP_STAMP(16);
-            const int bpt = (SAMP_NBIN + nth - 1) / nth;
-            const int b0 = min(SAMP_NBIN, tid * bpt), b1 = min(SAMP_NBIN, b0 + bpt);
+            // bins [b0, b0 + bpt) per thread in thread order: warp scan, then
+            // every warp scans the warp totals itself (one barrier); the
+            // thread holding rank k names its bin; max bin count up to it
+            const int b0 = min(SAMP_NBIN, tid * ((SAMP_NBIN + nth - 1) / nth));
+            const int bpt = min((SAMP_NBIN + nth - 1) / nth, SAMP_NBIN - b0);
             int tot = 0;
-            for (int d = b0; d < b1; ++d) tot += hist[d];
-            int total;
-            const int excl = block_excl_scan_i(tot, redi, &total);
-            {
-                int run = excl;
-                for (int d = b0; d < b1; ++d) { start[d] = run; run += hist[d]; }
+            for (int d = 0; d < bpt; ++d) tot += hist[b0 + d];
+            int incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
             }
+            if (lane == 31) redi[w] = incl;
             if (tid == 0) shi[0] = SAMP_NBIN - 1;
             __syncthreads();
+            int wt = lane < nw ? redi[lane] : 0, wi = wt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += n;
+            }
+            const int excl = __shfl_sync(0xffffffffu, wi - wt, w) + incl - tot;
+            {
+                int run = excl;
+                for (int d = 0; d < bpt; ++d) { start[b0 + d] = run; run += hist[b0 + d]; }
+            }
             if (need_k && excl <= P.top_k && P.top_k < excl + tot) {
-                for (int d = b0; d < b1; ++d)
-                    if (P.top_k < start[d] + hist[d]) { shi[0] = d; break; }
+                for (int d = 0; d < bpt; ++d)
+                    if (P.top_k < start[b0 + d] + hist[b0 + d]) { shi[0] = b0 + d; break; }
             }
             __syncthreads();
-            SAMP_STAMP(17);
             const int dsel = shi[0];
             int lmaxb = 0;
-            for (int d = b0; d < b1 && d <= dsel; ++d) lmaxb = max(lmaxb, hist[d]);
-            const int maxb = (int) block_max((float) lmaxb, redf);
+            for (int d = 0; d < bpt && b0 + d <= dsel; ++d) lmaxb = max(lmaxb, hist[b0 + d]);
+            lmaxb = (int) warp_max((float) lmaxb);
+            if (lane == 0) redi[w] = lmaxb;
+            __syncthreads();
+            const int maxb = (int) warp_max(lane < nw ? (float) redi[lane] : 0.0f);
             if (maxb <= SAMP_BIN_MAX) {
                 for (int i = tid; i < V; i += nth) {
                     const float v = s[i];
@@ -1281,11 +1307,12 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             }
         }
     }
-    if (fastc >= 0 && topk_pending) {
-        for (int i = tid; i < V; i += nth) if (s[i] <= thr_k) s[i] = -INFINITY;
-        topk_pending = false;
-        __syncthreads();
-    }
+    // List mode: with the fast path the survivors of top-k (and below, of
+    // top-p) are keys[0 .. nsurv) and s[] is not masked; a bit set marks them
+    // for the penalty and the index-order compaction.
+    const bool listmode = fastc >= 0;
+    int nsurv = fastc;
+    if (listmode) topk_pending = false;
     if (fastc < 0 && P.top_k > 0 && P.top_k < V && nfin > P.top_k) {
         // digits of 11, 11 and 10 bits: the first already spreads the scores
         // over their exponent and leading mantissa bits, so few keys share a
@@ -1462,8 +1489,12 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             }
             SAMP_STAMP(21);
             const int cut = j < c ? j + 1 : c;
-            for (int q = cut + tid; q < c; q += nth) s[(int) (keys[q] & 0xffffffffu)] = -INFINITY;
-            __syncthreads();
+            if (listmode) {
+                nsurv = cut;
+            } else {
+                for (int q = cut + tid; q < c; q += nth) s[(int) (keys[q] & 0xffffffffu)] = -INFINITY;
+                __syncthreads();
+            }
         }
     }
     if (topk_pending) {
@@ -1472,9 +1503,18 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     }
 
     SAMP_STAMP(8);
+    const int nwords = (V + 31) / 32;
+    if (listmode) {
+        for (int i = tid; i < nwords; i += nth) surv[i] = 0u;
+        __syncthreads();
+        for (int q = tid; q < nsurv; q += nth) {
+            const int i = (int) (keys[q] & 0xffffffffu);
+            atomicOr(&surv[i >> 5], 1u << (i & 31));
+        }
+    }
     // (4) repetition penalty over distinct history ids (main.cpp:774-781)
     if (P.repeat_penalty != 1.0f && hl > 0) {
-        for (int i = tid; i < (V + 31) / 32; i += nth) seen[i] = 0u;
+        for (int i = tid; i < nwords; i += nth) seen[i] = 0u;
         __syncthreads();
         for (int j = tid; j < hl; j += nth) {
             const int t = hist[j];
@@ -1483,25 +1523,33 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             const unsigned old = atomicOr(&seen[t >> 5], bit);
             if (old & bit) continue;
             const float v = s[t];
-            if (v == -INFINITY) continue;
+            if (listmode ? (surv[t >> 5] & bit) == 0u : v == -INFINITY) continue;
             s[t] = v > 0.0f ? __fdiv_rn(v, P.repeat_penalty) : __fmul_rn(v, P.repeat_penalty);
         }
-        __syncthreads();
     }
+    __syncthreads();
 
     SAMP_STAMP(9);
     // (5) softmax over survivors in index order (main.cpp:783-793).  Dropped
     // entries have p = 0 and add nothing to any later sum, so only the
     // survivors are compacted (index order: thread t owns [t*per, (t+1)*per))
     // and exponentiated; one whose exp underflows stays in the list with 0.
+    // (list mode: thread t owns bit-set words [t*wper, (t+1)*wper), the
+    // same index order)
     const int per = (V + nth - 1) / nth;
     const int i0 = min(V, tid * per), i1 = min(V, i0 + per);
+    const int wper = (nwords + nth - 1) / nth;
+    const int w0 = min(nwords, tid * wper), w1 = min(nwords, w0 + wper);
     float lm = -INFINITY;
     int cnt = 0;
-    for (int i = i0; i < i1; ++i) { const float v = s[i]; if (v != -INFINITY) { lm = fmaxf(lm, v); ++cnt; } }
+    if (listmode) {
+        for (int q = w0; q < w1; ++q)
+            for (unsigned m = surv[q]; m; m &= m - 1u) { lm = fmaxf(lm, s[q * 32 + __ffs(m) - 1]); ++cnt; }
+    } else {
+        for (int i = i0; i < i1; ++i) { const float v = s[i]; if (v != -INFINITY) { lm = fmaxf(lm, v); ++cnt; } }
+    }
     const float mx = block_max(lm, redf);
     int incl = cnt;
-    const int w = tid >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, incl, o);
@@ -1524,7 +1572,12 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     __syncthreads();
     {
         int o = redi[w] + incl - cnt;
-        for (int i = i0; i < i1; ++i) { const float v = s[i]; if (v != -INFINITY) { lst[o] = i; e[o] = v; ++o; } }
+        if (listmode) {
+            for (int q = w0; q < w1; ++q)
+                for (unsigned m = surv[q]; m; m &= m - 1u) { const int i = q * 32 + __ffs(m) - 1; lst[o] = i; e[o] = s[i]; ++o; }
+        } else {
+            for (int i = i0; i < i1; ++i) { const float v = s[i]; if (v != -INFINITY) { lst[o] = i; e[o] = v; ++o; } }
+        }
     }
     __syncthreads();
     const int cf = shi[4];
