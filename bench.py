@@ -539,18 +539,24 @@ def phase_timeline(pkg, step=5):
         c = c[c >= 0]
         return round(float(np.median(c)) / 1000.0, 2) if c.size else None
 
-    names = {0: "P1 start", 1: "P1 x ready", 13: "P1 LN done", 14: "P1 quant done", 15: "P1 dot done",
-             2: "P1 released", 3: "P2 qkv ready", 4: "P2 released", 5: "P3 att ready", 6: "P4 xm ready",
-             7: "P5 h ready", 10: "P5 quant done", 11: "P5 dot done", 8: "P5 released"}
+    # stamp indices of the Q4_0 kernel (attention CTAs compute their own q/k/v)
+    names = {0: "P1 start", 1: "P1 x ready", 12: "P1 LN done", 14: "P1 K/W staged", 15: "P1 qkv dot done",
+             16: "P1 V issued", 13: "P1 K/V appended", 3: "P2 V ready", 9: "P2 softmax", 17: "P2 PV",
+             18: "P2 head out Q8_0", 19: "P2 partials", 2: "P2 release barrier", 5: "P2 released",
+             4: "P2 next K/W issued", 6: "P4 xm ready", 7: "P5 h ready", 10: "P5 quant done", 11: "P5 dot done",
+             8: "P5 released"}
     out = {"decode_16_steps_ms": ms, "step": step}
     for l in (1, 12):
-        out[f"layer{l}"] = {nm: med(l * 20 + i) for i, nm in names.items()}
-    out["head"] = {"start": med(480), "released": med(481), "sampler logits ready": med(482),
-                   "sampled": med(483), "token seen": med(484)}
-    st = tl[0, 490:506]
+        out[f"layer{l}"] = {nm: med(l * 20 + i) for i, nm in names.items() if med(l * 20 + i) is not None}
+    out["head"] = {"start": med(480), "weights issued": med(489), "x ready": med(487), "dot done": med(488),
+                   "released": med(481), "sampler logits ready": med(482), "sampled": med(483),
+                   "token seen": med(484)}
+    st = tl[0, 490:512]
     stages = ["start", "loaded", "min-p", "top-k", "top-p gathered", "sorted", "top-p exp", "top-p psum",
-              "top-p cut", "penalty", "compacted", "final exp", "final psum", "rng", "dsum", "end"]
-    out["sampler_stages_us"] = {stages[i]: round((st[i] - st[0]) / 1000.0, 2) for i in range(16) if st[i] > 0}
+              "top-p cut", "penalty", "compacted", "final exp", "final psum", "rng", "dsum", "end",
+              "k:hist", "k:scan", "k:scatter", "k:sort", "p:crossing", "p:fallback"]
+    order = sorted([i for i in range(len(stages)) if st[i] > 0], key=lambda i: st[i])
+    out["sampler_stages_us"] = {stages[i]: round((st[i] - st[0]) / 1000.0, 2) for i in order}
     return out
 
 
