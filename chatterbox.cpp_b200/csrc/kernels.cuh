@@ -1120,26 +1120,28 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const float * cond = a.cond + (long long) slot * a.cond_stride;
     const float * unc = a.uncond ? a.uncond + (long long) slot * a.uncond_stride : nullptr;
     const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
+    const int rmode = a.rng_mode ? a.rng_mode[slot] : T3B_RNG_PHILOX;   // loaded early: used at the draw
     const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
 
     // (0) CFG mix, (1) temperature  (main.cpp:735-738).  Each thread issues
-    // its loads four at a time; the max and the count of finite scores are
-    // gathered on the way for min-p and the top-k skip.
+    // its loads eight at a time (through L2: the persistent kernel passes
+    // logits other CTAs have just written); the max and the count of finite
+    // scores are gathered on the way for min-p and the top-k skip.
     const bool cfg = unc != nullptr && P.cfg_weight != 0.0f;
     const bool use_t = P.temp > 0.0f && P.temp != 1.0f;
     const float inv_t = use_t ? __fdiv_rn(1.0f, P.temp) : 1.0f;
     float lmx = -INFINITY, lmn = INFINITY;
     int lfin = 0;
-    for (int i0 = 0; i0 < V; i0 += 4 * nth) {
-        float cv[4], uv[4];
+    for (int i0 = 0; i0 < V; i0 += 8 * nth) {
+        float cv[8], uv[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
             const int i = i0 + q * nth + tid;
-            cv[q] = i < V ? cond[i] : 0.0f;
-            uv[q] = (cfg && i < V) ? unc[i] : 0.0f;
+            cv[q] = i < V ? __ldcg(cond + i) : 0.0f;
+            uv[q] = (cfg && i < V) ? __ldcg(unc + i) : 0.0f;
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
             const int i = i0 + q * nth + tid;
             if (i < V) {
                 float v = cv[q];
@@ -1266,14 +1268,40 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 }
                 __syncthreads();
                 SAMP_STAMP(18);
-                for (int d = tid; d <= dsel; d += nth) {
-                    unsigned long long * kp = keys + start[d];
-                    const int n = hist[d];
-                    for (int x = 1; x < n; ++x) {
-                        const unsigned long long t = kp[x];
-                        int y = x - 1;
-                        while (y >= 0 && kp[y] > t) { kp[y + 1] = kp[y]; --y; }
-                        kp[y + 1] = t;
+                const int nsb = start[dsel] + hist[dsel];   // scattered scores, bins 0..dsel
+                if (nsb <= 2 * nth) {
+                    // each score counts the smaller keys of its bin (<= SAMP_BIN_MAX
+                    // reads) and moves to that rank once every count is known
+                    unsigned long long kq[2];
+                    int pq[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int q = tid + u * nth;
+                        pq[u] = -1;
+                        if (q < nsb) {
+                            const unsigned long long key = keys[q];
+                            const int d = samp_dbin(s[(int) (key & 0xffffffffu)], smin, scale);
+                            const int b = start[d], n = hist[d];
+                            int rk = 0;
+                            for (int j = 0; j < n; ++j) rk += keys[b + j] < key ? 1 : 0;
+                            kq[u] = key;
+                            pq[u] = b + rk;
+                        }
+                    }
+                    __syncthreads();
+#pragma unroll
+                    for (int u = 0; u < 2; ++u)
+                        if (pq[u] >= 0) keys[pq[u]] = kq[u];
+                } else {
+                    for (int d = tid; d <= dsel; d += nth) {   // insertion sort per bin
+                        unsigned long long * kp = keys + start[d];
+                        const int n = hist[d];
+                        for (int x = 1; x < n; ++x) {
+                            const unsigned long long t = kp[x];
+                            int y = x - 1;
+                            while (y >= 0 && kp[y] > t) { kp[y + 1] = kp[y]; --y; }
+                            kp[y + 1] = t;
+                        }
                     }
                 }
                 __syncthreads();
@@ -1630,7 +1658,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             tok = shi[5];
         } else {
             // (7) discrete_distribution draw
-            const int mode = a.rng_mode ? a.rng_mode[slot] : T3B_RNG_PHILOX;
+            const int mode = rmode;
             uint32_t x1, x2;
             if (mode == T3B_RNG_MT19937) {
                 uint32_t * st = a.mt + (size_t) slot * 625;
