@@ -49,7 +49,9 @@
 #define MK_B_HQ (MK_B_PART + 16 * 1024)     // fc output h in Q8_0: quants [4096] i8
 #define MK_B_HD (MK_B_HQ + 1024)            //   block scales [128]
 #define MK_B_HS (MK_B_HD + 128)             //   block sums [128]
-#define MK_B_TOTAL (MK_B_HS + 128)
+#define MK_B_XT (MK_B_HS + 128)             // Q4_0 layout: x as tagged words [1024] u64 (2048 floats)
+#define MK_B_HT (MK_B_XT + 2048)            // Q4_0 layout: h in Q8_0 as tagged words [1280] u64
+#define MK_B_TOTAL (MK_B_HT + 2560)
 enum { MK_C_QKV, MK_C_ATT, MK_C_XM, MK_C_H, MK_C_X, MK_C_LOG, MK_C_TOK, MK_C_N };
 #define MK_C_STRIDE 32   // counters 128 bytes apart
 #define MK_CTL_WORDS ((MK_C_N + 2) * MK_C_STRIDE)   // counters, abort flag, steps done
@@ -77,6 +79,7 @@ struct MegaArgs {
     unsigned long long * tl;       // nullable: [G][MK_TL] globaltimer stamps of step tl_step
     int tl_step;
     int first_tok;                 // token of the first step (< 0: the stream's step_tok)
+    unsigned epoch;                // launch number (1..4095): high bits of the x-word tags
     SampArgs samp;
 };
 #define MK_TL 512
@@ -92,6 +95,7 @@ struct MegaState {
     int * cancel_dev = nullptr;
     int grid = 0;
     size_t smem = 0;
+    unsigned epoch = 0;   // launches so far (mod 4095): tag space of the x words
 };
 inline void mega_free(MegaState & m) {
     if (m.layers) cudaFree(m.layers);
@@ -157,6 +161,48 @@ __device__ __forceinline__ bool mk_wait_vec(const unsigned * c, unsigned target,
     return true;
 }
 
+// x hand-off without a release fence (Q4_0 layout): each element is one
+// 64-bit word {tag, value} stored with a single relaxed store, tag = launch
+// epoch << 20 | layer occurrence k, so a word whose tag matches is the value
+// of that occurrence.  Warp 0 of the consumer polls all 1024 words (32 per
+// lane) until every tag matches, then writes the values to dst (smem).
+__device__ __forceinline__ unsigned mk_xtag(unsigned epoch, unsigned k) { return (epoch << 20) | (k & 0xfffffu); }
+__device__ __forceinline__ void mk_st_x(unsigned long long * p, unsigned tag, float v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((unsigned long long) tag << 32) | __float_as_uint(v))
+                 : "memory");
+}
+__device__ __forceinline__ bool mk_wait_x(const unsigned long long * src, unsigned tag, float * dst, const MegaArgs & a) {
+    __shared__ int okx;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        unsigned long long w[32];
+        int ok = 1;
+        for (unsigned spins = 0;; ++spins) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+                asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w[q]) : "l"(src + q * 32 + lane) : "memory");
+            bool all = true;
+#pragma unroll
+            for (int q = 0; q < 32; ++q) all = all && (unsigned) (w[q] >> 32) == tag;
+            if (__all_sync(0xffffffffu, all)) break;
+            int stop = 0;
+            if (lane == 0 && (spins > MK_SPIN || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag))) {
+                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                stop = 1;
+            }
+            if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
+            __nanosleep(20);
+        }
+        if (ok) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) dst[q * 32 + lane] = __uint_as_float((unsigned) w[q]);
+        }
+        if (lane == 0) okx = ok;
+    }
+    __syncthreads();
+    return okx != 0;
+}
+
 // LayerNorm parameters of this thread's two elements (2*tid, 2*tid+1),
 // loaded before a wait
 struct MkLn { float2 g, b; };
@@ -177,6 +223,50 @@ struct MkAct {
     int * s;        // block sums [K/32]
     __half * h;     // f16 copy [K] (F16 weights)
 };
+
+// h hand-off without a release fence (Q4_0 layout), in the tagged-word form
+// of the x hand-off: words [0, 1024) carry four quants each (block b in words
+// 8b .. 8b+7), words 1024 + b and 1152 + b the block's scale and sum.  Warps
+// 0 and 1 each poll their 640 words (20 per lane) until every tag matches.
+#define MK_HT_WORDS 1280
+__device__ __forceinline__ bool mk_wait_h(const unsigned long long * src, unsigned tag, const MkAct & x, const MegaArgs & a) {
+    __shared__ int okh[2];
+    if (threadIdx.x < 64) {
+        const int t = threadIdx.x, lane = t & 31;
+        unsigned long long w[MK_HT_WORDS / 64];
+        int ok = 1;
+        for (unsigned spins = 0;; ++spins) {
+#pragma unroll
+            for (int q = 0; q < MK_HT_WORDS / 64; ++q)
+                asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w[q]) : "l"(src + q * 64 + t) : "memory");
+            bool all = true;
+#pragma unroll
+            for (int q = 0; q < MK_HT_WORDS / 64; ++q) all = all && (unsigned) (w[q] >> 32) == tag;
+            if (__all_sync(0xffffffffu, all)) break;
+            int stop = 0;
+            if (lane == 0 && (spins > MK_SPIN || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag))) {
+                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                stop = 1;
+            }
+            if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
+            __nanosleep(20);
+        }
+        if (ok) {
+#pragma unroll
+            for (int q = 0; q < MK_HT_WORDS / 64; ++q) {
+                const int j = q * 64 + t;
+                const unsigned v = (unsigned) w[q];
+                if (j < 1024) *(unsigned *) (x.q + 4 * j) = v;
+                else if (j < 1152) x.d[j - 1024] = __uint_as_float(v);
+                else x.s[j - 1152] = (int) v;
+            }
+        }
+        if (lane == 0) okh[t >> 5] = ok;
+    }
+    __syncthreads();
+    return okh[0] != 0 && okh[1] != 0;
+}
+
 
 // Sum over the CTA in double with a single barrier: warp trees, then every
 // warp reduces the 16 warp partials itself (same order in every warp).
@@ -431,7 +521,7 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 // LN_f + speech_head rows of this CTA; the head keeps its own weight type.
 template <int HT>
 __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const MkAct & act, float * part,
-                                     float * rowsum, double * redd) {
+                                     float * rowsum, double * redd, float * xbuf, bool tagged) {
     const int D = 1024, tid = threadIdx.x, G = gridDim.x;
     const int r0 = mk_r0(a.V, blockIdx.x, G), r1 = mk_r0(a.V, blockIdx.x + 1, G);
     MkPref<HT> pf;
@@ -441,8 +531,14 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
     const int cta = blockIdx.x;
     MK_STAMP(489);
-    if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
-    const float2 xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
+    float2 xv;
+    if (tagged) {
+        if (!mk_wait_x((const unsigned long long *) (a.buf + MK_B_XT), mk_xtag(a.epoch, kx), xbuf, a)) return false;
+        xv = *(const float2 *) (xbuf + 2 * tid);
+    } else {
+        if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
+        xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
+    }
     MK_STAMP(487);
     mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, HT == T3B_F16);
     mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
@@ -624,6 +720,8 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // scratch (reused by every phase): vec[4096] f32 | q[4096] i8 | d,s [128] | h[4096] f16 | part
     constexpr bool FUSE = T != T3B_F16;   // out-projection folded into the attention CTAs
     constexpr bool OWN = T == T3B_Q4_0;   // attention CTAs compute their head's q/k/v themselves
+    constexpr bool LLX = OWN;             // x and h handed off as tagged words (no release fence)
+    unsigned long long * bXT = (unsigned long long *) (a.buf + MK_B_XT);
     float * vec = (float *) smem;         // (Q8_0 / F16 layout only)
     MkAct act;
     float * part;
@@ -765,7 +863,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 const float bq = att && tid < 3 * T3B_HD ? __ldg(Ly.bqkv + (tid >> 6) * D + hh_ * T3B_HD + (tid & 63)) : 0.0f;
                 MK_STAMP(l * 20 + 0);
                 float2 xv;
-                if (l > 0) {
+                if (l > 0 && LLX) {
+                    if (!mk_wait_x(bXT, mk_xtag(a.epoch, k - 1u), xres, a)) MK_BAIL;
+                    xv = *(const float2 *) (xres + 2 * tid);
+                } else if (l > 0) {
                     if (!mk_acquire(cX, (k - 1u) * GW, a)) MK_BAIL;
                     xv = __ldcg((const float2 *) bX + tid);
                     *(float2 *) (xres + 2 * tid) = xv;
@@ -1121,17 +1222,35 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             int sq = q;
 #pragma unroll
                             for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-                            bHQ[r0_ + tid] = (int8_t) q;
-                            if (lane == 0) {
-                                bHD[(r0_ >> 5) + w] = __half2float(__float2half_rn(d));
-                                bHS[(r0_ >> 5) + w] = sq;
+                            if (LLX) {
+                                // four lanes' quants per tagged word
+                                const unsigned qb = (unsigned) q & 0xffu;
+                                const unsigned q1 = __shfl_down_sync(0xffffffffu, qb, 1);
+                                const unsigned q2 = __shfl_down_sync(0xffffffffu, qb, 2);
+                                const unsigned q3 = __shfl_down_sync(0xffffffffu, qb, 3);
+                                const int b = (r0_ >> 5) + w;
+                                const unsigned tg = mk_xtag(a.epoch, k);
+                                unsigned long long * ht = (unsigned long long *) (a.buf + MK_B_HT);
+                                if ((lane & 3) == 0)
+                                    mk_st_x(ht + b * 8 + (lane >> 2), tg, __uint_as_float(qb | (q1 << 8) | (q2 << 16) | (q3 << 24)));
+                                if (lane == 0) {
+                                    mk_st_x(ht + 1024 + b, tg, __half2float(__float2half_rn(d)));
+                                    mk_st_x(ht + 1152 + b, tg, __int_as_float(sq));
+                                }
+                            } else {
+                                bHQ[r0_ + tid] = (int8_t) q;
+                                if (lane == 0) {
+                                    bHD[(r0_ >> 5) + w] = __half2float(__float2half_rn(d));
+                                    bHS[(r0_ >> 5) + w] = sq;
+                                }
                             }
                         }
                     } else if (tid < r1_ - r0_) {
                         bH[r0_ + tid] = gelu_ggml(__fadd_rn(rowsum[tid], bias));
                     }
                 }
-                mk_release(cH);
+                if (LLX) __syncthreads();
+                else mk_release(cH);
             }
             // ---------------- P5: fc2 + bias + residual ------------------------
             if (worker) {
@@ -1142,11 +1261,15 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
                 if (FUSE) {
                     // h arrives in Q8_0: 4096 quants, 128 scales, 128 sums
-                    if (!mk_acquire(cH, k * GW, a)) MK_BAIL;
-                    if (tid < 256) *(int4 *) (act.q + 16 * tid) = __ldcg((const int4 *) bHQ + tid);
-                    else if (tid < 384) act.d[tid - 256] = __ldcg(bHD + tid - 256);
-                    else act.s[tid - 384] = __ldcg(bHS + tid - 384);
-                    __syncthreads();
+                    if (LLX) {
+                        if (!mk_wait_h((const unsigned long long *) (a.buf + MK_B_HT), mk_xtag(a.epoch, k), act, a)) MK_BAIL;
+                    } else {
+                        if (!mk_acquire(cH, k * GW, a)) MK_BAIL;
+                        if (tid < 256) *(int4 *) (act.q + 16 * tid) = __ldcg((const int4 *) bHQ + tid);
+                        else if (tid < 384) act.d[tid - 256] = __ldcg(bHD + tid - 256);
+                        else act.s[tid - 384] = __ldcg(bHS + tid - 384);
+                        __syncthreads();
+                    }
                     MK_STAMP(l * 20 + 7);
                 } else {
                     if (!mk_wait_vec(cH, k * GW, bH, 4 * D, vec, a)) MK_BAIL;
@@ -1158,9 +1281,12 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 MK_STAMP(l * 20 + 11);
                 if (tid < r1_ - r0_) {
                     const int n = r0_ + tid;
-                    bX[n] = __fadd_rn(__fadd_rn(rowsum[tid], bias), xmid[n]);
+                    const float xo = __fadd_rn(__fadd_rn(rowsum[tid], bias), xmid[n]);
+                    if (LLX) mk_st_x(bXT + n, mk_xtag(a.epoch, k), xo);
+                    else bX[n] = xo;
                 }
-                mk_release(cX);
+                if (LLX) __syncthreads();
+                else mk_release(cX);
                 MK_STAMP(l * 20 + 8);
             }
         }
@@ -1168,9 +1294,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         MK_STAMP(480);
         {
             bool ok;
-            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, GW, act, part, rowsum, redd);
-            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, GW, act, part, rowsum, redd);
-            else ok = mk_head<T3B_Q4_0>(a, step, GW, act, part, rowsum, redd);
+            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, GW, act, part, rowsum, redd, xres, LLX);
+            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, GW, act, part, rowsum, redd, xres, LLX);
+            else ok = mk_head<T3B_Q4_0>(a, step, GW, act, part, rowsum, redd, xres, LLX);
             if (!ok) MK_BAIL;
         }
         // OWN: layer 0 of the next step (K rows up to this step's position)

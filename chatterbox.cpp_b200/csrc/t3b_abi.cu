@@ -793,6 +793,7 @@ int mega_prepare(t3b_ctx * ctx) {
     CK(cudaMalloc(&m.layers, sizeof(MkLayer) * hl.size()));
     CK(cudaMemcpy(m.layers, hl.data(), sizeof(MkLayer) * hl.size(), cudaMemcpyHostToDevice));
     CK(cudaMalloc(&m.buf, sizeof(float) * MK_B_TOTAL));
+    CK(cudaMemset(m.buf, 0, sizeof(float) * MK_B_TOTAL));   // x-word tags start unused (epoch 0)
     // counters | abort flag | steps done, each on its own 128-byte line: one memset per launch
     CK(cudaMalloc(&m.cnt, sizeof(unsigned) * MK_CTL_WORDS));
     m.abort_flag = (int *) (m.cnt + MK_C_N * MK_C_STRIDE);
@@ -840,6 +841,8 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     a.samp = sampler_args(ctx, false);
     a.samp.done = nullptr;
     a.first_tok = first_tok;
+    m.epoch = m.epoch % 4095u + 1u;   // 1..4095, never the same as the previous launch's
+    a.epoch = m.epoch;
     CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_CTL_WORDS, st));
     // debug: T3B_MK_TIMELINE=<file> stamps every phase boundary of step
     // T3B_MK_TIMELINE_STEP (default 2) per CTA and writes [G][256] u64 ns

@@ -248,6 +248,36 @@ def test_decode_loop_matches_oracle(pkg, orc, quant, graph_path):
             lo = mir.step(P + i, int(toks[i]))
 
 
+@pytest.mark.parametrize("n_text", [248, 266])
+def test_decode_long_context_matches_oracle(pkg, orc, n_text):
+    """Persistent kernel, Q4_0, at positions where K and V no longer fit the
+    attention CTA's K stage together (pos >= 320: V is staged separately);
+    n_text = 248 starts the decode at 312 and crosses that boundary inside
+    one launch.  Tokens equal the oracle sampler's draws on the device
+    logits; logits within the Q4_0 bound of the oracle's teacher-forced
+    logits."""
+    hp, t, m = model(pkg, "q4_0", 2)
+    m.alloc_streams(1, 512)
+    text = _prompt(21, n_text)
+    params = dict(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2)
+    seed, steps = 4321, 16
+    toks, tr = _decode_traced(pkg, m, text, params, seed, steps, False)
+    assert toks.size == steps + 1
+    words = orc.mt19937_words(seed, 0, 2 * steps + 4)
+    mir = orc.Model(hp, t, max_ctx=512, gemv_mode=1, gelu_f16=1, kv_f16=1)
+    P, lo = mir.prompt(text)
+    assert P == n_text + 64
+    nz = max(noise_floor(orc, hp, t, text, [int(x) for x in toks[:steps]], 512))
+    for i in range(steps + 1):
+        tok, aux = orc.sample(tr[i], params, words[2 * i], words[2 * i + 1], hist=toks[:i].astype(np.int32))
+        if not aux[2]:
+            assert tok == toks[i], (i, tok, toks[i])
+        e = rel_err(tr[i], lo)
+        assert e < bound("q4_0", nz, 1e-3), (i, e, nz)
+        if i < steps:
+            lo = mir.step(P + i, int(toks[i]))
+
+
 def test_megakernel_matches_graph_path(pkg):
     """F16 weights: the persistent kernel and the graph loop sample the same
     first token from identical prefill logits and produce step-1 logits that
