@@ -1338,7 +1338,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     // List mode: with the fast path the survivors of top-k (and below, of
     // top-p) are keys[0 .. nsurv) and s[] is not masked; a bit set marks them
     // for the penalty and the index-order compaction.
-    const bool listmode = fastc >= 0;
+    bool listmode = fastc >= 0;
     int nsurv = fastc;
     if (listmode) topk_pending = false;
     if (fastc < 0 && P.top_k > 0 && P.top_k < V && nfin > P.top_k) {
@@ -1516,13 +1516,13 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 __syncthreads();
             }
             SAMP_STAMP(21);
-            const int cut = j < c ? j + 1 : c;
-            if (listmode) {
-                nsurv = cut;
-            } else {
-                for (int q = cut + tid; q < c; q += nth) s[(int) (keys[q] & 0xffffffffu)] = -INFINITY;
-                __syncthreads();
-            }
+            // the survivors are keys[0 .. cut): list mode from here on (the
+            // top-k drop was applied by the gather or is implied by the list)
+            listmode = true;
+            nsurv = j < c ? j + 1 : c;
+        } else {
+            listmode = true;   // nothing survived
+            nsurv = 0;
         }
     }
     if (topk_pending) {

@@ -518,43 +518,6 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 // phase timeline (debug): stamp point `i` of the traced step
 #define MK_STAMP(i) do { if (a.tl && step == a.tl_step && tid == 0) a.tl[(size_t) cta * MK_TL + (i)] = globaltimer_ns(); } while (0)
 
-// LN_f + speech_head rows of this CTA; the head keeps its own weight type.
-template <int HT>
-__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const MkAct & act, float * part,
-                                     float * rowsum, double * redd, float * xbuf, bool tagged) {
-    const int D = 1024, tid = threadIdx.x, G = gridDim.x;
-    const int r0 = mk_r0(a.V, blockIdx.x, G), r1 = mk_r0(a.V, blockIdx.x + 1, G);
-    MkPref<HT> pf;
-    mk_prefetch<HT>(a.head, D, r0, r1, pf);
-    const MkLn lp = mk_ln_prefetch(a.lnfg, a.lnfb);
-    const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
-    const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
-    const int cta = blockIdx.x;
-    MK_STAMP(489);
-    float2 xv;
-    if (tagged) {
-        if (!mk_wait_x((const unsigned long long *) (a.buf + MK_B_XT), mk_xtag(a.epoch, kx), xbuf, a)) return false;
-        xv = *(const float2 *) (xbuf + 2 * tid);
-    } else {
-        if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
-        xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
-    }
-    MK_STAMP(487);
-    mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, HT == T3B_F16);
-    mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
-    MK_STAMP(488);
-    float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
-    float * lg = a.buf + MK_B_LOG;
-    if (tid < r1 - r0) {
-        const int n = r0 + tid;
-        const float v = __fadd_rn(rowsum[tid], hb);
-        if (tr) tr[n] = v;
-        if (a.logits_out) a.logits_out[n] = v;
-        lg[n] = v;
-    }
-    mk_release(a.cnt + MK_C_LOG * MK_C_STRIDE);
-    return true;
-}
 
 // Dynamic shared memory.  Q4_0 layers (the attention CTAs compute their
 // head's q/k/v rows from weights staged in shared memory):
@@ -672,6 +635,95 @@ __device__ __forceinline__ void mk_qkv_own(const unsigned char * wst, const MkAc
     }
 }
 
+// Row sums of `rows` (<= 64) staged Q4_0 rows of K = 1024 with the lane
+// layout of mk_qkv_own (8 lanes per row, blocks c, c+8, c+16, c+24).
+__device__ __forceinline__ void mk_rows_q4_smem(const unsigned char * wst, int rows, const MkAct & x, float * out) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, g = lane >> 3, c = lane & 7;
+    const int row = w * 4 + g;   // 16 warps x 4 row groups
+    float t = 0.0f;
+    if (row < rows) {
+        const unsigned char * rp = wst + (size_t) row * MK_QKVW_ROW;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int b = c + 8 * j;
+            const int4 xa = *(const int4 *) (x.q + b * 32), xb = *(const int4 *) (x.q + b * 32 + 16);
+            const uint4 qv = *(const uint4 *) (rp + b * 16);
+            const float dw = __half2float(*(const __half *) (rp + 512 + b * 2));
+            int si = 0;
+            si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), xa.x, si);
+            si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), xb.x, si);
+            si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), xa.y, si);
+            si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), xb.y, si);
+            si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), xa.z, si);
+            si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), xb.z, si);
+            si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), xa.w, si);
+            si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), xb.w, si);
+            si -= 8 * x.s[b];
+            t = __fadd_rn(t, __fmul_rn(__fmul_rn((float) si, dw), x.d[b]));
+        }
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (c == 0 && row < rows) out[row] = t;
+}
+
+// LN_f + speech_head rows of this CTA; the head keeps its own weight type.
+// hw (Q4_0 head, Q4_0 layers): this CTA's head rows, bulk-copied into
+// shared memory during the last layer (completion: phase `hpar` of hmb);
+// the dot then reads them there instead of a register prefetch, whose issue
+// alone took ~3 us.
+template <int HT>
+__device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const MkAct & act, float * part,
+                                     float * rowsum, double * redd, float * xbuf, bool tagged,
+                                     const unsigned char * hw, unsigned long long * hmb, unsigned hpar) {
+    const int D = 1024, tid = threadIdx.x, G = gridDim.x;
+    const int r0 = mk_r0(a.V, blockIdx.x, G), r1 = mk_r0(a.V, blockIdx.x + 1, G);
+    MkPref<HT> pf;
+    if (!hw) mk_prefetch<HT>(a.head, D, r0, r1, pf);
+    const MkLn lp = mk_ln_prefetch(a.lnfg, a.lnfb);
+    const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
+    const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
+    const int cta = blockIdx.x;
+    MK_STAMP(489);
+    float2 xv;
+    if (tagged) {
+        if (!mk_wait_x((const unsigned long long *) (a.buf + MK_B_XT), mk_xtag(a.epoch, kx), xbuf, a)) return false;
+        xv = *(const float2 *) (xbuf + 2 * tid);
+    } else {
+        if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
+        xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
+    }
+    MK_STAMP(487);
+    mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, HT == T3B_F16);
+    if (hw) {
+        __shared__ int okhd;
+        if (tid == 0) {
+            const bool ok = mk_mbar_wait(hmb, hpar);
+            if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+            okhd = ok;
+        }
+        __syncthreads();
+        if (!okhd) return false;
+        mk_rows_q4_smem(hw, r1 - r0, act, rowsum);
+        __syncthreads();
+    } else {
+        mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
+    }
+    MK_STAMP(488);
+    float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
+    float * lg = a.buf + MK_B_LOG;
+    if (tid < r1 - r0) {
+        const int n = r0 + tid;
+        const float v = __fadd_rn(rowsum[tid], hb);
+        if (tr) tr[n] = v;
+        if (a.logits_out) a.logits_out[n] = v;
+        lg[n] = v;
+    }
+    mk_release(a.cnt + MK_C_LOG * MK_C_STRIDE);
+    return true;
+}
+
+
 // Bulk prefetch of a CTA's weight slice into L2 (one instruction, no
 // completion to track): issued one phase ahead so the register prefetch of
 // that phase hits L2 instead of HBM.
@@ -705,6 +757,7 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
             if (kw_out >= 0) mk_mbar_wait(&mbar[0], (unsigned) kw_out & 1u);          \
             if (v_out >= 0) mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u);            \
         }                                                                             \
+        if (OWN && tid == 0 && hd_out >= 0) mk_mbar_wait(&mbar[2], (unsigned) hd_out & 1u); \
         return;                                                                       \
     } while (0)
 
@@ -770,15 +823,31 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // otherwise mbar[1] = the V rows, loaded into the weight stage after the
     // q/k/v rows are computed (vph counts its phases).  kw_out / v_out: phase
     // of a copy issued and not yet waited for.
-    __shared__ __align__(8) unsigned long long mbar[2];
+    // mbar[2] (every CTA, Q4_0 head): this CTA's head rows, one phase per step.
+    __shared__ __align__(8) unsigned long long mbar[3];
     __shared__ int okf;
-    int kw_out = -1, v_out = -1, vph = 0;
-    if (OWN && att && tid == 0) {
+    int kw_out = -1, v_out = -1, vph = 0, hd_out = -1;
+    if (OWN && tid == 0) {
         mk_mbar_init(&mbar[0]);
         mk_mbar_init(&mbar[1]);
+        mk_mbar_init(&mbar[2]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    // Q4_0 head with at most 64 rows per CTA: its rows are bulk-copied into the
+    // K stage (free by then in every CTA) during the last layer, when no fenced
+    // release can be waiting: the attention CTAs have all released and the x/h
+    // hand-offs are tagged
+    const int hr0 = mk_r0(a.V, cta, G), hr1 = mk_r0(a.V, cta + 1, G);
+    const bool hstage = OWN && a.head.type == T3B_Q4_0 && hr1 - hr0 <= 64 && a.head.rb == MK_QKVW_ROW;
+    auto issue_head = [&](int step_) {
+        if (tid == MK_THREADS - 32) {
+            const unsigned bytes = (unsigned) (hr1 - hr0) * MK_QKVW_ROW;
+            mk_mbar_expect(&mbar[2], bytes);
+            if (bytes) mk_bulk_g2s(kst, a.head.w + (size_t) hr0 * MK_QKVW_ROW, bytes, &mbar[2]);
+        }
+        hd_out = step_;
+    };
     // OWN attention CTAs: bulk copies of use u's K rows [0, npos) of layer nl
     // and of that layer's q/k/v weights for this head, issued by the last
     // warp's first thread (not the hand-off poller)
@@ -1145,11 +1214,12 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 // K and V rows are consumed (the release's barrier): stage the
                 // next layer's (use k); layer 0 of the next step is staged
                 // after the head, whose release would otherwise wait for it
-                if (OWN && l + 1 < NL) {
+                if (OWN && (l + 1 < NL || hstage)) {
                     // only once every head has released: bulk traffic in
                     // flight slows the release of the CTAs still storing
                     if (!mk_acquire(cATT, k * Hn, a)) MK_BAIL;
-                    issue_kw((int) k, l + 1, pos);
+                    if (l + 1 < NL) issue_kw((int) k, l + 1, pos);
+                    else issue_head(step);
                 }
                 MK_STAMP(l * 20 + 4);
             }
@@ -1207,6 +1277,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 if (r1_ > r0_) {   // CTA-uniform
                     mk_ln_quant(x0, x1, lp, a.eps, redd, act, T == T3B_F16);
                     mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                    if (OWN) MK_STAMP(l * 20 + 10);   // fc dot done
                     if (FUSE) {
                         // warp w: GELU of block w of this CTA's rows, then
                         // Q8_0 with the arithmetic of mk_quant_block
@@ -1259,10 +1330,12 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 mk_prefetch<T>(Ly.fc2, 4 * D, r0_, r1_, pf_);
                 if (l + 1 < NL && !OWN) mk_l2_prefetch(a.layers[l + 1].qkv, 3 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
+                if (OWN) MK_STAMP(l * 20 + 3);   // fc2 weights issued
                 if (FUSE) {
                     // h arrives in Q8_0: 4096 quants, 128 scales, 128 sums
                     if (LLX) {
                         if (!mk_wait_h((const unsigned long long *) (a.buf + MK_B_HT), mk_xtag(a.epoch, k), act, a)) MK_BAIL;
+                        if (l + 1 == NL && hstage) issue_head(step);
                     } else {
                         if (!mk_acquire(cH, k * GW, a)) MK_BAIL;
                         if (tid < 256) *(int4 *) (act.q + 16 * tid) = __ldcg((const int4 *) bHQ + tid);
@@ -1276,7 +1349,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     MK_STAMP(l * 20 + 7);
                     mk_quantize(act, 4 * D, true);
                 }
-                MK_STAMP(l * 20 + 10);
+                if (!OWN) MK_STAMP(l * 20 + 10);
                 mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
                 MK_STAMP(l * 20 + 11);
                 if (tid < r1_ - r0_) {
@@ -1294,9 +1367,14 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         MK_STAMP(480);
         {
             bool ok;
-            if (a.head.type == T3B_F16) ok = mk_head<T3B_F16>(a, step, GW, act, part, rowsum, redd, xres, LLX);
-            else if (a.head.type == T3B_Q8_0) ok = mk_head<T3B_Q8_0>(a, step, GW, act, part, rowsum, redd, xres, LLX);
-            else ok = mk_head<T3B_Q4_0>(a, step, GW, act, part, rowsum, redd, xres, LLX);
+            if (a.head.type == T3B_F16)
+                ok = mk_head<T3B_F16>(a, step, GW, act, part, rowsum, redd, xres, LLX, nullptr, nullptr, 0u);
+            else if (a.head.type == T3B_Q8_0)
+                ok = mk_head<T3B_Q8_0>(a, step, GW, act, part, rowsum, redd, xres, LLX, nullptr, nullptr, 0u);
+            else
+                ok = mk_head<T3B_Q4_0>(a, step, GW, act, part, rowsum, redd, xres, LLX, hstage ? (const unsigned char *) kst : nullptr,
+                                       &mbar[2], (unsigned) step & 1u);
+            if (ok) hd_out = -1;
             if (!ok) MK_BAIL;
         }
         // OWN: layer 0 of the next step (K rows up to this step's position)
