@@ -570,6 +570,13 @@ __device__ __forceinline__ bool mk_mbar_wait(unsigned long long * mb, unsigned p
         __nanosleep(20);
     }
 }
+// bulk copy of weights: L2 evict-first, like every other weight stream
+__device__ __forceinline__ void mk_bulk_g2s_w(void * dst, const void * src, unsigned bytes, unsigned long long * mb) {
+    unsigned long long pol;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                 ::"r"(mk_saddr(dst)), "l"(src), "r"(bytes), "r"(mk_saddr(mb)), "l"(pol) : "memory");
+}
 __device__ __forceinline__ void mk_fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
 // head h's q, k and v rows (64 each) of a Q4_0 q/k/v matrix (K = 1024):
 // three contiguous sections, one bulk copy each
@@ -844,7 +851,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         if (tid == MK_THREADS - 32) {
             const unsigned bytes = (unsigned) (hr1 - hr0) * MK_QKVW_ROW;
             mk_mbar_expect(&mbar[2], bytes);
-            if (bytes) mk_bulk_g2s(kst, a.head.w + (size_t) hr0 * MK_QKVW_ROW, bytes, &mbar[2]);
+            if (bytes) mk_bulk_g2s_w(kst, a.head.w + (size_t) hr0 * MK_QKVW_ROW, bytes, &mbar[2]);
         }
         hd_out = step_;
     };
