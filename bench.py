@@ -541,10 +541,10 @@ def phase_timeline(pkg, step=5):
 
     # stamp indices of the Q4_0 kernel (attention CTAs compute their own q/k/v)
     names = {0: "P1 start", 1: "P1 x ready", 12: "P1 LN done", 14: "P1 K/W staged", 15: "P1 qkv dot done",
-             16: "P1 V issued", 13: "P1 K/V appended", 3: "P2 V ready", 9: "P2 softmax", 17: "P2 PV",
+             16: "P1 V issued", 13: "P1 K/V appended", 9: "P2 softmax", 17: "P2 PV",
              18: "P2 head out Q8_0", 19: "P2 partials", 2: "P2 release barrier", 5: "P2 released",
-             4: "P2 next K/W issued", 6: "P4 xm ready", 7: "P5 h ready", 10: "P5 quant done", 11: "P5 dot done",
-             8: "P5 released"}
+             4: "P2 next K/W issued", 6: "P4 xm ready", 10: "P4 fc dot done", 3: "P5 fc2 issued",
+             7: "P5 h ready", 11: "P5 dot done", 8: "P5 released"}
     out = {"decode_16_steps_ms": ms, "step": step}
     for l in (1, 12):
         out[f"layer{l}"] = {nm: med(l * 20 + i) for i, nm in names.items() if med(l * 20 + i) is not None}
