@@ -14,17 +14,22 @@
 // issues the loads of its weight slice for a phase BEFORE waiting for that
 // phase's input, so weight streaming overlaps the dependency latency.
 //
-// Phases per layer (rows split evenly over the G CTAs):
+// Phases per layer, Q8_0 / F16 weights (rows split evenly over the G CTAs):
 //   P1 LN1 + QKV GEMV (+ K/V append to the f16 cache)        -> q,k,v slots
-//   P2 attention, CTA h < n_head owns head h; for Q4_0/Q8_0 weights the same
-//      CTA also quantises its 64 outputs (Q8_0 blocks 2h, 2h+1) and forms the
+//   P2 attention, CTA h < n_head owns head h; for Q8_0 weights the same CTA
+//      also quantises its 64 outputs (Q8_0 blocks 2h, 2h+1) and forms the
 //      out-projection over them for all 1024 rows       -> per-head partials
 //   P3 (F16 weights only) proj GEMV + bias + residual        -> x_mid slots
 //   P4 x_mid = sum of the 16 head partials + bias + residual (every CTA),
 //      LN2 + fc GEMV + bias + GELU                            -> h slots
 //   P5 fc2 GEMV + bias + residual                             -> x slots
-// then LN_f + head GEMV -> logit slots, CTA 0 runs the sampler, publishes
-// the token slot, and every CTA builds the next step's embedding itself.
+// Q4_0 weights ("OWN" layout): CTAs 1..16 are attention CTAs that compute
+// their own head's q/k/v rows from weights bulk-copied into shared memory
+// during the previous layer (no q/k/v hand-off), then P2 as above; the other
+// 132 CTAs are workers that run P4 and P5 alone; x and h move as tagged
+// 64-bit words (value + launch/layer tag) instead of counter hand-offs.
+// Then LN_f + head GEMV -> logit slots, CTA 0 runs the sampler, publishes the
+// token slot, and every CTA builds the next step's embedding itself.
 //
 // Every wait is bounded (MK_SPIN polls); on timeout the CTA raises the abort
 // flag and the error word, and all CTAs leave at their next wait.
