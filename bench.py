@@ -259,8 +259,10 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    n_launch0 = m.launch_count()
     toks = m.decode([params], K, ignore_stop=True)[0]
     dev_ms = m.last_device_ms()
+    n_launch = m.launch_count() - n_launch0
     torch.cuda.synchronize()
     time.sleep(0.25)
     clk.__exit__()
@@ -315,7 +317,7 @@ def main():
             "batched_kernels": batched_kernels(pkg, torch, peak),
             "gemv_sweep": gemv_sweep(pkg, torch, peak) if not args.no_batched else None,
             "e2e": e2e, "clocks": clk.summary(),
-            "gpu_launches": 2,   # first-token sampler + one t3_decode_megakernel launch
+            "gpu_launches": n_launch,   # counted by the library (t3b_launch_count) over the timed decode
             "tokens_head": [int(x) for x in toks[:8]]}
     if ws == 1 and not args.no_cpu_baseline:   # the CPU baseline is measured at N = 1 only
         line["cpu_baseline"] = cpu_reference(args, hp, t, text, "port")

@@ -29,6 +29,8 @@ EXPORTS = [
     "t3b_set_rng", "t3b_set_rng_state", "t3b_get_rng_state", "t3b_set_history", "t3b_decode", "t3b_cancel",
     "t3b_last_device_ms", "t3b_stream_handle", "t3b_trace_logits", "t3b_get_logits_trace", "t3b_op_row_bytes", "t3b_op_repack", "t3b_op_gemv", "t3b_op_attention",
     "t3b_op_sample_philox", "t3b_expf_fixup_count", "t3b_op_expf", "t3b_op_attention_noalloc",
+    "t3b_trace_hidden", "t3b_get_hidden_trace", "t3b_set_wait_limit", "t3b_launch_count", "t3b_s3gen_tokens",
+    "t3b_op_check",
 ]
 
 
@@ -101,6 +103,12 @@ def lib():
             "t3b_op_sample_philox": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, C.c_int, vp, vp, vp, vp, vp]),
             "t3b_expf_fixup_count": (C.c_int, []),
             "t3b_op_expf": (C.c_int, [vp, vp, C.c_int, vp]),
+            "t3b_trace_hidden": (C.c_int, [vp, C.c_int]),
+            "t3b_get_hidden_trace": (C.c_int, [vp, vp]),
+            "t3b_set_wait_limit": (C.c_int, [vp, C.c_uint]),
+            "t3b_launch_count": (C.c_uint64, [vp]),
+            "t3b_s3gen_tokens": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, C.c_int, vp]),
+            "t3b_op_check": (C.c_int, [vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -238,6 +246,28 @@ class T3Model:
         out = np.zeros((n, self.V), np.float32)
         check(lib().t3b_get_logits_trace(self.ctx, _ptr(out), n), self.ctx)
         return out
+
+    def trace_hidden(self, on=True):
+        """Record the residual stream of the next step's first row (embedding
+        and every layer's output)."""
+        check(lib().t3b_trace_hidden(self.ctx, 1 if on else 0), self.ctx)
+
+    def hidden_trace(self):
+        out = np.zeros((self.hp["n_layer"] + 1, self.hp["n_embd"]), np.float32)
+        check(lib().t3b_get_hidden_trace(self.ctx, _ptr(out)), self.ctx)
+        return out
+
+    def set_wait_limit(self, polls):
+        """Polls before a persistent-kernel wait gives up (0 = default)."""
+        check(lib().t3b_set_wait_limit(self.ctx, int(polls)), self.ctx)
+
+    def launch_count(self):
+        return int(lib().t3b_launch_count(self.ctx))
+
+    def s3gen_tokens(self, stream, tokens_dev_ptr, cap, n_dev_ptr, append_silence=True, consumer_stream=None):
+        """S3Gen hand-off: the stream's speech tokens into a device buffer."""
+        check(lib().t3b_s3gen_tokens(self.ctx, stream, tokens_dev_ptr, int(cap), n_dev_ptr,
+                                     1 if append_silence else 0, consumer_stream), self.ctx)
 
     def stream_handle(self):
         """cudaStream_t of this context (int), e.g. for torch.cuda.ExternalStream."""

@@ -8,6 +8,13 @@
 #define T3B_ATTN_CHUNK 128   // keys per attention CTA (one key per thread)
 #define T3B_ATTN_ROWS_MIN 8  // from this many query rows on, one CTA per (row, head) walks all keys
 
+// S3Gen's token input (src/chatterbox_tts.cpp:1389-1398,
+// include/tts-cpp/chatterbox/s3gen_pipeline.h:15): its speech vocabulary,
+// the silence token and the lookahead silence appended to a final chunk.
+#define T3B_S3_VOCAB 6561
+#define T3B_S3_SILENCE 4299
+#define T3B_S3_LOOKAHEAD 3
+
 // Device-side error word bits (read back by the host after a launch).
 #define T3B_DEVERR_TOKEN   1u   // token id outside the embedding table
 #define T3B_DEVERR_POS     2u   // position outside the KV cache / wpe table

@@ -1768,3 +1768,46 @@ __global__ void advance_pos_kernel(int * pos, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) pos[i] += 1;
 }
+
+// S3Gen's token input taken from a stream's history on the device, the
+// preprocessing s3gen_synthesize_to_wav applies (src/chatterbox_tts.cpp:
+// 1389-1398): ids in [0, s3_vocab) kept in order (the start and stop tokens
+// drop out), then `sil` copies of the silence token.  One CTA of 1024
+// threads compacts the history chunk by chunk (ballot + warp-total scan).
+// *n_out = tokens written, or -1 when they do not fit `cap`.
+__global__ __launch_bounds__(1024) void s3gen_tokens_kernel(const int * __restrict__ hist, const int * __restrict__ hist_len,
+                                                            int s3_vocab, int sil_tok, int sil, int * __restrict__ out,
+                                                            int cap, int * __restrict__ n_out) {
+    __shared__ int wtot[32];
+    __shared__ int base_s;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int n = *hist_len;
+    int base = 0;
+    for (int c0 = 0; c0 < n; c0 += 1024) {
+        const int i = c0 + tid;
+        const int t = i < n ? hist[i] : -1;
+        const bool keep = t >= 0 && t < s3_vocab;
+        const unsigned b = __ballot_sync(0xffffffffu, keep);
+        const int in_warp = __popc(b & ((1u << lane) - 1u));
+        if (lane == 0) wtot[w] = __popc(b);
+        __syncthreads();
+        if (w == 0) {
+            const int v = wtot[lane];
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += u;
+            }
+            wtot[lane] = incl - v;                      // exclusive prefix of the warp totals
+            if (lane == 31) base_s = base + incl;       // next chunk's base
+        }
+        __syncthreads();
+        const int dst = base + wtot[w] + in_warp;
+        if (keep && dst < cap) out[dst] = t;
+        base = base_s;
+        __syncthreads();
+    }
+    if (tid < sil && base + tid < cap) out[base + tid] = sil_tok;
+    if (tid == 0) *n_out = base + sil <= cap ? base + sil : -1;
+}

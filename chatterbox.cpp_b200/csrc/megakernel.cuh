@@ -38,8 +38,9 @@
 #include "kernels.cuh"
 
 #define MK_THREADS 512
-#define MK_MAX_POS 640            // positions whose K/V fit the attention stage
-#define MK_SPIN (1u << 21)        // polls per wait before giving up (~1 s)
+#define MK_MAX_POS 640            // positions whose K/V fit the attention stage at once
+#define MK_TP 320                 // longer contexts: positions per streamed K/V tile (K rows then V rows)
+#define MK_SPIN (1u << 21)        // default polls per wait before giving up (~1 s); MegaArgs.spin
 #define MK_MAXI 3                 // weight items (32-element blocks) per thread per phase
 
 // activation buffers (floats) and arrival counters (one 128-byte line each)
@@ -85,6 +86,8 @@ struct MegaArgs {
     int tl_step;
     int first_tok;                 // token of the first step (< 0: the stream's step_tok)
     unsigned epoch;                // launch number (1..4095): high bits of the x-word tags
+    unsigned spin;                 // polls before a wait for another CTA or a staging copy gives up
+    float * htrace;                // nullable: [n_layer + 1][1024] residual stream of step 0 (embedding, each layer's output)
     SampArgs samp;
 };
 #define MK_TL 512
@@ -134,8 +137,8 @@ __device__ __forceinline__ bool mk_acquire(const unsigned * c, unsigned target, 
         unsigned spins = 0;
         while (ld_acquire_u32(c) < target) {
             __nanosleep(20);
-            if (++spins > MK_SPIN || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag)) {
-                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+            if (++spins > a.spin || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag)) {
+                if (spins > a.spin) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                 ok = 0;
                 break;
             }
@@ -191,8 +194,8 @@ __device__ __forceinline__ bool mk_wait_x(const unsigned long long * src, unsign
             for (int q = 0; q < 32; ++q) all = all && (unsigned) (w[q] >> 32) == tag;
             if (__all_sync(0xffffffffu, all)) break;
             int stop = 0;
-            if (lane == 0 && (spins > MK_SPIN || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag))) {
-                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+            if (lane == 0 && (spins > a.spin || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag))) {
+                if (spins > a.spin) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                 stop = 1;
             }
             if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
@@ -249,8 +252,8 @@ __device__ __forceinline__ bool mk_wait_h(const unsigned long long * src, unsign
             for (int q = 0; q < MK_HT_WORDS / 64; ++q) all = all && (unsigned) (w[q] >> 32) == tag;
             if (__all_sync(0xffffffffu, all)) break;
             int stop = 0;
-            if (lane == 0 && (spins > MK_SPIN || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag))) {
-                if (spins > MK_SPIN) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+            if (lane == 0 && (spins > a.spin || ((spins & 255u) == 0 && *(volatile int *) a.abort_flag))) {
+                if (spins > a.spin) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                 stop = 1;
             }
             if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
@@ -563,15 +566,15 @@ __device__ __forceinline__ void mk_bulk_g2s(void * dst, const void * src, unsign
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(mk_saddr(dst)), "l"(src), "r"(bytes), "r"(mk_saddr(mb)) : "memory");
 }
-// wait for phase `parity` of mb; false after MK_SPIN polls
-__device__ __forceinline__ bool mk_mbar_wait(unsigned long long * mb, unsigned parity) {
+// wait for phase `parity` of mb; false after `limit` polls
+__device__ __forceinline__ bool mk_mbar_wait(unsigned long long * mb, unsigned parity, unsigned limit = MK_SPIN) {
     const unsigned ad = mk_saddr(mb);
     for (unsigned spins = 0;; ++spins) {
         unsigned done;
         asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                      : "=r"(done) : "r"(ad), "r"(parity) : "memory");
         if (done) return true;
-        if (spins >= MK_SPIN) return false;
+        if (spins >= limit) return false;
         __nanosleep(20);
     }
 }
@@ -710,7 +713,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const
     if (hw) {
         __shared__ int okhd;
         if (tid == 0) {
-            const bool ok = mk_mbar_wait(hmb, hpar);
+            const bool ok = mk_mbar_wait(hmb, hpar, a.spin);
             if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
             okhd = ok;
         }
@@ -765,11 +768,12 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
 // every exit first waits (bounded) for this CTA's copies still in flight
 #define MK_BAIL do {                                                                  \
         asm volatile("cp.async.wait_all;" ::: "memory");                              \
-        if (OWN && att && tid == 0) {                                                 \
+        if (tid == 0) {                                                               \
             if (kw_out >= 0) mk_mbar_wait(&mbar[0], (unsigned) kw_out & 1u);          \
             if (v_out >= 0) mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u);            \
+            if (hd_out >= 0) mk_mbar_wait(&mbar[2], (unsigned) hd_out & 1u);          \
+            if (a_out >= 0) mk_mbar_wait(&mbar[3], (unsigned) a_out & 1u);            \
         }                                                                             \
-        if (OWN && tid == 0 && hd_out >= 0) mk_mbar_wait(&mbar[2], (unsigned) hd_out & 1u); \
         return;                                                                       \
     } while (0)
 
@@ -836,13 +840,16 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // q/k/v rows are computed (vph counts its phases).  kw_out / v_out: phase
     // of a copy issued and not yet waited for.
     // mbar[2] (every CTA, Q4_0 head): this CTA's head rows, one phase per step.
-    __shared__ __align__(8) unsigned long long mbar[3];
+    // Contexts longer than MK_MAX_POS (any layout): K/V tiles stream through
+    // buffer A (kst; mbar[3], aph phases) and buffer B (vst; mbar[1]).
+    __shared__ __align__(8) unsigned long long mbar[4];
     __shared__ int okf;
-    int kw_out = -1, v_out = -1, vph = 0, hd_out = -1;
-    if (OWN && tid == 0) {
+    int kw_out = -1, v_out = -1, vph = 0, hd_out = -1, a_out = -1, aph = 0;
+    if (tid == 0) {
         mk_mbar_init(&mbar[0]);
         mk_mbar_init(&mbar[1]);
         mk_mbar_init(&mbar[2]);
+        mk_mbar_init(&mbar[3]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -864,20 +871,56 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // and of that layer's q/k/v weights for this head, issued by the last
     // warp's first thread (not the hand-off poller)
     auto packed = [](int p) { return 2 * (p + 1) <= MK_MAX_POS; };
+    auto tiled = [](int p) { return p + 1 > MK_MAX_POS; };
     auto issue_kw = [&](int u, int nl, int npos) {
         if (tid == MK_THREADS - 32) {
+            const bool tl = tiled(npos);
             const bool pk = packed(npos);
-            const unsigned rb = (unsigned) npos * T3B_HD * 2;
+            const int nk = tl ? MK_TP : npos;
+            const unsigned rb = (unsigned) nk * T3B_HD * 2;
             const __half * kb = a.kv + (size_t) nl * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
             mk_fence_proxy_async();   // K/V rows this CTA stored (generic proxy) are read by the bulk copy
-            mk_mbar_expect(&mbar[0], (pk ? 2u : 1u) * rb + MK_QKVW_BYTES);
-            if (npos > 0) {
+            mk_mbar_expect(&mbar[0], (pk || tl ? 2u : 1u) * rb + MK_QKVW_BYTES);
+            if (nk > 0) {
                 mk_bulk_g2s(kst, kb, rb, &mbar[0]);
-                if (pk) mk_bulk_g2s(kst + (size_t) (npos + 1) * T3B_HD, kb + a.v_off, rb, &mbar[0]);
+                if (tl) mk_bulk_g2s(kst + (size_t) MK_TP * T3B_HD, kb + a.v_off, rb, &mbar[0]);
+                else if (pk) mk_bulk_g2s(kst + (size_t) (npos + 1) * T3B_HD, kb + a.v_off, rb, &mbar[0]);
             }
             mk_bulk_qkvw(qkvw, a.layers[nl].qkv, hh_, &mbar[0]);
         }
         kw_out = u;
+    };
+    // long contexts: tile i of positions [0, npos) (K rows, then V rows at
+    // row MK_TP) into buffer A (kst, mbar[3]) or B (vst, mbar[1]); the
+    // current position is never copied (its K/V come from the q/k/v outputs)
+    auto issue_tile = [&](int i, int npos, const __half * kb_, bool inB) {
+        if (tid == MK_THREADS - 32) {
+            const int t0 = i * MK_TP;
+            const int n = max(0, min(MK_TP, npos - t0));
+            const unsigned rb = (unsigned) n * T3B_HD * 2;
+            __half * dst = inB ? vst : kst;
+            unsigned long long * mb = inB ? &mbar[1] : &mbar[3];
+            mk_fence_proxy_async();
+            mk_mbar_expect(mb, 2u * rb);
+            if (n > 0) {
+                mk_bulk_g2s(dst, kb_ + (size_t) t0 * T3B_HD, rb, mb);
+                mk_bulk_g2s(dst + (size_t) MK_TP * T3B_HD, kb_ + a.v_off + (size_t) t0 * T3B_HD, rb, mb);
+            }
+        }
+        if (inB) v_out = vph++;
+        else a_out = aph++;
+    };
+    // wait (one thread, bounded) for the outstanding phase `ph` of mb
+    auto wait_copy = [&](unsigned long long * mb, int & ph) -> bool {
+        if (tid == 0) {
+            const bool ok = mk_mbar_wait(mb, (unsigned) ph & 1u, a.spin);
+            if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+            okf = ok;
+        }
+        __syncthreads();
+        if (!okf) return false;
+        ph = -1;
+        return true;
     };
     unsigned * cQKV = a.cnt + MK_C_QKV * MK_C_STRIDE, * cATT = a.cnt + MK_C_ATT * MK_C_STRIDE;
     unsigned * cXM = a.cnt + MK_C_XM * MK_C_STRIDE, * cH = a.cnt + MK_C_H * MK_C_STRIDE;
@@ -910,8 +953,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         if (cta == 0 && tid == 0 && a.cancel) cancelled = *(volatile const int *) a.cancel;
         const int pos = a.p0 + step;
         // embedding: x = speech_emb[tok] + wpe[pos]
-        for (int i = tid; i < D; i += MK_THREADS)
+        for (int i = tid; i < D; i += MK_THREADS) {
             xres[i] = __fadd_rn(__half2float(a.semb[(size_t) tok * D + i]), a.wpe[(size_t) pos * D + i]);
+            if (a.htrace && step == 0 && cta == 0) a.htrace[i] = xres[i];
+        }
         __syncthreads();
         for (int l = 0; l < NL; ++l) {
             const MkLayer & Ly = a.layers[l];
@@ -961,7 +1006,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, false);
                     MK_STAMP(l * 20 + 12);
                     if (tid == 0) {   // K rows and q/k/v weights of this use
-                        const bool ok = mk_mbar_wait(&mbar[0], (unsigned) (k - 1u) & 1u);
+                        const bool ok = mk_mbar_wait(&mbar[0], (unsigned) (k - 1u) & 1u, a.spin);
                         if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                         okf = ok;
                     }
@@ -974,7 +1019,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     MK_STAMP(l * 20 + 15);
                     const bool pk = packed(pos);
                     __half * vrow = pk ? kst + (size_t) (pos + 1) * T3B_HD : vst;
-                    if (!pk) {
+                    if (tiled(pos)) {
+                        // tile 0 came with the weights; tile 1 replaces them
+                        if (pos >= MK_TP) issue_tile(1, pos, kb, true);
+                    } else if (!pk) {
                         // V rows [0, pos) replace the weights (every read of
                         // them finished before the barrier above).  Issued by
                         // the last warp, which has no part in the K/V append.
@@ -992,7 +1040,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             const int vv = tid >= 2 * T3B_HD, c = tid & 63;
                             const __half hv = __float2half_rn(v);
                             (vv ? (__half *) (kb + a.v_off) : (__half *) kb)[(size_t) pos * T3B_HD + c] = hv;
-                            (vv ? vrow : kst)[(size_t) pos * T3B_HD + c] = hv;
+                            if (!tiled(pos)) (vv ? vrow : kst)[(size_t) pos * T3B_HD + c] = hv;
                         }
                     }
                     __syncthreads();
@@ -1040,7 +1088,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 const int h = hh_;
                 const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) h * a.max_ctx * T3B_HD;
                 const __half * vb = kb + a.v_off;
-                if (!OWN) {
+                if (!OWN && tiled(pos)) {
+                    issue_tile(0, pos, kb, false);
+                    if (pos >= MK_TP) issue_tile(1, pos, kb, true);
+                } else if (!OWN) {
                     // stage K/V of positions [0, pos) while q/k/v are computed
                     mk_stage_kv(kst, kb, pos);
                     mk_stage_kv(vst, vb, pos);
@@ -1056,7 +1107,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     __syncthreads();
                     if (!ok) MK_BAIL;
                     MK_STAMP(l * 20 + 3);
-                    if (tid < T3B_HD) {
+                    if (tid < T3B_HD && !tiled(pos)) {
                         kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
                         vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
                     }
@@ -1065,81 +1116,156 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 }
                 const int L = pos + 1;
                 const int lane = tid & 31, w = tid >> 5;
-                // scores: thread t owns keys t and t + 512; each thread walks the
-                // 8 16-byte chunks of its K row in a rotated order so the warp's
-                // shared-memory reads spread over all banks
-                float sc[2];
-                float lm = -INFINITY;
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int j = tid + u * MK_THREADS;
-                    sc[u] = -INFINITY;
-                    if (j < L) {
-                        const uint4 * kp = (const uint4 *) (kst + (size_t) j * T3B_HD);
-                        float dot = 0.0f;
-#pragma unroll
-                        for (int cc = 0; cc < 8; ++cc) {
-                            const int c = (cc + tid) & 7;
-                            const uint4 uu = kp[c];
-                            const float4 qa = *(const float4 *) (qkvh + c * 8), qb = *(const float4 *) (qkvh + c * 8 + 4);
-                            const __half2 * hp = (const __half2 *) &uu;
-                            const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
-                            const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
-                            dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
-                            dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
-                            dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
-                            dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
-                        }
-                        sc[u] = dot * 0.125f;
-                        lm = fmaxf(lm, sc[u]);
-                    }
-                }
                 float * rf = (float *) redd;   // 64 floats: [0,16) max, [32,48) sum
-                lm = warp_max(lm);
-                if (lane == 0) rf[w] = lm;
-                __syncthreads();
-                const float mx = warp_max(rf[lane & 15]);
-                float * pw = att_s + 256;      // [L] weights
-                float ls = 0.0f;
+                float * pw = att_s + 256;      // [L] (or one tile's) softmax weights
+                float lsum;
+                float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
+                if (!tiled(pos)) {
+                    // scores: thread t owns keys t and t + 512; each thread walks the
+                    // 8 16-byte chunks of its K row in a rotated order so the warp's
+                    // shared-memory reads spread over all banks
+                    float sc[2];
+                    float lm = -INFINITY;
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int j = tid + u * MK_THREADS;
-                    if (j < L) { const float p = expf(sc[u] - mx); pw[j] = p; ls += p; }
+                    for (int u = 0; u < 2; ++u) {
+                        const int j = tid + u * MK_THREADS;
+                        sc[u] = -INFINITY;
+                        if (j < L) {
+                            const uint4 * kp = (const uint4 *) (kst + (size_t) j * T3B_HD);
+                            float dot = 0.0f;
+#pragma unroll
+                            for (int cc = 0; cc < 8; ++cc) {
+                                const int c = (cc + tid) & 7;
+                                const uint4 uu = kp[c];
+                                const float4 qa = *(const float4 *) (qkvh + c * 8), qb = *(const float4 *) (qkvh + c * 8 + 4);
+                                const __half2 * hp = (const __half2 *) &uu;
+                                const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
+                                const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
+                                dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
+                                dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
+                                dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
+                                dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
+                            }
+                            sc[u] = dot * 0.125f;
+                            lm = fmaxf(lm, sc[u]);
+                        }
+                    }
+                    lm = warp_max(lm);
+                    if (lane == 0) rf[w] = lm;
+                    __syncthreads();
+                    const float mx = warp_max(rf[lane & 15]);
+                    float ls = 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int j = tid + u * MK_THREADS;
+                        if (j < L) { const float p = expf(sc[u] - mx); pw[j] = p; ls += p; }
+                    }
+                    ls = warp_sum(ls);
+                    if (lane == 0) rf[32 + w] = ls;
+                    const bool vwait = OWN && v_out >= 0;   // V rows loaded separately (not packed)
+                    if (vwait && tid == 0) {   // this layer's V rows
+                        const bool ok = mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u, a.spin);
+                        if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                        okf = ok;
+                        MK_STAMP(l * 20 + 3);
+                    }
+                    __syncthreads();
+                    if (vwait) {
+                        if (!okf) MK_BAIL;
+                        v_out = -1;
+                    }
+                    const __half * vsrc = (OWN && packed(pos)) ? kst + (size_t) (pos + 1) * T3B_HD : vst;
+                    lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
+                    MK_STAMP(l * 20 + 9);
+                    // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
+                    // dims 2l, 2l+1; two accumulators hide the load latency
+                    {
+                        int j = w;
+                        for (; j + 16 < L; j += 32) {
+                            const float2 v0 = __half22float2(*(const __half2 *) (vsrc + (size_t) j * T3B_HD + 2 * lane));
+                            const float2 v1 = __half22float2(*(const __half2 *) (vsrc + (size_t) (j + 16) * T3B_HD + 2 * lane));
+                            const float p0 = pw[j], p1 = pw[j + 16];
+                            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+                            o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
+                        }
+                        if (j < L) {
+                            const float2 v0 = __half22float2(*(const __half2 *) (vsrc + (size_t) j * T3B_HD + 2 * lane));
+                            const float p0 = pw[j];
+                            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+                        }
+                    }
+                } else {
+                    // L > MK_MAX_POS: tiles of MK_TP positions through buffers A
+                    // and B, online softmax (running max m, per-thread sums
+                    // and per-warp outputs rescaled when the max grows)
+                    const int nt = (L + MK_TP - 1) / MK_TP;
+                    float m_run = -INFINITY, l_t = 0.0f;
+                    for (int i = 0; i < nt; ++i) {
+                        const bool inB = (i & 1) != 0;
+                        __half * tb = inB ? vst : kst;
+                        if (!(OWN && i == 0)) {   // OWN: tile 0 arrived with the weights
+                            if (!wait_copy(inB ? &mbar[1] : &mbar[3], inB ? v_out : a_out)) MK_BAIL;
+                        }
+                        const int t0 = i * MK_TP, n = min(MK_TP, L - t0);
+                        if (i == nt - 1 && tid < 2 * T3B_HD) {   // the current position, f16 as in the cache
+                            const int c = tid & 63, vv = tid >> 6;
+                            tb[(size_t) (vv * MK_TP + pos - t0) * T3B_HD + c] = __float2half_rn(qkvh[64 + tid]);
+                        }
+                        __syncthreads();
+                        float sc = -INFINITY;
+                        if (tid < n) {
+                            const uint4 * kp = (const uint4 *) (tb + (size_t) tid * T3B_HD);
+                            float dot = 0.0f;
+#pragma unroll
+                            for (int cc = 0; cc < 8; ++cc) {
+                                const int c = (cc + tid) & 7;
+                                const uint4 uu = kp[c];
+                                const float4 qa = *(const float4 *) (qkvh + c * 8), qb = *(const float4 *) (qkvh + c * 8 + 4);
+                                const __half2 * hp = (const __half2 *) &uu;
+                                const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
+                                const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
+                                dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
+                                dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
+                                dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
+                                dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
+                            }
+                            sc = dot * 0.125f;
+                        }
+                        const float lm = warp_max(sc);
+                        if (lane == 0) rf[w] = lm;
+                        __syncthreads();
+                        const float m_new = fmaxf(m_run, warp_max(rf[lane & 15]));
+                        const float resc = expf(m_run - m_new);   // 0 for the first tile
+                        m_run = m_new;
+                        const float p = tid < n ? expf(sc - m_new) : 0.0f;
+                        if (tid < n) pw[tid] = p;
+                        l_t = __fmaf_rn(l_t, resc, p);
+                        __syncthreads();
+                        const __half * vt = tb + (size_t) MK_TP * T3B_HD;
+                        o0.x *= resc; o0.y *= resc; o1.x *= resc; o1.y *= resc;
+                        int j = w;
+                        for (; j + 16 < n; j += 32) {
+                            const float2 v0 = __half22float2(*(const __half2 *) (vt + (size_t) j * T3B_HD + 2 * lane));
+                            const float2 v1 = __half22float2(*(const __half2 *) (vt + (size_t) (j + 16) * T3B_HD + 2 * lane));
+                            const float p0 = pw[j], p1 = pw[j + 16];
+                            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+                            o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
+                        }
+                        if (j < n) {
+                            const float2 v0 = __half22float2(*(const __half2 *) (vt + (size_t) j * T3B_HD + 2 * lane));
+                            const float p0 = pw[j];
+                            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+                        }
+                        __syncthreads();   // tile buffer, pw and rf free again
+                        if (i + 2 < nt) issue_tile(i + 2, pos, kb, inB);
+                    }
+                    const float ls = warp_sum(l_t);
+                    if (lane == 0) rf[32 + w] = ls;
+                    __syncthreads();
+                    lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
+                    MK_STAMP(l * 20 + 9);
                 }
-                ls = warp_sum(ls);
-                if (lane == 0) rf[32 + w] = ls;
-                const bool vwait = OWN && v_out >= 0;   // V rows loaded separately (not packed)
-                if (vwait && tid == 0) {   // this layer's V rows
-                    const bool ok = mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u);
-                    if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
-                    okf = ok;
-                    MK_STAMP(l * 20 + 3);
-                }
-                __syncthreads();
-                if (vwait) {
-                    if (!okf) MK_BAIL;
-                    v_out = -1;
-                }
-                const __half * vsrc = (OWN && packed(pos)) ? kst + (size_t) (pos + 1) * T3B_HD : vst;
-                const float lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
-                MK_STAMP(l * 20 + 9);
-                // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
-                // dims 2l, 2l+1; two accumulators hide the load latency
                 {
-                    float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
-                    int j = w;
-                    for (; j + 16 < L; j += 32) {
-                        const float2 v0 = __half22float2(*(const __half2 *) (vsrc + (size_t) j * T3B_HD + 2 * lane));
-                        const float2 v1 = __half22float2(*(const __half2 *) (vsrc + (size_t) (j + 16) * T3B_HD + 2 * lane));
-                        const float p0 = pw[j], p1 = pw[j + 16];
-                        o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
-                        o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
-                    }
-                    if (j < L) {
-                        const float2 v0 = __half22float2(*(const __half2 *) (vsrc + (size_t) j * T3B_HD + 2 * lane));
-                        const float p0 = pw[j];
-                        o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
-                    }
                     float * og = att_s + 256 + MK_MAX_POS;   // [16][64]
                     og[w * 64 + 2 * lane] = o0.x + o1.x;
                     og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
@@ -1369,6 +1495,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     const float xo = __fadd_rn(__fadd_rn(rowsum[tid], bias), xmid[n]);
                     if (LLX) mk_st_x(bXT + n, mk_xtag(a.epoch, k), xo);
                     else bX[n] = xo;
+                    if (a.htrace && step == 0) a.htrace[(size_t) (l + 1) * D + n] = xo;
                 }
                 if (LLX) __syncthreads();
                 else mk_release(cX);

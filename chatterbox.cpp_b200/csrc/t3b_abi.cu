@@ -136,6 +136,7 @@ struct Layer {
 struct StepGraph {
     cudaGraph_t g = nullptr;
     cudaGraphExec_t ge = nullptr;
+    int n_kernels = 0;   // kernel nodes per launch (launch accounting)
 };
 
 }  // namespace
@@ -158,6 +159,11 @@ struct t3b_ctx {
     unsigned * err_pin = nullptr;   // pinned host copy of err_word (read in the same synchronize as results)
     volatile int cancel = 0;
     float last_ms = 0.0f;
+    unsigned wait_limit = 0;            // persistent-kernel wait limit in polls (0: MK_SPIN)
+    unsigned long long launches = 0;    // kernels launched by t3b_step / t3b_sample / t3b_decode
+    float * htrace = nullptr;           // nullable: [n_layer + 1][n_embd] residual stream of the last traced step
+    cudaEvent_t hand_ev = nullptr;      // t3b_s3gen_tokens: consumer streams wait on it
+    cudaEvent_t q_ev[2] = {nullptr, nullptr};   // graph decode loop: bounds the steps queued ahead
 
     // streams
     int S = 0, rps = 1, max_ctx = 0, hist_cap = 0, s_max = 1;
@@ -296,8 +302,9 @@ GemvEpi epi_plain(int kind, float * y, int ldy, const float * bias, const float 
 // rows of the M), written to logits_out rows y_row[...] (device array) or
 // consecutively when y_row is null.
 void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int head_first, int head_rows,
-                float * logits_out, const int * y_row, cudaStream_t st) {
+                float * logits_out, const int * y_row, cudaStream_t st, float * htrace = nullptr) {
     const int D = ctx->hp.n_embd, H = ctx->hp.n_head;
+    if (htrace) cudaMemcpyAsync(htrace, ctx->x, sizeof(float) * D, cudaMemcpyDeviceToDevice, st);
     for (int il = 0; il < ctx->hp.n_layer; ++il) {
         const Layer & Ly = ctx->L[il];
         // LN1 + QKV + K/V append
@@ -334,6 +341,8 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         if (!q_fc) launch_prep(ctx, ctx->h, 4 * D, M, 4 * D, nullptr, nullptr, Ly.fc2.type, st);
         launch_gemv(Ly.fc2, q_fc ? ctx->xq2 : ctx->xq, q_fc ? ctx->xd2 : ctx->xd, q_fc ? ctx->xs2 : ctx->xs, ctx->xh, M,
                     epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D), st);
+        if (htrace)
+            cudaMemcpyAsync(htrace + (size_t) (il + 1) * D, ctx->x, sizeof(float) * D, cudaMemcpyDeviceToDevice, st);
     }
     if (head_rows > 0) {
         launch_prep(ctx, ctx->x + (size_t) head_first * D, D, head_rows, D, ctx->lnf_g, ctx->lnf_b, ctx->head.type, st);
@@ -480,6 +489,9 @@ void t3b_destroy(t3b_ctx * ctx) {
     cudaStreamSynchronize(ctx->st);
     free_streams(ctx);
     if (ctx->trace) cudaFree(ctx->trace);
+    if (ctx->htrace) cudaFree(ctx->htrace);
+    if (ctx->hand_ev) cudaEventDestroy(ctx->hand_ev);
+    for (cudaEvent_t e : ctx->q_ev) if (e) cudaEventDestroy(e);
     for (void * p : ctx->allocs) cudaFree(p);
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
@@ -506,6 +518,39 @@ int t3b_trace_logits(t3b_ctx * ctx, int max_steps) {
     }
     return T3B_OK;
 }
+
+int t3b_trace_hidden(t3b_ctx * ctx, int on) {
+    if (!ctx) return T3B_ERR_ARG;
+    CK(cudaSetDevice(ctx->device));
+    CK(cudaStreamSynchronize(ctx->st));
+    if (ctx->htrace && !on) { CK(cudaFree(ctx->htrace)); ctx->htrace = nullptr; }
+    if (!ctx->htrace && on) {
+        const size_t n = (size_t) (ctx->hp.n_layer + 1) * ctx->hp.n_embd;
+        CK(cudaMalloc(&ctx->htrace, sizeof(float) * n));
+        CK(cudaMemset(ctx->htrace, 0, sizeof(float) * n));
+    }
+    return T3B_OK;
+}
+
+int t3b_get_hidden_trace(t3b_ctx * ctx, float * out) {
+    if (!ctx || !out || !ctx->htrace) {
+        if (ctx) set_err(&ctx->err, "t3b_get_hidden_trace: tracing is off");
+        return T3B_ERR_ARG;
+    }
+    CK(cudaSetDevice(ctx->device));
+    CK(cudaStreamSynchronize(ctx->st));
+    CK(cudaMemcpy(out, ctx->htrace, sizeof(float) * (size_t) (ctx->hp.n_layer + 1) * ctx->hp.n_embd,
+                  cudaMemcpyDeviceToHost));
+    return T3B_OK;
+}
+
+int t3b_set_wait_limit(t3b_ctx * ctx, unsigned polls) {
+    if (!ctx) return T3B_ERR_ARG;
+    ctx->wait_limit = polls;
+    return T3B_OK;
+}
+
+unsigned long long t3b_launch_count(const t3b_ctx * ctx) { return ctx ? ctx->launches : 0ull; }
 
 int t3b_get_logits_trace(t3b_ctx * ctx, float * out, int n) {
     if (!ctx || !out || n < 0 || n > ctx->trace_cap + 1 || !ctx->trace) {
@@ -719,7 +764,7 @@ SampArgs sampler_args(t3b_ctx * ctx, bool with_done) {
 }
 
 int ensure_graph(t3b_ctx * ctx, int n, bool sample, StepGraph ** out) {
-    std::vector<int> key{n, sample ? 1 : 0};
+    std::vector<int> key{n, sample ? 1 : 0, ctx->htrace ? 1 : 0};
     auto it = ctx->graphs.find(key);
     if (it != ctx->graphs.end()) { *out = &it->second; return T3B_OK; }
     const int M = n * ctx->rps;
@@ -729,7 +774,7 @@ int ensure_graph(t3b_ctx * ctx, int n, bool sample, StepGraph ** out) {
     CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     embed_step_kernel<<<M, 256, 0, st>>>(ctx->semb, ctx->wpe, ctx->step_tok, ctx->row_slot, ctx->pos,
                                          ctx->hp.n_embd, V, ctx->hp.n_ctx, ctx->x, ctx->err_word);
-    run_layers(ctx, M, ctx->row_of, ctx->pos, 0, M, ctx->logits, ctx->row_of, st);
+    run_layers(ctx, M, ctx->row_of, ctx->pos, 0, M, ctx->logits, ctx->row_of, st, ctx->htrace);
     if (sample) {
         SampArgs a = sampler_args(ctx, true);
         sampler_kernel<<<n, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, st>>>(a);
@@ -738,6 +783,15 @@ int ensure_graph(t3b_ctx * ctx, int n, bool sample, StepGraph ** out) {
     cudaError_t ce = cudaStreamEndCapture(st, &sg.g);
     if (ce != cudaSuccess) { set_err(&ctx->err, "graph capture: %s", cudaGetErrorString(ce)); return T3B_ERR_CUDA; }
     CK(cudaGraphInstantiate(&sg.ge, sg.g, 0));
+    size_t nn = 0;
+    CK(cudaGraphGetNodes(sg.g, nullptr, &nn));
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (nn) CK(cudaGraphGetNodes(sg.g, nodes.data(), &nn));
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType ty;
+        CK(cudaGraphNodeGetType(nd, &ty));
+        sg.n_kernels += ty == cudaGraphNodeTypeKernel;
+    }
     auto res = ctx->graphs.emplace(key, sg);
     *out = &res.first->second;
     return T3B_OK;
@@ -745,15 +799,16 @@ int ensure_graph(t3b_ctx * ctx, int n, bool sample, StepGraph ** out) {
 
 
 // Persistent batch-1 decode (megakernel.cuh).  Eligible when one stream
-// without CFG decodes a T3 with n_embd 1024 / 16 heads, every layer matrix in
-// one of Q4_0 / Q8_0 / F16, and the positions fit the attention stage.  The
-// CTA count is the SM count; each CTA's row slices must fit its registers.
+// without CFG decodes a T3 with n_embd 1024 / 16 heads and every layer matrix
+// in one of Q4_0 / Q8_0 / F16, at any position of the cache (contexts longer
+// than MK_MAX_POS stream their K/V in tiles).  The CTA count is the SM count;
+// each CTA's row slices must fit its registers.
 bool mega_eligible(t3b_ctx * ctx, int n, int max_pos_after) {
     if (getenv("T3B_NO_MEGAKERNEL")) return false;
     if (n != 1 || ctx->rps != 1) return false;
     if (ctx->hp.n_embd != 1024 || ctx->hp.n_head != 16) return false;
     if (ctx->hp.n_speech_vocab > T3B_SAMPLER_VMAX) return false;
-    if (max_pos_after > MK_MAX_POS) return false;
+    if (max_pos_after > ctx->max_ctx) return false;   // longer than MK_MAX_POS: K/V streamed in tiles
     const int T = ctx->L[0].attn.type;
     for (const Layer & Ly : ctx->L)
         if (Ly.attn.type != T || Ly.proj.type != T || Ly.fc.type != T || Ly.fc2.type != T) return false;
@@ -841,6 +896,8 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     a.samp = sampler_args(ctx, false);
     a.samp.done = nullptr;
     a.first_tok = first_tok;
+    a.spin = ctx->wait_limit ? ctx->wait_limit : MK_SPIN;
+    a.htrace = ctx->htrace;
     m.epoch = m.epoch % 4095u + 1u;   // 1..4095, never the same as the previous launch's
     a.epoch = m.epoch;
     CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_CTL_WORDS, st));
@@ -860,6 +917,7 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
                     : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0>
                                     : (const void *) t3_decode_megakernel<T3B_F16>;
     CK(cudaLaunchCooperativeKernel(fn, dim3(m.grid), dim3(MK_THREADS), args, m.smem, st));
+    ctx->launches += 1;
     if (steps) CK(cudaMemcpyAsync(steps, m.steps_done, sizeof(int), cudaMemcpyDeviceToHost, st));
     if (tl) {
         std::vector<unsigned long long> h((size_t) m.grid * MK_TL);
@@ -938,6 +996,7 @@ int t3b_step(t3b_ctx * ctx, int n, const int32_t * streams, const int32_t * toke
     CK(cudaMemcpyAsync(ctx->pos, pos.data(), sizeof(int) * pos.size(), cudaMemcpyHostToDevice, st));
     CK(cudaEventRecord(ctx->ev0, st));
     CK(cudaGraphLaunch(g->ge, st));
+    ctx->launches += (unsigned long long) g->n_kernels;
     CK(cudaEventRecord(ctx->ev1, st));
     if (logits_out)
         for (int i = 0; i < n; ++i)
@@ -970,6 +1029,7 @@ int t3b_sample(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     CK(cudaEventRecord(ctx->ev0, st));
     sampler_kernel<<<n, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, st>>>(a);
     CK(cudaGetLastError());
+    ctx->launches += 1;
     CK(cudaEventRecord(ctx->ev1, st));
     CK(cudaMemcpyAsync(tokens_out, ctx->tok_out, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
@@ -1020,6 +1080,7 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     CK(cudaEventRecord(ctx->ev0, st));
     sampler_kernel<<<n, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, st>>>(a);
     CK(cudaGetLastError());
+    ctx->launches += 1;
     int steps_done = 0;
     if (mega) {
         // a stop token drawn from the prefill logits ends the loop at once
@@ -1055,6 +1116,14 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
         return T3B_OK;
     }
     for (int s = 0; s < max_steps; ++s) {
+        // at most 16 steps queued ahead of the GPU, so that a cancel (or
+        // the done flags) is seen within that many steps
+        if (s > 0 && (s % 8) == 0) {
+            cudaEvent_t & q = ctx->q_ev[(s / 8) & 1];
+            if (!q) CK(cudaEventCreateWithFlags(&q, cudaEventDisableTiming));
+            else if (s >= 16) CK(cudaEventSynchronize(q));
+            CK(cudaEventRecord(q, st));
+        }
         if (ctx->cancel) { set_err(&ctx->err, "t3b_decode: cancelled"); CK(cudaStreamSynchronize(st)); return T3B_ERR_CANCELLED; }
         if (!ignore_stop && s > 0 && (s % 16) == 0) {
             std::vector<int> d(ctx->S);
@@ -1065,6 +1134,7 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
             if (all) break;
         }
         CK(cudaGraphLaunch(g->ge, st));
+        ctx->launches += (unsigned long long) g->n_kernels;
         if (trace)
             CK(cudaMemcpyAsync(ctx->trace + (size_t) (s + 1) * ctx->hp.n_speech_vocab,
                                ctx->logits + (size_t) slots[0] * ctx->rps * ctx->hp.n_speech_vocab, Vb,
@@ -1092,6 +1162,28 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     return T3B_OK;
 }
 
+// S3Gen hand-off: the stream's speech tokens go from its device history
+// straight into the caller's device buffer (the S3Gen input), ordered on the
+// caller's stream by an event; no host round trip.
+int t3b_s3gen_tokens(t3b_ctx * ctx, int stream, int32_t * tokens_dev, int cap, int32_t * n_dev, int append_silence,
+                     void * consumer_stream) {
+    if (!ctx) return T3B_ERR_ARG;
+    if (ctx->S == 0) { set_err(&ctx->err, "t3b_s3gen_tokens: no streams allocated"); return T3B_ERR_STATE; }
+    if (stream < 0 || stream >= ctx->S || !tokens_dev || !n_dev || cap < 0) {
+        set_err(&ctx->err, "t3b_s3gen_tokens: bad args");
+        return T3B_ERR_ARG;
+    }
+    CK(cudaSetDevice(ctx->device));
+    if (!ctx->hand_ev) CK(cudaEventCreateWithFlags(&ctx->hand_ev, cudaEventDisableTiming));
+    s3gen_tokens_kernel<<<1, 1024, 0, ctx->st>>>(ctx->hist + (size_t) stream * ctx->hist_cap, ctx->hist_len + stream,
+                                                T3B_S3_VOCAB, T3B_S3_SILENCE, append_silence ? T3B_S3_LOOKAHEAD : 0,
+                                                tokens_dev, cap, n_dev);
+    CK(cudaGetLastError());
+    CK(cudaEventRecord(ctx->hand_ev, ctx->st));
+    if (consumer_stream) CK(cudaStreamWaitEvent((cudaStream_t) consumer_stream, ctx->hand_ev, 0));
+    return T3B_OK;
+}
+
 // ----------------------------- op-level ----------------------------------
 
 int t3b_op_repack(int dtype, const void * gguf_rows_host, int N, int K, void * out_dev) {
@@ -1107,7 +1199,9 @@ int t3b_op_repack(int dtype, const void * gguf_rows_host, int N, int K, void * o
 namespace {
 // scratch for op-level calls (per device, grown on demand)
 struct OpScratch { int8_t * xq = nullptr; float * xd = nullptr; int * xs = nullptr; __half * xh = nullptr; size_t cap = 0;
-                   float * part = nullptr; unsigned * cnt = nullptr; size_t pcap = 0, ccap = 0; };
+                   float * part = nullptr; unsigned * cnt = nullptr; size_t pcap = 0, ccap = 0;
+                   unsigned * errw = nullptr;   // device error word of the op-level attention on this device
+                 };
 std::mutex g_op_mu;
 std::map<int, OpScratch> g_op;
 }
@@ -1170,12 +1264,16 @@ int t3b_op_attention(const float * q_dev, const void * k_dev, const void * v_dev
         if (sc->ccap < cneed) {
             cudaFree(sc->cnt);
             if (cudaMalloc(&sc->cnt, cneed * 4) != cudaSuccess) { sc->ccap = 0; set_err(nullptr, "t3b_op_attention: scratch allocation failed"); return T3B_ERR_OOM; }
-            cudaMemset(sc->cnt, 0, cneed * 4);
+            // on the caller's stream: the kernel below must see zeros
+            if (cudaMemsetAsync(sc->cnt, 0, cneed * 4, st) != cudaSuccess) { set_err(nullptr, "t3b_op_attention: memset failed"); return T3B_ERR_CUDA; }
             sc->ccap = cneed;
         }
+        if (!sc->errw) {
+            if (cudaMalloc(&sc->errw, 4) != cudaSuccess) { set_err(nullptr, "t3b_op_attention: scratch allocation failed"); return T3B_ERR_OOM; }
+            if (cudaMemsetAsync(sc->errw, 0, 4, st) != cudaSuccess) { set_err(nullptr, "t3b_op_attention: memset failed"); return T3B_ERR_CUDA; }
+        }
     }
-    static unsigned * errw = nullptr;
-    if (!errw) { cudaMalloc(&errw, 4); cudaMemset(errw, 0, 4); }
+    unsigned * errw = sc->errw;
     // caches: [M][n_head][max_ctx][64]; K and V given separately
     AttnArgs a{};
     a.q = q_dev; a.ldq = n_head * T3B_HD;
@@ -1270,7 +1368,7 @@ extern "C" int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev,
         return T3B_ERR_ARG;
     }
     const long long s_max = (max_ctx + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;
-    const long long records = (long long) M * n_head * s_max;
+    const long long records = M >= T3B_ATTN_ROWS_MIN ? 0 : (long long) M * n_head * s_max;   // many rows: no split
     if (records * (T3B_HD + 2) > (long long) T3B_NOALLOC_PART_FLOATS || (long long) M * n_head > T3B_NOALLOC_CNT) {
         set_err(nullptr, "t3b_op_attention_noalloc: %d rows x %d heads x %lld splits exceeds the static scratch "
                 "(%u partial records, %u counters)", M, n_head, s_max,
@@ -1297,10 +1395,12 @@ extern "C" int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev,
         sc = it->second;
     }
     cudaStream_t st = (cudaStream_t) cuda_stream;
-    // the counters must start at zero; the arrays keep the previous call's
-    // contents, so clear the ones this call uses (and the error word)
-    cudaError_t e = cudaMemsetAsync(sc.cnt, 0, sizeof(unsigned) * (size_t) M * n_head, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(sc.cnt + T3B_NOALLOC_CNT, 0, sizeof(unsigned), st);
+    const bool rows = M >= T3B_ATTN_ROWS_MIN;   // same kernel choice as t3b_op_attention
+    cudaError_t e = cudaSuccess;
+    // the split-K counters must start at zero; the array keeps the previous
+    // call's contents, so clear the ones this call uses.  The error word is
+    // left alone: t3b_op_check reads and clears it.
+    if (!rows) e = cudaMemsetAsync(sc.cnt, 0, sizeof(unsigned) * (size_t) M * n_head, st);
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention_noalloc: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
     AttnArgs a{};
     a.q = q_dev; a.ldq = n_head * T3B_HD;
@@ -1309,8 +1409,46 @@ extern "C" int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev,
     a.row_of = nullptr; a.len = len_dev; a.len_add = 0; a.max_ctx = max_ctx; a.n_head = n_head;
     a.out = out_dev; a.ldo = n_head * T3B_HD; a.part = sc.part; a.cnt = sc.cnt; a.s_max = (int) s_max;
     a.err = sc.cnt + T3B_NOALLOC_CNT;
-    attn_decode_kernel<<<dim3(n_head, M, (unsigned) s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
+    if (rows) attn_rows_kernel<<<dim3(n_head, M), 128, 0, st>>>(a);
+    else attn_decode_kernel<<<dim3(n_head, M, (unsigned) s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention_noalloc: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
+    return T3B_OK;
+}
+
+// Reads and clears the device error words of the op-level attention entry
+// points on the current device, after the stream's work so far.
+extern "C" int t3b_op_check(void * cuda_stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { set_err(nullptr, "t3b_op_check: no device"); return T3B_ERR_CUDA; }
+    cudaStream_t st = (cudaStream_t) cuda_stream;
+    unsigned * words[2] = {nullptr, nullptr};
+    {
+        std::lock_guard<std::mutex> lk(g_op_mu);
+        auto it = g_op.find(dev);
+        if (it != g_op.end()) words[0] = it->second.errw;
+    }
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        auto it = g_noalloc.find(dev);
+        if (it != g_noalloc.end()) words[1] = it->second.cnt + T3B_NOALLOC_CNT;
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess) { set_err(nullptr, "t3b_op_check: stream failed"); return T3B_ERR_CUDA; }
+    unsigned w = 0;
+    for (unsigned * p : words) {
+        if (!p) continue;
+        unsigned v = 0;
+        if (cudaMemcpy(&v, p, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemset(p, 0, sizeof v) != cudaSuccess) {
+            set_err(nullptr, "t3b_op_check: error word read failed");
+            return T3B_ERR_CUDA;
+        }
+        w |= v;
+    }
+    if (w) {
+        set_err(nullptr, "op-level device check failed (error word 0x%x:%s%s)", w,
+                (w & T3B_DEVERR_POS) ? " length-out-of-range" : "", (w & T3B_DEVERR_TOKEN) ? " token-out-of-range" : "");
+        return T3B_ERR_DEVICE;
+    }
     return T3B_OK;
 }

@@ -173,6 +173,39 @@ int t3b_get_logits_trace(t3b_ctx * ctx, float * out, int n);
  * callers that order their own work or timing events against it. */
 void * t3b_stream_handle(const t3b_ctx * ctx);
 
+/* Residual-stream trace (parity diagnostics; no counterpart in
+ * chatterbox.cpp, whose graph keeps intermediate tensors internal).  With
+ * on != 0, a t3b_step (and the first step of a persistent-kernel
+ * t3b_decode) records the hidden state of its first row: row 0 = the step
+ * embedding speech_emb[tok] + wpe[pos] (main.cpp:625-627), row l + 1 = the
+ * output of layer l (after the MLP residual, main.cpp:571).
+ * t3b_get_hidden_trace copies [n_layer + 1][n_embd] floats to host memory. */
+int t3b_trace_hidden(t3b_ctx * ctx, int on);
+int t3b_get_hidden_trace(t3b_ctx * ctx, float * out);
+
+/* Polls after which a wait of the persistent decode kernel (for another
+ * CTA's hand-off or for a staging copy) gives up and the call returns
+ * T3B_ERR_TIMEOUT; 0 restores the default (~2M polls, about a second).  A
+ * copy still in flight is always waited for before a CTA exits.  No
+ * counterpart in chatterbox.cpp (its CPU graph has no device waits). */
+int t3b_set_wait_limit(t3b_ctx * ctx, unsigned polls);
+
+/* Kernels this context launched from t3b_step, t3b_sample and t3b_decode
+ * (cumulative; a persistent decode counts one launch). */
+unsigned long long t3b_launch_count(const t3b_ctx * ctx);
+
+/* S3Gen hand-off (replaces the host copy of `generated` that
+ * chatterbox_engine.cpp:395 passes to s3gen_synthesize_to_wav,
+ * src/chatterbox_tts.cpp:1297): writes the stream's speech tokens into the
+ * caller's DEVICE buffer tokens_dev with S3Gen's own preprocessing
+ * (chatterbox_tts.cpp:1389-1398: ids >= 6561, i.e. start/stop, dropped;
+ * append_silence != 0 appends 3 silence tokens 4299), and the count into
+ * the device int *n_dev (-1 when it exceeds cap).  Runs after the context's
+ * queued work; consumer_stream (cudaStream_t, nullable) is made to wait for
+ * it, so a ggml-cuda S3Gen stream can read the buffer without a host sync. */
+int t3b_s3gen_tokens(t3b_ctx * ctx, int stream, int32_t * tokens_dev, int cap, int32_t * n_dev, int append_silence,
+                     void * consumer_stream);
+
 /* ---------------- kernel-level entry points (device pointers) ----------- */
 
 /* Bytes of one repacked weight row: Q4_0 K*9/16, Q8_0 K*17/16, F16 2K. */
@@ -217,15 +250,24 @@ int t3b_op_sample_philox(const float * cond_dev, const float * uncond_dev, int r
  * device.  The split partials and completion counters live in a fixed
  * static device array that every GPU loading libt3b200.so keeps until the
  * process exits (4 MiB of partials + 16 KiB of counters).  Limits: M x n_head
- * x ceil(max_ctx / 128) <= 15887 partial records and M x n_head <= 4096;
- * larger calls return T3B_ERR_ARG without launching.  The first call on a
- * device resolves the array's address (cudaGetSymbolAddress) and should be
- * made before any stream capture.  All calls share the array: each call
- * clears the counters it uses on `cuda_stream` first, and calls whose
- * kernels overlap on the GPU (two streams, or two threads) race on it. */
+ * x ceil(max_ctx / 128) <= 15887 partial records (for M < 8; from 8 rows on
+ * the kernel needs no partials) and M x n_head <= 4096; larger calls return
+ * T3B_ERR_ARG without launching.  The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress) and should be made before any
+ * stream capture.  All calls share the array: each call clears the counters
+ * it uses on `cuda_stream` first, and calls whose kernels overlap on the
+ * GPU (two streams, or two threads) race on it.  Length errors are kept for
+ * t3b_op_check. */
 int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev, const void * v_dev, int M,
                              int n_head, int max_ctx, const int32_t * len_dev, float * out_dev,
                              void * cuda_stream);
+
+/* Synchronises cuda_stream, then reads and clears the device error words of
+ * t3b_op_attention and t3b_op_attention_noalloc on the current device: a row
+ * whose len is <= 0 or > max_ctx is skipped by the kernel (its output left
+ * unwritten) and reported here as T3B_ERR_DEVICE.  Errors stay recorded
+ * until this call. */
+int t3b_op_check(void * cuda_stream);
 
 /* Host expf fix-up table size (entries where the device exp needed a
  * correction to equal the host libm's expf). */

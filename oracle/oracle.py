@@ -14,7 +14,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_sampler.so")
-REF_TREE = os.environ.get("T3B_REFERENCE_TREE", "/root/reference")
+REF_TREE = os.environ.get("T3B_REFERENCE_TREE", "")
 
 _lib = None
 _ref = None
@@ -25,13 +25,13 @@ U32P = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
 
 
 def build(ref=None):
-    """Compile liboracle.so, and the reference sampler when the reference
-    tree is present (ref=None: build it if possible)."""
+    """Compile liboracle.so, and the reference sampler when a reference tree
+    is available: ref = the tree's path, None = $T3B_REFERENCE_TREE when it
+    is set, False = never."""
     subprocess.check_call(["make", "-s", "-C", HERE, "liboracle.so"])
-    if ref is None:
-        ref = os.path.isfile(os.path.join(REF_TREE, "src", "main.cpp"))
-    if ref:
-        subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={REF_TREE}"])
+    tree = ref if isinstance(ref, str) else (REF_TREE if ref is not False else "")
+    if tree and os.path.isfile(os.path.join(tree, "src", "main.cpp")):
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={tree}"])
 
 
 def lib():
@@ -67,6 +67,8 @@ def lib():
         L.orc_prompt.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, F32P]
         L.orc_step.restype = C.c_int
         L.orc_step.argtypes = [C.c_void_p, C.c_int, C.c_int32, F32P]
+        L.orc_step_trace.restype = C.c_int
+        L.orc_step_trace.argtypes = [C.c_void_p, C.c_int, C.c_int32, F32P, F32P]
         L.orc_model_kv.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, F32P]
         _lib = L
     return _lib
@@ -174,6 +176,14 @@ class Model:
         if lib().orc_step(self.h, n_past, token, out) != 0:
             raise ValueError("bad step")
         return out
+
+    def step_trace(self, n_past, token):
+        """step() plus the residual stream: (logits, hidden [n_layer + 1, n_embd])."""
+        out = np.zeros(self.hp["n_speech_vocab"], np.float32)
+        hid = np.zeros((self.hp["n_layer"] + 1, self.hp["n_embd"]), np.float32)
+        if lib().orc_step_trace(self.h, n_past, token, out, hid) != 0:
+            raise ValueError("bad step")
+        return out, hid
 
     def kv(self, layer, which, n_pos):
         out = np.zeros(self.hp["n_head"] * n_pos * (self.hp["n_embd"] // self.hp["n_head"]), np.float32)

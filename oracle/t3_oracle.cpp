@@ -249,6 +249,7 @@ struct Model {
     const float * builtin_spk = nullptr; const int32_t * builtin_cond = nullptr; int n_builtin_cond = 0;
     std::vector<Layer> layers;
     std::vector<float> kc, vc;   // [layer][head][pos][hd]
+    float * trace = nullptr;     // nullable: [n_layer + 1][n_embd] residual stream of the last row (tests)
     size_t kv_index(int l, int h, int pos) const {
         const int hd = n_embd / n_head;
         return (((size_t) l * n_head + h) * max_ctx + pos) * hd;
@@ -312,6 +313,7 @@ void forward(Model & m, std::vector<float> & x, int n_past, int N, float * logit
         for (size_t i = 0; i < (size_t) N * 4 * D; ++i) h4[i] = gelu(h4[i], m.gelu_f16);
         matvec(L.fc2_w.type, L.fc2_w.data, D, 4 * D, h4.data(), N, L.fc2_b, tmp.data(), m.gemv_mode);
         for (size_t i = 0; i < (size_t) N * D; ++i) x[i] = tmp[i] + x[i];
+        if (m.trace) std::memcpy(m.trace + (size_t) (il + 1) * D, &x[(size_t) (N - 1) * D], sizeof(float) * D);
     }
     const int r0 = all_logits ? 0 : N - 1;
     for (int r = r0; r < N; ++r) {
@@ -624,6 +626,20 @@ int orc_step(void * h, int n_past, int32_t token, float * logits_out) {
         x[d] = h2f(m->speech_emb[(size_t) token * D + d]) + m->wpe[(size_t) n_past * D + d];
     forward(*m, x, n_past, 1, logits_out, false);
     return 0;
+}
+
+// orc_step that also records the residual stream: hidden_out[0] = the
+// step embedding, hidden_out[l + 1] = layer l's output ([n_layer + 1][n_embd]).
+int orc_step_trace(void * h, int n_past, int32_t token, float * logits_out, float * hidden_out) {
+    Model * m = (Model *) h;
+    if (n_past + 1 > m->max_ctx || token < 0 || token >= m->n_vocab) return -1;
+    const int D = m->n_embd;
+    for (int d = 0; d < D; ++d)
+        hidden_out[d] = h2f(m->speech_emb[(size_t) token * D + d]) + m->wpe[(size_t) n_past * D + d];
+    m->trace = hidden_out;
+    const int rc = orc_step(h, n_past, token, logits_out);
+    m->trace = nullptr;
+    return rc;
 }
 
 // Copy of one layer's K or V cache rows [n_head][0..n_pos)[hd] for tests.

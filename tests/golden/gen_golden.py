@@ -3,7 +3,7 @@
 Run in a container that holds the chatterbox.cpp tree (the reference
 sampler is compiled from it by `make -C oracle ref`):
 
-    python tests/golden/gen_golden.py
+    T3B_REFERENCE_TREE=<chatterbox.cpp tree> python tests/golden/gen_golden.py
 
 sampler_ref.json   sample_next_token_ex (the reference's own code, compiled
                    from src/main.cpp) on seeded synthetic logits: token and
@@ -93,7 +93,10 @@ def quant():
 
 
 if __name__ == "__main__":
-    oracle.build(ref=True)
+    tree = os.environ.get("T3B_REFERENCE_TREE", "")
+    if not tree:
+        sys.exit("set T3B_REFERENCE_TREE to the chatterbox.cpp source tree")
+    oracle.build(ref=tree)
     data = dict(generator="tests/golden/gen_golden.py", reference="chatterbox.cpp src/main.cpp:726-801 "
                 "sample_next_token_ex compiled by oracle/Makefile (target ref)",
                 cases=sampler_cases(), sequences=sequences())

@@ -227,3 +227,22 @@ def test_sampler_philox_matches_oracle(pkg, orc):
             assert got[r] == t, (trial, r, params[r])
             checked += 1
         assert checked > rows * 0.9
+
+
+def test_attention_length_error_is_reported(pkg):
+    """A row whose length is 0 is skipped by the kernel and reported by
+    t3b_op_check as T3B_ERR_DEVICE; the word is cleared by the read."""
+    L = pkg.lib()
+    M, H, T = 3, 16, 256
+    q = torch.randn(M, H * 64, device="cuda")
+    kv = torch.randn(2, M, H, T, 64, device="cuda").half()
+    out = torch.zeros(M, H * 64, device="cuda")
+    st = _stream()
+    ok = torch.tensor([5, 7, 9], dtype=torch.int32, device="cuda")
+    pkg.check(L.t3b_op_attention(_p(q), _p(kv[0]), _p(kv[1]), M, H, T, _p(ok), _p(out), st))
+    assert L.t3b_op_check(st) == 0
+    bad = torch.tensor([5, 0, 9], dtype=torch.int32, device="cuda")
+    pkg.check(L.t3b_op_attention(_p(q), _p(kv[0]), _p(kv[1]), M, H, T, _p(bad), _p(out), st))
+    assert L.t3b_op_check(st) == -5
+    assert "length-out-of-range" in pkg.last_error()
+    assert L.t3b_op_check(st) == 0

@@ -324,3 +324,173 @@ def test_errors_are_reported(pkg):
         m.decode([pkg.SampleParams.make()], 100)         # would overflow the cache
     # the context stays usable after errors
     m.step([1], n_past=[10])
+
+
+@pytest.mark.parametrize("graph_path", [False, True])
+@pytest.mark.parametrize("quant", ["q4_0", "q8_0", "f16"])
+def test_layer_outputs_match_oracle(pkg, orc, quant, graph_path):
+    """Residual stream after every layer of one t3b_step (persistent kernel,
+    or the CUDA-graph path) against the oracle's teacher-forced step on the
+    same prompt.  The first two layers, before the Q8_0 re-quantisation
+    noise compounds, are held to the logits tolerances of the target (rel
+    1e-2 Q4_0, 2e-3 Q8_0 / F16); the reached error of every layer is
+    printed (PARITY lines)."""
+    hp, t, m = model(pkg, quant, 24, seed=21)
+    m.alloc_streams(1, 256)
+    text = _prompt(2, 40)
+    mir = orc.Model(hp, t, max_ctx=256, gemv_mode=1, gelu_f16=1, kv_f16=1)
+    orc.set_threads(os.cpu_count() or 8)
+    P, _ = mir.prompt(text)
+    if graph_path:
+        os.environ["T3B_NO_MEGAKERNEL"] = "1"
+    try:
+        m.trace_hidden(True)
+        P2, _ = m.prefill(0, text)
+        g = m.step([321])[0, 0]
+        hid = m.hidden_trace()
+    finally:
+        os.environ.pop("T3B_NO_MEGAKERNEL", None)
+        m.trace_hidden(False)
+    assert P2 == P
+    lo, ho = mir.step_trace(P, 321)
+    errs = [rel_err(hid[i], ho[i]) for i in range(hid.shape[0])]
+    path = "graph" if graph_path else "persistent"
+    print(f"PARITY layers {quant} {path}: " + " ".join(f"{e:.2e}" for e in errs) + f" logits {rel_err(g, lo):.2e}")
+    assert errs[0] < 1e-6                                     # embedding: f16 row + f32 position, exact
+    assert max(errs[1], errs[2]) < TOL[quant], errs[:3]
+    assert all(np.isfinite(hid).ravel())
+
+
+def test_wait_timeout_is_reported_and_context_recovers(pkg):
+    """A persistent-kernel wait limited to a few polls runs out (the
+    producers are still busy), the call returns T3B_ERR_TIMEOUT, every CTA
+    leaves after draining its copies, and the next decode on the same
+    context, at the default limit, gives the tokens of an undisturbed run."""
+    hp, t, m = model(pkg, "q4_0", 2)
+    m.alloc_streams(1, 512)
+    text = _prompt(31, 20)
+    params = pkg.SampleParams.make(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2)
+    m.prefill(0, text)
+    m.set_rng(0, pkg.T3B_RNG_MT19937, 5, 0)
+    ref = m.decode([params], 12, ignore_stop=True)[0]
+    m.prefill(0, text)
+    m.set_rng(0, pkg.T3B_RNG_MT19937, 5, 0)
+    m.set_wait_limit(2)
+    try:
+        with pytest.raises(pkg.T3BError) as e:
+            m.decode([params], 12, ignore_stop=True)
+        assert e.value.code == -7, str(e.value)
+    finally:
+        m.set_wait_limit(0)
+    m.prefill(0, text)
+    m.set_rng(0, pkg.T3B_RNG_MT19937, 5, 0)
+    again = m.decode([params], 12, ignore_stop=True)[0]
+    np.testing.assert_array_equal(again, ref)
+
+
+@pytest.mark.parametrize("cfg", [False, True])
+def test_cancel_from_another_thread(pkg, cfg):
+    """Engine::cancel (chatterbox_engine.cpp:342-344, 546-548): t3b_cancel
+    from a second host thread ends a long t3b_decode with T3B_ERR_CANCELLED
+    well before it would have finished; the context stays usable.  Without
+    CFG the decode runs in the persistent kernel (flag read once per step),
+    with CFG in the host-driven graph loop."""
+    import threading
+    import time
+    hp, t, m = model(pkg, "q4_0", 24, seed=21)
+    m.alloc_streams(1, 2048, cfg=cfg)
+    text = _prompt(32, 40)
+    params = pkg.SampleParams.make(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2, cfg_weight=0.5 if cfg else 0.0)
+    P, _ = m.prefill(0, text)
+    steps = 2048 - P - 8
+    t0 = time.perf_counter()
+    m.decode([params], 64, ignore_stop=True)
+    per_step = (time.perf_counter() - t0) / 64
+    m.prefill(0, text)
+    timer = threading.Timer(0.05, m.cancel)
+    timer.start()
+    t0 = time.perf_counter()
+    try:
+        with pytest.raises(pkg.T3BError) as e:
+            m.decode([params], steps, ignore_stop=True)
+    finally:
+        timer.cancel()
+    took = time.perf_counter() - t0
+    assert e.value.code == -6, str(e.value)
+    assert took < 0.5 * steps * per_step, (took, steps * per_step)
+    m.prefill(0, text)
+    assert m.decode([params], 4, ignore_stop=True)[0].size == 5
+
+
+def test_s3gen_handoff_matches_reference_preprocessing(pkg):
+    """t3b_s3gen_tokens writes, on the device, what s3gen_synthesize_to_wav
+    builds from `generated` (src/chatterbox_tts.cpp:1389-1398): tokens below
+    6561 in order (start/stop dropped) plus 3 silence tokens (4299)."""
+    hp, t, m = model(pkg, "q4_0", 2)
+    m.alloc_streams(2, 512)
+    hist = np.array([5, 6561, 17, 6562, 6560, 0, 4299, 6562], np.int32)
+    m.set_history(1, hist)
+    buf = torch.full((64,), -7, dtype=torch.int32, device="cuda")
+    n = torch.zeros(1, dtype=torch.int32, device="cuda")
+    side = torch.cuda.Stream()
+    m.s3gen_tokens(1, buf.data_ptr(), 64, n.data_ptr(), True, side.cuda_stream)
+    with torch.cuda.stream(side):
+        out = buf.clone()
+        cnt = n.clone()
+    side.synchronize()
+    want = [x for x in hist.tolist() if 0 <= x < 6561] + [4299] * 3
+    assert int(cnt[0]) == len(want)
+    assert out[:len(want)].cpu().tolist() == want
+    m.s3gen_tokens(1, buf.data_ptr(), 3, n.data_ptr(), False, None)   # does not fit: count -1
+    torch.cuda.synchronize()
+    assert int(n[0]) == -1
+    # a decoded utterance: the hand-off equals the host copy minus the stop token
+    m.prefill(0, _prompt(33, 12))
+    toks = m.decode([pkg.SampleParams.make()], 40)[0]
+    m.s3gen_tokens(0, buf.data_ptr(), 64, n.data_ptr(), False, None)
+    torch.cuda.synchronize()
+    want = [x for x in toks.tolist() if x < 6561]
+    assert buf[:int(n[0])].cpu().tolist() == want
+
+
+@pytest.mark.parametrize("quant", ["q4_0", "q8_0", "f16"])
+def test_decode_reference_prompt_shape_past_640(pkg, orc, quant):
+    """The reference's own prompt shape: the Turbo builtin conditioning
+    prompt of 375 speech tokens (src/chatterbox_cli.cpp:707) + 86 text ids =
+    463 positions, then 200 decode steps to position 663, past the 640
+    positions the persistent kernel holds in shared memory at once (its K/V
+    then stream in tiles).  One persistent launch does the whole decode
+    (launch count); every token equals the oracle sampler's draw on the
+    device logits, and the logits stay within the bound of the oracle's
+    teacher-forced logits."""
+    hp = dict(pkg.t3_gguf.T3_TURBO, n_layer=4, cond_prompt_len=375)
+    hp, t = pkg.t3_gguf.random_t3(hp, quant=quant, seed=41)
+    m = pkg.T3Model(hp, t)
+    try:
+        m.alloc_streams(1, 1024)
+        text = _prompt(41, 86)
+        params = dict(top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2)
+        seed, steps = 99, 200
+        n0 = m.launch_count()
+        toks, tr = _decode_traced(pkg, m, text, params, seed, steps, False)
+        assert m.launch_count() - n0 == 2          # first-token sampler + one persistent launch
+        assert toks.size == steps + 1
+        words = orc.mt19937_words(seed, 0, 2 * steps + 4)
+        orc.set_threads(os.cpu_count() or 8)
+        mir = orc.Model(hp, t, max_ctx=1024, gemv_mode=1, gelu_f16=1, kv_f16=1)
+        P, lo = mir.prompt(text)
+        assert P == 463 and P + steps > 640
+        nz = max(noise_floor(orc, hp, t, text, [int(x) for x in toks[:8]], 1024))
+        worst = 0.0
+        for i in range(steps + 1):
+            tok, aux = orc.sample(tr[i], params, words[2 * i], words[2 * i + 1], hist=toks[:i].astype(np.int32))
+            if not aux[2]:
+                assert tok == toks[i], (i, tok, toks[i])
+            e = rel_err(tr[i], lo)
+            worst = max(worst, e)
+            assert e < bound(quant, nz, 1e-3), (i, P + i, e, nz)
+            if i < steps:
+                lo = mir.step(P + i, int(toks[i]))
+        print(f"PARITY long-context {quant}: worst logits rel err {worst:.2e} over positions {P}..{P + steps}")
+    finally:
+        m.close()
