@@ -30,7 +30,7 @@ EXPORTS = [
     "t3b_last_device_ms", "t3b_stream_handle", "t3b_trace_logits", "t3b_get_logits_trace", "t3b_op_row_bytes", "t3b_op_repack", "t3b_op_gemv", "t3b_op_attention",
     "t3b_op_sample_philox", "t3b_expf_fixup_count", "t3b_op_expf", "t3b_op_attention_noalloc",
     "t3b_trace_hidden", "t3b_get_hidden_trace", "t3b_set_wait_limit", "t3b_launch_count", "t3b_s3gen_tokens",
-    "t3b_op_check",
+    "t3b_op_check", "t3b_serve_submit", "t3b_serve_run", "t3b_serve_result",
 ]
 
 
@@ -63,6 +63,13 @@ class SampleParams(C.Structure):
     @classmethod
     def make(cls, top_k=1000, top_p=0.95, temp=0.8, repeat_penalty=1.2, min_p=0.0, cfg_weight=0.0):
         return cls(int(top_k), float(top_p), float(temp), float(repeat_penalty), float(min_p), float(cfg_weight))
+
+
+class Request(C.Structure):
+    """t3b_request: one utterance for the continuous-batching scheduler."""
+    _fields_ = [("text", C.c_void_p), ("n_text", C.c_int32), ("cond_tokens", C.c_void_p), ("n_cond", C.c_int32),
+                ("spk_emb", C.c_void_p), ("params", SampleParams), ("rng_mode", C.c_int32), ("seed", C.c_uint64),
+                ("n_predict", C.c_int32), ("min_tokens", C.c_int32), ("max_retries", C.c_int32)]
 
 
 _lib = None
@@ -109,6 +116,9 @@ def lib():
             "t3b_launch_count": (C.c_uint64, [vp]),
             "t3b_s3gen_tokens": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, C.c_int, vp]),
             "t3b_op_check": (C.c_int, [vp]),
+            "t3b_serve_submit": (C.c_int, [vp, C.POINTER(Request)]),
+            "t3b_serve_run": (C.c_int, [vp, C.c_int, i32p, i32p]),
+            "t3b_serve_result": (C.c_int, [vp, C.c_int, vp, C.c_int, i32p, i32p]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -268,6 +278,35 @@ class T3Model:
         """S3Gen hand-off: the stream's speech tokens into a device buffer."""
         check(lib().t3b_s3gen_tokens(self.ctx, stream, tokens_dev_ptr, int(cap), n_dev_ptr,
                                      1 if append_silence else 0, consumer_stream), self.ctx)
+
+    # ---------------- continuous batching ----------------
+    def serve_submit(self, text, params, seed=0, n_predict=1000, min_tokens=0, max_retries=0,
+                     rng_mode=T3B_RNG_MT19937, cond=None, spk=None):
+        """Queue one utterance; returns its request id."""
+        t = np.ascontiguousarray(text, np.int32)
+        c = None if cond is None else np.ascontiguousarray(cond, np.int32)
+        s = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        r = Request(_ptr(t), t.size, _ptr(c), 0 if c is None else c.size, _ptr(s), params, int(rng_mode), int(seed),
+                    int(n_predict), int(min_tokens), int(max_retries))
+        rid = lib().t3b_serve_submit(self.ctx, C.byref(r))
+        if rid < 0:
+            check(rid, self.ctx)
+        return rid
+
+    def serve_run(self, max_iters):
+        """Run scheduler iterations; returns (n_active, n_queued)."""
+        a, q = C.c_int32(0), C.c_int32(0)
+        check(lib().t3b_serve_run(self.ctx, int(max_iters), C.byref(a), C.byref(q)), self.ctx)
+        return a.value, q.value
+
+    def serve_result(self, rid, cap=16384):
+        """Tokens of a finished request (None while pending), and attempts."""
+        out = np.zeros(cap, np.int32)
+        n, att = C.c_int32(0), C.c_int32(0)
+        rc = lib().t3b_serve_result(self.ctx, int(rid), _ptr(out), cap, C.byref(n), C.byref(att))
+        if rc < 0:
+            check(rc, self.ctx)
+        return (out[:n.value].copy() if rc == 1 else None), att.value
 
     def stream_handle(self):
         """cudaStream_t of this context (int), e.g. for torch.cuda.ExternalStream."""

@@ -141,6 +141,10 @@ struct StepGraph {
 
 }  // namespace
 
+struct ServeState;                       // serve.cuh: continuous-batching scheduler
+ServeState * serve_create();
+void serve_destroy(ServeState * s);
+
 struct t3b_ctx {
     int device = 0;
     cudaStream_t st = nullptr;
@@ -193,6 +197,8 @@ struct t3b_ctx {
     MegaState mega{};
     // logits trace (debug)
     float * trace = nullptr; int trace_cap = 0;
+    // continuous batching over the stream slots (t3b_serve_*)
+    ServeState * serve = nullptr;
 };
 
 #undef ERRP
@@ -239,6 +245,8 @@ void free_streams(t3b_ctx * ctx) {
     ctx->sallocs.clear();
     ctx->S = 0; ctx->R = 0; ctx->kv = nullptr;
     mega_free(ctx->mega);
+    serve_destroy(ctx->serve);
+    ctx->serve = nullptr;
 }
 
 // ----- kernel launch helpers (stream = ctx->st) -----
@@ -601,6 +609,7 @@ int t3b_stream_alloc(t3b_ctx * ctx, int n_streams, int max_ctx, int cfg) {
     CK(cudaMemsetAsync(ctx->kv, 0, sizeof(__half) * ctx->row_elems * rows, ctx->st));
     ctx->pos_host.assign(rows, 0);
     ctx->rng_mode_host.assign(n_streams, T3B_RNG_MT19937);
+    ctx->serve = serve_create();
     // default RNG: std::mt19937 with its default seed 5489, like a
     // default-constructed engine
     for (int s = 0; s < n_streams && rc == T3B_OK; ++s) rc = t3b_set_rng(ctx, s, T3B_RNG_MT19937, 5489u, 0);
@@ -1183,6 +1192,12 @@ int t3b_s3gen_tokens(t3b_ctx * ctx, int stream, int32_t * tokens_dev, int cap, i
     if (consumer_stream) CK(cudaStreamWaitEvent((cudaStream_t) consumer_stream, ctx->hand_ev, 0));
     return T3B_OK;
 }
+
+}  // extern "C"
+
+#include "serve.cuh"
+
+extern "C" {
 
 // ----------------------------- op-level ----------------------------------
 

@@ -156,6 +156,47 @@ int t3b_set_history(t3b_ctx * ctx, int stream, const int32_t * tokens, int n);
 int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_params * params,
                int max_steps, int ignore_stop, int32_t * tokens_out, int32_t * n_out);
 
+/* ---------------- continuous batching (many utterances in flight) -------
+ * Replaces the one-utterance-at-a-time loops of chatterbox.cpp's callers
+ * (Engine::Impl::run_t3, chatterbox_engine.cpp:330-358; the CLI's segment
+ * loop, chatterbox_cli.cpp:1597-1683) for serving: requests queue, each is
+ * admitted into a free stream slot of this context (t3b_stream_alloc sets
+ * the slot count, context length and CFG), every t3b_serve_run iteration
+ * steps all admitted streams as one batch, and a stream that ends (stop
+ * token, n_predict steps or a full cache) frees its slot for the next
+ * request at once.  Per request the loop is run_t3's; a trailing stop token
+ * is popped.  Early-stop retry as the CLI's (chatterbox_cli.cpp:1615-1674):
+ * a stop-token ending shorter than min_tokens replays the request (at most
+ * max_retries times) with its RNG advanced by attempt * 1009 draws, keeping
+ * the longest attempt if all are short (min_tokens 0 = off). */
+typedef struct t3b_request {
+    const int32_t * text;           /* text token ids (copied at submit) */
+    int32_t         n_text;
+    const int32_t * cond_tokens;    /* NULL: the GGUF's builtin voice */
+    int32_t         n_cond;
+    const float *   spk_emb;        /* NULL: builtin speaker embedding */
+    t3b_sample_params params;
+    int32_t         rng_mode;       /* T3B_RNG_MT19937 (std::mt19937(seed)) or T3B_RNG_PHILOX */
+    uint64_t        seed;
+    int32_t         n_predict;      /* decode steps after the first token (Engine n_predict) */
+    int32_t         min_tokens;     /* the CLI uses max(8, 5 * n_text) */
+    int32_t         max_retries;    /* the CLI uses 3 */
+} t3b_request;
+
+/* Queues a request; returns its id (>= 0) or a T3B_ERR_* code. */
+int t3b_serve_submit(t3b_ctx * ctx, const t3b_request * req);
+/* Runs up to max_iters iterations (admit into free slots, one batched
+ * step + sample of every admitted stream, retire ended streams); returns
+ * early when nothing is admitted or queued.  *n_active / *n_queued
+ * (nullable) = streams in slots / requests waiting afterwards.
+ * t3b_last_device_ms() = device time of the iterations' batched steps. */
+int t3b_serve_run(t3b_ctx * ctx, int max_iters, int32_t * n_active, int32_t * n_queued);
+/* 1 when request `id` has finished (min(n, cap) tokens copied to host
+ * tokens_out, *n_out = n), 0 while it is pending; *attempts (nullable) =
+ * attempts made so far.  A request refused at admission (e.g. a prompt
+ * longer than the context) finishes with that error code. */
+int t3b_serve_result(t3b_ctx * ctx, int id, int32_t * tokens_out, int cap, int32_t * n_out, int32_t * attempts);
+
 /* Engine::cancel() equivalent (chatterbox_engine.cpp:546-548). */
 void t3b_cancel(t3b_ctx * ctx);
 

@@ -6,7 +6,7 @@ import os
 import numpy as np
 import pytest
 
-from conftest import ROOT, noise_floor, rel_err, synth_logits
+from conftest import ROOT, noise_floor, nudged, rel_err, synth_logits
 
 pytestmark = pytest.mark.gpu
 
@@ -331,10 +331,14 @@ def test_errors_are_reported(pkg):
 def test_layer_outputs_match_oracle(pkg, orc, quant, graph_path):
     """Residual stream after every layer of one t3b_step (persistent kernel,
     or the CUDA-graph path) against the oracle's teacher-forced step on the
-    same prompt.  The first two layers, before the Q8_0 re-quantisation
-    noise compounds, are held to the logits tolerances of the target (rel
-    1e-2 Q4_0, 2e-3 Q8_0 / F16); the reached error of every layer is
-    printed (PARITY lines)."""
+    same prompt.  The first layer, before any Q8_0 re-quantisation flip can
+    compound, is held to the logits tolerances of the target (rel 1e-2
+    Q4_0, 2e-3 Q8_0 / F16).  Every later layer is held to the target
+    tolerance or to 4x the oracle's own sensitivity at that layer (its
+    residual stream under a 1-ulp change of the positions), whichever is
+    larger: this locates the depth at which a flip of ggml's activation
+    rounding appears.  Reached errors and sensitivities are printed (PARITY
+    lines)."""
     hp, t, m = model(pkg, quant, 24, seed=21)
     m.alloc_streams(1, 256)
     text = _prompt(2, 40)
@@ -353,11 +357,18 @@ def test_layer_outputs_match_oracle(pkg, orc, quant, graph_path):
         m.trace_hidden(False)
     assert P2 == P
     lo, ho = mir.step_trace(P, 321)
+    nud = orc.Model(hp, nudged(t), max_ctx=256, gemv_mode=1, gelu_f16=1, kv_f16=1)
+    nud.prompt(text)
+    ln, hn = nud.step_trace(P, 321)
     errs = [rel_err(hid[i], ho[i]) for i in range(hid.shape[0])]
+    sens = [rel_err(hn[i], ho[i]) for i in range(hid.shape[0])]
     path = "graph" if graph_path else "persistent"
     print(f"PARITY layers {quant} {path}: " + " ".join(f"{e:.2e}" for e in errs) + f" logits {rel_err(g, lo):.2e}")
+    print(f"PARITY oracle-1ulp {quant}: " + " ".join(f"{e:.2e}" for e in sens) + f" logits {rel_err(ln, lo):.2e}")
     assert errs[0] < 1e-6                                     # embedding: f16 row + f32 position, exact
-    assert max(errs[1], errs[2]) < TOL[quant], errs[:3]
+    assert errs[1] < TOL[quant], errs[:2]
+    for i in range(2, len(errs)):
+        assert errs[i] < max(TOL[quant], 4.0 * sens[i]), (i, errs[i], sens[i])
     assert all(np.isfinite(hid).ravel())
 
 
