@@ -201,7 +201,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="leave out the batched CFG run (profiling commands)")
-    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels", "sweep"], default=None,
+    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels", "sweep", "serve3", "serve4"],
+                    default=None,
                     help="run one kernel micro-benchmark alone (ncu captures), or the megakernel phase timeline")
     args = ap.parse_args()
     if args.only:
@@ -217,6 +218,8 @@ def main():
         elif args.only == "kernels":
             import torch
             r = batched_kernels(pkg, torch, peak)
+        elif args.only in ("serve3", "serve4"):
+            r = serving(pkg, torch, peak, int(args.only[-1]), None, 1, 0, 0, steps=args.steps if args.steps != 256 else None)
         elif args.only == "sweep":
             import torch
             r = gemv_sweep(pkg, torch, peak)
@@ -313,7 +316,9 @@ def main():
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
             "sampler": sampler_microbench(pkg, torch, peak),
-            "batched_cfg": batched_cfg(pkg, torch, peak) if rank == 0 and not args.no_batched else None,
+            "serving_configs3": serving(pkg, torch, peak, 3, dist, ws, rank, local) if not args.no_batched else None,
+            "serving_configs4": ({q: serving(pkg, torch, peak, 4, dist, ws, rank, local, quant=q) for q in ("q4_0", "f16")}
+                                 if ws == 8 and not args.no_batched else None),
             "batched_kernels": batched_kernels(pkg, torch, peak),
             "gemv_sweep": gemv_sweep(pkg, torch, peak) if not args.no_batched else None,
             "e2e": e2e, "clocks": clk.summary(),
@@ -328,6 +333,77 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def serving(pkg, torch, peak, which, dist, ws, rank, local, quant=None, steps=None):
+    """BASELINE configs[3] (which=3) or configs[4] (which=4) through the
+    continuous-batching scheduler (t3b_serve_*), streams sharded over the
+    ranks by expected KV cost (greedy LPT, sharding.assign_streams).
+
+    64 utterances with CFG (128 rows), prompts U[100, 400],
+    decode to 1024 tokens (or a stop token), Q8_0.  configs[4]: 512 with
+    CFG (1024 rows over 8 GPUs), contexts U[50, 2048] (prompt U[50, 2048-K],
+    then K decode steps), Q4_0 or F16, per-stream temperature U[0.6, 1.0],
+    top_p U[0.8, 1.0] and penalty U[1.0, 1.5]; every stream draws from its
+    own Philox stream.  Seeded synthetic prompts; random-init weights.
+
+    value = decode tokens of all ranks / max over ranks of the device time
+    of the batched steps (t3b_serve_stats); wall = the same tokens over the
+    slowest rank's wall time of the whole serve loop (admission prefills,
+    host bookkeeping and every step's token read-back included)."""
+    rng = np.random.default_rng(1000 + which)
+    if which == 3:
+        n_total, quant, K = 64, quant or "q8_0", steps or 1024
+        P = rng.integers(100, 401, n_total)
+        prm = [pkg.SampleParams.make(**PARAMS, cfg_weight=0.5) for _ in range(n_total)]
+    else:
+        n_total, quant, K = 512, quant or "q4_0", steps or 128
+        P = rng.integers(50, 2049 - K, n_total)
+        temp, top_p, pen = rng.uniform(0.6, 1.0, n_total), rng.uniform(0.8, 1.0, n_total), rng.uniform(1.0, 1.5, n_total)
+        prm = [pkg.SampleParams.make(top_k=1000, top_p=float(top_p[i]), temp=float(temp[i]),
+                                     repeat_penalty=float(pen[i]), cfg_weight=0.5) for i in range(n_total)]
+    costs = [pkg.sharding.stream_cost(int(p), K, cfg=True) for p in P]
+    mine = pkg.sharding.assign_streams(costs, ws)[rank]
+    hp = dict(pkg.t3_gguf.T3_TURBO)
+    hp, t = pkg.t3_gguf.random_t3(hp, quant=quant, seed=3)
+    m = pkg.T3Model(hp, t, device=local)
+    m.alloc_streams(len(mine), int(max(P[i] for i in mine)) + K + 8, cfg=True)
+    for i in mine:
+        ri = np.random.default_rng(5000 + i)
+        n_cond = min(hp["cond_prompt_len"], int(P[i]) - 3)     # short contexts use fewer conditioning tokens
+        cond = ri.integers(0, hp["start_speech_token"], n_cond).astype(np.int32)
+        text = ri.integers(0, 50257, int(P[i]) - 2 - n_cond).astype(np.int32)
+        m.serve_submit(text, prm[i], seed=7000 + i, n_predict=K, rng_mode=pkg.T3B_RNG_PHILOX, cond=cond)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    while True:
+        act, q = m.serve_run(256)
+        if act == 0 and q == 0:
+            break
+    wall = time.perf_counter() - t0
+    tokens, step_ms = m.serve_stats()
+    m.close()
+    value, ms = pkg.sharding.job_throughput(dist, step_ms, tokens, ws)
+    wall_value, wall_ms = pkg.sharding.job_throughput(dist, wall * 1000.0, tokens, ws)
+    # algorithmic bytes of the decode steps: weights once per step plus every
+    # row's K/V (98 304 B per cached position) and logits
+    wbytes = model_weight_bytes(t)
+    kvp = 2 * hp["n_layer"] * hp["n_embd"] * 2
+    rows_pos = sum(2 * (int(P[i]) + (K + 1) / 2.0) for i in mine)    # mean context per row over the decode
+    local_steps = max(1.0, tokens / max(1, len(mine)))
+    step_bytes = wbytes + kvp * rows_pos + 2 * len(mine) * hp["n_speech_vocab"] * 4
+    ach = step_bytes * local_steps / (step_ms / 1000.0) / 1e9 if step_ms > 0 else 0.0
+    return {"config": f"configs[{which}]: {n_total} utterances x CFG, {quant.upper()}, "
+                      + ("prompts U[100,400], decode to 1024 tokens or stop" if which == 3 else
+                         f"contexts U[50,2048] (prompt U[50,{2048 - K}] + {K} decode steps), per-stream "
+                         "temp U[0.6,1] / top_p U[0.8,1] / penalty U[1,1.5]")
+                      + f"; streams sharded over {ws} GPU(s) by KV cost",
+            "value": value, "unit": UNIT, "scaling": "strong", "n_gpus": ws, "decode_tokens": int(tokens),
+            "device_ms": ms, "wall_tokens_per_s": wall_value, "wall_ms": wall_ms,
+            "rank0_streams": len(mine), "rank0_achieved_gbs": ach, "rank0_frac": ach / peak, "peak": peak,
+            "path": "t3b_serve_run: admit (prefill + first sample) into free slots, one batched step + sampler "
+                    "per iteration over all admitted streams, retire at stop / n_predict"}
 
 
 def sampler_microbench(pkg, torch, peak, reps=200):

@@ -30,7 +30,7 @@ EXPORTS = [
     "t3b_last_device_ms", "t3b_stream_handle", "t3b_trace_logits", "t3b_get_logits_trace", "t3b_op_row_bytes", "t3b_op_repack", "t3b_op_gemv", "t3b_op_attention",
     "t3b_op_sample_philox", "t3b_expf_fixup_count", "t3b_op_expf", "t3b_op_attention_noalloc",
     "t3b_trace_hidden", "t3b_get_hidden_trace", "t3b_set_wait_limit", "t3b_launch_count", "t3b_s3gen_tokens",
-    "t3b_op_check", "t3b_serve_submit", "t3b_serve_run", "t3b_serve_result",
+    "t3b_op_check", "t3b_op_attention_prompt", "t3b_serve_submit", "t3b_serve_run", "t3b_serve_result", "t3b_serve_stats",
 ]
 
 
@@ -116,9 +116,11 @@ def lib():
             "t3b_launch_count": (C.c_uint64, [vp]),
             "t3b_s3gen_tokens": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, C.c_int, vp]),
             "t3b_op_check": (C.c_int, [vp]),
+            "t3b_op_attention_prompt": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
             "t3b_serve_submit": (C.c_int, [vp, C.POINTER(Request)]),
             "t3b_serve_run": (C.c_int, [vp, C.c_int, i32p, i32p]),
             "t3b_serve_result": (C.c_int, [vp, C.c_int, vp, C.c_int, i32p, i32p]),
+            "t3b_serve_stats": (C.c_int, [vp, C.POINTER(C.c_longlong), C.POINTER(C.c_double)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -307,6 +309,12 @@ class T3Model:
         if rc < 0:
             check(rc, self.ctx)
         return (out[:n.value].copy() if rc == 1 else None), att.value
+
+    def serve_stats(self):
+        """(tokens sampled by batched steps, their device ms) since alloc_streams."""
+        n, ms = C.c_longlong(0), C.c_double(0)
+        check(lib().t3b_serve_stats(self.ctx, C.byref(n), C.byref(ms)), self.ctx)
+        return n.value, ms.value
 
     def stream_handle(self):
         """cudaStream_t of this context (int), e.g. for torch.cuda.ExternalStream."""

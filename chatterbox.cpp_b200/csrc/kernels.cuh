@@ -782,6 +782,175 @@ __global__ __launch_bounds__(128) void attn_rows_kernel(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Causal attention over a prompt chunk (eval_prompt's ggml_flash_attn_ext
+// with the causal mask, main.cpp:663-677): the M query rows are consecutive
+// positions of ONE cache row (row m at position len[m], attending keys
+// 0 .. len[m] + len_add - 1).  Flash-attention tiling: a CTA takes 64 query
+// rows of one head and walks the keys in tiles of 64 staged in shared
+// memory, so every K/V row is read once per query tile instead of once per
+// query row.  Online softmax per query row; f32 arithmetic on f16 K/V, the
+// score q.k / 8 as in the decode kernels.  Thread (ty, tx) of 16 x 16 holds
+// a 4 x 4 block: queries 4ty.., keys 4tx.. for the scores, dims 4tx.. of the
+// output.  Optional Q8_0 output (the out-projection's input) as in
+// attn_rows_kernel.
+// grid = (n_head, ceil(M / 64)), 256 threads, T3B_PREFILL_SMEM dynamic smem.
+// ---------------------------------------------------------------------------
+#define T3B_PF_T 64
+#define T3B_PF_LD (T3B_PF_T + 4)   // padded rows (floats), 16-byte aligned
+#define T3B_PREFILL_SMEM (4 * T3B_PF_T * T3B_PF_LD * 4)
+__global__ __launch_bounds__(256) void attn_prefill_kernel(AttnArgs a, int M) {
+    extern __shared__ __align__(16) float pf_sm[];
+    float * qT = pf_sm;                           // [d][q]
+    float * kT = qT + T3B_PF_T * T3B_PF_LD;       // [d][k]
+    float * vS = kT + T3B_PF_T * T3B_PF_LD;       // [k][d]
+    float * pT = vS + T3B_PF_T * T3B_PF_LD;       // [k][q]
+    __shared__ int lmax_s;
+    const int h = blockIdx.x, m0 = blockIdx.y * T3B_PF_T, tid = threadIdx.x;
+    const int ty = tid >> 4, tx = tid & 15;
+    if (tid == 0) lmax_s = 0;
+    __syncthreads();
+    int Lq[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + 4 * ty + i;
+        Lq[i] = 0;
+        if (m < M) {
+            const int L = a.len[m] + a.len_add;
+            if (L <= 0 || L > a.max_ctx) { if (tx == 0) atomicOr(a.err, T3B_DEVERR_POS); }
+            else Lq[i] = L;
+        }
+        if (tx == 0 && Lq[i] > 0) atomicMax(&lmax_s, Lq[i]);
+    }
+    // Q tile, transposed
+    for (int e = tid; e < T3B_PF_T * T3B_HD; e += 256) {
+        const int qi = e >> 6, d = e & 63, m = m0 + qi;
+        qT[d * T3B_PF_LD + qi] = m < M ? a.q[(size_t) m * a.ldq + h * T3B_HD + d] : 0.0f;
+    }
+    __syncthreads();
+    const int Lmax = lmax_s;
+    const int crow = a.row_of ? a.row_of[m0] : m0;
+    const __half * kb = a.kv + (size_t) crow * a.row_elems + a.layer_off + (size_t) h * a.max_ctx * T3B_HD;
+    const __half * vb = kb + a.v_off;
+    float mrun[4], lrun[4], o[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        mrun[i] = -INFINITY; lrun[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
+    }
+    for (int k0 = 0; k0 < Lmax; k0 += T3B_PF_T) {
+        // K (transposed) and V tiles: thread -> key tid / 4, dims 16 (tid % 4) ..
+        {
+            const int kk = tid >> 2, c = (tid & 3) * 16, j = k0 + kk;
+            uint4 k2[2], v2[2];
+            if (j < Lmax) {
+                k2[0] = __ldg((const uint4 *) (kb + (size_t) j * T3B_HD + c));
+                k2[1] = __ldg((const uint4 *) (kb + (size_t) j * T3B_HD + c + 8));
+                v2[0] = __ldg((const uint4 *) (vb + (size_t) j * T3B_HD + c));
+                v2[1] = __ldg((const uint4 *) (vb + (size_t) j * T3B_HD + c + 8));
+            } else {
+                k2[0] = k2[1] = v2[0] = v2[1] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            const __half * kh = (const __half *) k2;
+            const __half * vh = (const __half *) v2;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                kT[(c + e) * T3B_PF_LD + kk] = __half2float(kh[e]);
+                vS[kk * T3B_PF_LD + c + e] = __half2float(vh[e]);
+            }
+        }
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+#pragma unroll 8
+        for (int d = 0; d < T3B_HD; ++d) {
+            const float4 qa = *(const float4 *) (qT + d * T3B_PF_LD + 4 * ty);
+            const float4 ka = *(const float4 *) (kT + d * T3B_PF_LD + 4 * tx);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sc[i][j] = fmaf(qv[i], kv[j], sc[i][j]);
+        }
+        float corr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float rm = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                sc[i][j] = k0 + 4 * tx + j < Lq[i] ? sc[i][j] * 0.125f : -INFINITY;
+                rm = fmaxf(rm, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, off));
+            const float mn = fmaxf(mrun[i], rm);
+            corr[i] = mrun[i] == -INFINITY ? 0.0f : expf(mrun[i] - mn);
+            float ps = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - mn);
+                pT[(4 * tx + j) * T3B_PF_LD + 4 * ty + i] = p;
+                ps += p;
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            lrun[i] = lrun[i] * corr[i] + ps;
+            mrun[i] = mn;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[i][j] *= corr[i];
+        const int kn = min(T3B_PF_T, Lmax - k0);
+#pragma unroll 4
+        for (int k = 0; k < kn; ++k) {
+            const float4 pa = *(const float4 *) (pT + k * T3B_PF_LD + 4 * ty);
+            const float4 va = *(const float4 *) (vS + k * T3B_PF_LD + 4 * tx);
+            const float pv[4] = {pa.x, pa.y, pa.z, pa.w}, vv[4] = {va.x, va.y, va.z, va.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o[i][j] = fmaf(pv[i], vv[j], o[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + 4 * ty + i;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = Lq[i] > 0 ? o[i][j] / lrun[i] : 0.0f;
+        if (m < M && Lq[i] > 0)
+            *(float4 *) (a.out + (size_t) m * a.ldo + h * T3B_HD + 4 * tx) = make_float4(v[0], v[1], v[2], v[3]);
+        if (a.qx) {   // Q8_0 block (tx / 8) of the head: eight lanes hold its 32 dims
+            float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            int q[4], sq = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { q[j] = (int) roundf(__fmul_rn(v[j], id)); sq += q[j]; }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+            if (m < M && Lq[i] > 0) {
+                *(int *) (a.qx + (size_t) m * a.ldo + h * T3B_HD + 4 * tx) =
+                    (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((q[3] & 0xff) << 24);
+                if ((tx & 7) == 0) {
+                    const size_t blk = (size_t) m * (a.ldo / 32) + h * 2 + (tx >> 3);
+                    a.qd[blk] = __half2float(__float2half_rn(d));
+                    a.qs[blk] = sq;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Fused sampler
 // ---------------------------------------------------------------------------
 struct ExpFix { const unsigned long long * tab; int bits; int n; };   // n = fix-up entries (0: none)

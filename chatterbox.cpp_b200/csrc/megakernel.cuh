@@ -765,19 +765,158 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
     mk_prefetch<T>((W), (K), r0_, r1_, pf_);
 
 
+// Bulk-copy bookkeeping of a CTA, one register (every thread holds the same
+// value): per mbarrier i (0: K rows + q/k/v weights, 1: V rows / tile
+// buffer B, 2: head rows, 3: tile buffer A) bit 2i = a phase was issued
+// and not yet waited for, bit 2i+1 = that phase's parity; bits 8 and 9 =
+// the parity of the next phase of mbarriers 1 and 3.
+#define CP_OUT(i) ((cp >> (2 * (i))) & 1u)
+#define CP_PAR(i) ((cp >> (2 * (i) + 1)) & 1u)
+#define CP_ISSUE(i, par) (cp = (cp & ~(3u << (2 * (i)))) | ((1u | (((unsigned) (par) & 1u) << 1)) << (2 * (i))))
+#define CP_DONE(i) (cp &= ~(1u << (2 * (i))))
+// issue on mbarrier 1 or 3, whose phases alternate parity
+#define CP_ISSUE_NEXT(i, nb) do { CP_ISSUE(i, (cp >> (nb)) & 1u); cp ^= 1u << (nb); } while (0)
+
+// waits (bounded, MK_SPIN polls each) for every copy phase still in flight
+__device__ __noinline__ void mk_drain(unsigned long long * mbar, unsigned cp) {
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i)
+        if (CP_OUT(i)) mk_mbar_wait(&mbar[i], CP_PAR(i));
+}
+
 // every exit first waits (bounded) for this CTA's copies still in flight
 #define MK_BAIL do {                                                                  \
         asm volatile("cp.async.wait_all;" ::: "memory");                              \
-        if (tid == 0) {                                                               \
-            if (kw_out >= 0) mk_mbar_wait(&mbar[0], (unsigned) kw_out & 1u);          \
-            if (v_out >= 0) mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u);            \
-            if (hd_out >= 0) mk_mbar_wait(&mbar[2], (unsigned) hd_out & 1u);          \
-            if (a_out >= 0) mk_mbar_wait(&mbar[3], (unsigned) a_out & 1u);            \
-        }                                                                             \
+        if (tid == 0 && (cp & 0xffu)) mk_drain(mbar, cp);                            \
         return;                                                                       \
     } while (0)
 
-template <int T>
+// ---------------------------------------------------------------------------
+// contexts longer than MK_MAX_POS: K/V streamed in tiles of MK_TP positions
+// (out of line: the loop is rarely taken, and inlined into the layer loop its
+// code slowed every phase of the common case by ~9%)
+// ---------------------------------------------------------------------------
+// Tile i of positions [0, npos) of one head (K rows, then V rows at row
+// MK_TP) into buffer A (kst, mbarrier 3) or B (vst, mbarrier 1), issued by
+// the CTA's copy thread; every thread updates the bookkeeping.  The current
+// position is never copied: its K/V come from the q/k/v outputs.
+__device__ __noinline__ unsigned mk_issue_tile(unsigned cp, int i, int npos, const __half * kb, size_t v_off, bool inB,
+                                               __half * kst, __half * vst, unsigned long long * mbar) {
+    if (threadIdx.x == MK_THREADS - 32) {
+        const int t0 = i * MK_TP;
+        const int n = max(0, min(MK_TP, npos - t0));
+        const unsigned rb = (unsigned) n * T3B_HD * 2;
+        __half * dst = inB ? vst : kst;
+        unsigned long long * mb = inB ? &mbar[1] : &mbar[3];
+        mk_fence_proxy_async();   // K/V rows this CTA stored (generic proxy) are read by the bulk copy
+        mk_mbar_expect(mb, 2u * rb);
+        if (n > 0) {
+            mk_bulk_g2s(dst, kb + (size_t) t0 * T3B_HD, rb, mb);
+            mk_bulk_g2s(dst + (size_t) MK_TP * T3B_HD, kb + v_off + (size_t) t0 * T3B_HD, rb, mb);
+        }
+    }
+    if (inB) CP_ISSUE_NEXT(1, 8);
+    else CP_ISSUE_NEXT(3, 9);
+    return cp;
+}
+
+// One head's attention over L = pos + 1 > MK_MAX_POS positions: tiles
+// through buffers A and B with an online softmax (running max, per-thread
+// sums and per-warp outputs rescaled when the max grows).  Tile 0 is
+// expected in A (tile0_ready: it came with the q/k/v weights), tile 1 in B
+// (issued by the caller); this issues tiles 2.. as buffers free up.  Writes
+// the per-warp outputs og[16][64] and returns the softmax denominator, or a
+// negative value (every thread) when a copy wait gave up; *cpp is updated.
+__device__ __noinline__ float mk_attend_tiled(unsigned * cpp, bool tile0_ready, int pos, const __half * kb, size_t v_off,
+                                              const float * qkvh, __half * kst, __half * vst, float * pw, float * rf,
+                                              float * og, unsigned long long * mbar, int * okf, unsigned spin,
+                                              unsigned * err, int * abort_flag) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int L = pos + 1, nt = (L + MK_TP - 1) / MK_TP;
+    unsigned cp = *cpp;
+    float m_run = -INFINITY, l_t = 0.0f;
+    float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < nt; ++i) {
+        const bool inB = (i & 1) != 0;
+        const int bi = inB ? 1 : 3;
+        __half * tb = inB ? vst : kst;
+        if (!(tile0_ready && i == 0)) {
+            if (tid == 0) {
+                const bool ok = mk_mbar_wait(&mbar[bi], CP_PAR(bi), spin);
+                if (!ok) { atomicOr(err, T3B_DEVERR_TIMEOUT); atomicExch(abort_flag, 1); }
+                *okf = ok;
+            }
+            __syncthreads();
+            if (!*okf) { *cpp = cp; return -1.0f; }
+            CP_DONE(bi);
+        }
+        const int t0 = i * MK_TP, n = min(MK_TP, L - t0);
+        if (i == nt - 1 && tid < 2 * T3B_HD) {   // the current position, f16 as in the cache
+            const int c = tid & 63, vv = tid >> 6;
+            tb[(size_t) (vv * MK_TP + pos - t0) * T3B_HD + c] = __float2half_rn(qkvh[64 + tid]);
+        }
+        __syncthreads();
+        float sc = -INFINITY;
+        if (tid < n) {
+            const uint4 * kp = (const uint4 *) (tb + (size_t) tid * T3B_HD);
+            float dot = 0.0f;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const int c = (cc + tid) & 7;
+                const uint4 uu = kp[c];
+                const float4 qa = *(const float4 *) (qkvh + c * 8), qb = *(const float4 *) (qkvh + c * 8 + 4);
+                const __half2 * hp = (const __half2 *) &uu;
+                const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
+                const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
+                dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
+                dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
+                dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
+                dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
+            }
+            sc = dot * 0.125f;
+        }
+        const float lm = warp_max(sc);
+        if (lane == 0) rf[w] = lm;
+        __syncthreads();
+        const float m_new = fmaxf(m_run, warp_max(rf[lane & 15]));
+        const float resc = expf(m_run - m_new);   // 0 for the first tile
+        m_run = m_new;
+        const float p = tid < n ? expf(sc - m_new) : 0.0f;
+        if (tid < n) pw[tid] = p;
+        l_t = __fmaf_rn(l_t, resc, p);
+        __syncthreads();
+        const __half * vt = tb + (size_t) MK_TP * T3B_HD;
+        o0.x *= resc; o0.y *= resc; o1.x *= resc; o1.y *= resc;
+        int j = w;
+        for (; j + 16 < n; j += 32) {
+            const float2 v0 = __half22float2(*(const __half2 *) (vt + (size_t) j * T3B_HD + 2 * lane));
+            const float2 v1 = __half22float2(*(const __half2 *) (vt + (size_t) (j + 16) * T3B_HD + 2 * lane));
+            const float p0 = pw[j], p1 = pw[j + 16];
+            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+            o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
+        }
+        if (j < n) {
+            const float2 v0 = __half22float2(*(const __half2 *) (vt + (size_t) j * T3B_HD + 2 * lane));
+            const float p0 = pw[j];
+            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+        }
+        __syncthreads();   // tile buffer, pw and rf free again
+        if (i + 2 < nt) cp = mk_issue_tile(cp, i + 2, pos, kb, v_off, inB, kst, vst, mbar);
+    }
+    const float ls = warp_sum(l_t);
+    if (lane == 0) rf[32 + w] = ls;
+    og[w * 64 + 2 * lane] = o0.x + o1.x;
+    og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
+    __syncthreads();
+    *cpp = cp;
+    return warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
+}
+
+// LONG: the instantiation that can stream K/V in tiles past MK_MAX_POS
+// positions.  The host launches it only when a decode will pass that many
+// positions; the common instantiation carries none of that code, which
+// (measured) keeps every phase of the short-context step ~12% faster.
+template <int T, bool LONG>
 __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int D = 1024;
@@ -837,14 +976,14 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // n_layer + layer completes phase u), plus its V rows when K and V of
     // positions [0, pos] fit the K stage together ("packed": V at row pos+1);
     // otherwise mbar[1] = the V rows, loaded into the weight stage after the
-    // q/k/v rows are computed (vph counts its phases).  kw_out / v_out: phase
-    // of a copy issued and not yet waited for.
+    // q/k/v rows are computed.
     // mbar[2] (every CTA, Q4_0 head): this CTA's head rows, one phase per step.
     // Contexts longer than MK_MAX_POS (any layout): K/V tiles stream through
-    // buffer A (kst; mbar[3], aph phases) and buffer B (vst; mbar[1]).
+    // buffer A (kst; mbar[3]) and buffer B (vst; mbar[1]).
+    // cp: which phases are in flight and their parities (CP_* above).
     __shared__ __align__(8) unsigned long long mbar[4];
     __shared__ int okf;
-    int kw_out = -1, v_out = -1, vph = 0, hd_out = -1, a_out = -1, aph = 0;
+    unsigned cp = 0u;
     if (tid == 0) {
         mk_mbar_init(&mbar[0]);
         mk_mbar_init(&mbar[1]);
@@ -865,13 +1004,13 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             mk_mbar_expect(&mbar[2], bytes);
             if (bytes) mk_bulk_g2s_w(kst, a.head.w + (size_t) hr0 * MK_QKVW_ROW, bytes, &mbar[2]);
         }
-        hd_out = step_;
+        CP_ISSUE(2, step_);
     };
     // OWN attention CTAs: bulk copies of use u's K rows [0, npos) of layer nl
     // and of that layer's q/k/v weights for this head, issued by the last
     // warp's first thread (not the hand-off poller)
     auto packed = [](int p) { return 2 * (p + 1) <= MK_MAX_POS; };
-    auto tiled = [](int p) { return p + 1 > MK_MAX_POS; };
+    auto tiled = [](int p) { return LONG && p + 1 > MK_MAX_POS; };
     auto issue_kw = [&](int u, int nl, int npos) {
         if (tid == MK_THREADS - 32) {
             const bool tl = tiled(npos);
@@ -888,39 +1027,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             }
             mk_bulk_qkvw(qkvw, a.layers[nl].qkv, hh_, &mbar[0]);
         }
-        kw_out = u;
-    };
-    // long contexts: tile i of positions [0, npos) (K rows, then V rows at
-    // row MK_TP) into buffer A (kst, mbar[3]) or B (vst, mbar[1]); the
-    // current position is never copied (its K/V come from the q/k/v outputs)
-    auto issue_tile = [&](int i, int npos, const __half * kb_, bool inB) {
-        if (tid == MK_THREADS - 32) {
-            const int t0 = i * MK_TP;
-            const int n = max(0, min(MK_TP, npos - t0));
-            const unsigned rb = (unsigned) n * T3B_HD * 2;
-            __half * dst = inB ? vst : kst;
-            unsigned long long * mb = inB ? &mbar[1] : &mbar[3];
-            mk_fence_proxy_async();
-            mk_mbar_expect(mb, 2u * rb);
-            if (n > 0) {
-                mk_bulk_g2s(dst, kb_ + (size_t) t0 * T3B_HD, rb, mb);
-                mk_bulk_g2s(dst + (size_t) MK_TP * T3B_HD, kb_ + a.v_off + (size_t) t0 * T3B_HD, rb, mb);
-            }
-        }
-        if (inB) v_out = vph++;
-        else a_out = aph++;
-    };
-    // wait (one thread, bounded) for the outstanding phase `ph` of mb
-    auto wait_copy = [&](unsigned long long * mb, int & ph) -> bool {
-        if (tid == 0) {
-            const bool ok = mk_mbar_wait(mb, (unsigned) ph & 1u, a.spin);
-            if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
-            okf = ok;
-        }
-        __syncthreads();
-        if (!okf) return false;
-        ph = -1;
-        return true;
+        CP_ISSUE(0, u);
     };
     unsigned * cQKV = a.cnt + MK_C_QKV * MK_C_STRIDE, * cATT = a.cnt + MK_C_ATT * MK_C_STRIDE;
     unsigned * cXM = a.cnt + MK_C_XM * MK_C_STRIDE, * cH = a.cnt + MK_C_H * MK_C_STRIDE;
@@ -1012,7 +1119,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     }
                     __syncthreads();
                     if (!okf) MK_BAIL;
-                    kw_out = -1;
+                    CP_DONE(0);
                     MK_STAMP(l * 20 + 14);
                     mk_qkv_own(qkvw, act, qkvh);
                     __syncthreads();
@@ -1021,7 +1128,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     __half * vrow = pk ? kst + (size_t) (pos + 1) * T3B_HD : vst;
                     if (tiled(pos)) {
                         // tile 0 came with the weights; tile 1 replaces them
-                        if (pos >= MK_TP) issue_tile(1, pos, kb, true);
+                        cp = mk_issue_tile(cp, 1, pos, kb, a.v_off, true, kst, vst, mbar);
                     } else if (!pk) {
                         // V rows [0, pos) replace the weights (every read of
                         // them finished before the barrier above).  Issued by
@@ -1030,7 +1137,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             mk_mbar_expect(&mbar[1], (unsigned) pos * T3B_HD * 2);
                             if (pos > 0) mk_bulk_g2s(vst, kb + a.v_off, (unsigned) pos * T3B_HD * 2, &mbar[1]);
                         }
-                        v_out = vph++;
+                        CP_ISSUE_NEXT(1, 8);
                     }
                     MK_STAMP(l * 20 + 16);
                     if (tid < 3 * T3B_HD) {
@@ -1089,8 +1196,8 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) h * a.max_ctx * T3B_HD;
                 const __half * vb = kb + a.v_off;
                 if (!OWN && tiled(pos)) {
-                    issue_tile(0, pos, kb, false);
-                    if (pos >= MK_TP) issue_tile(1, pos, kb, true);
+                    cp = mk_issue_tile(cp, 0, pos, kb, a.v_off, false, kst, vst, mbar);
+                    cp = mk_issue_tile(cp, 1, pos, kb, a.v_off, true, kst, vst, mbar);
                 } else if (!OWN) {
                     // stage K/V of positions [0, pos) while q/k/v are computed
                     mk_stage_kv(kst, kb, pos);
@@ -1162,9 +1269,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     }
                     ls = warp_sum(ls);
                     if (lane == 0) rf[32 + w] = ls;
-                    const bool vwait = OWN && v_out >= 0;   // V rows loaded separately (not packed)
+                    const bool vwait = OWN && CP_OUT(1);   // V rows loaded separately (not packed)
                     if (vwait && tid == 0) {   // this layer's V rows
-                        const bool ok = mk_mbar_wait(&mbar[1], (unsigned) v_out & 1u, a.spin);
+                        const bool ok = mk_mbar_wait(&mbar[1], CP_PAR(1), a.spin);
                         if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                         okf = ok;
                         MK_STAMP(l * 20 + 3);
@@ -1172,7 +1279,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     __syncthreads();
                     if (vwait) {
                         if (!okf) MK_BAIL;
-                        v_out = -1;
+                        CP_DONE(1);
                     }
                     const __half * vsrc = (OWN && packed(pos)) ? kst + (size_t) (pos + 1) * T3B_HD : vst;
                     lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
@@ -1195,80 +1302,18 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         }
                     }
                 } else {
-                    // L > MK_MAX_POS: tiles of MK_TP positions through buffers A
-                    // and B, online softmax (running max m, per-thread sums
-                    // and per-warp outputs rescaled when the max grows)
-                    const int nt = (L + MK_TP - 1) / MK_TP;
-                    float m_run = -INFINITY, l_t = 0.0f;
-                    for (int i = 0; i < nt; ++i) {
-                        const bool inB = (i & 1) != 0;
-                        __half * tb = inB ? vst : kst;
-                        if (!(OWN && i == 0)) {   // OWN: tile 0 arrived with the weights
-                            if (!wait_copy(inB ? &mbar[1] : &mbar[3], inB ? v_out : a_out)) MK_BAIL;
-                        }
-                        const int t0 = i * MK_TP, n = min(MK_TP, L - t0);
-                        if (i == nt - 1 && tid < 2 * T3B_HD) {   // the current position, f16 as in the cache
-                            const int c = tid & 63, vv = tid >> 6;
-                            tb[(size_t) (vv * MK_TP + pos - t0) * T3B_HD + c] = __float2half_rn(qkvh[64 + tid]);
-                        }
-                        __syncthreads();
-                        float sc = -INFINITY;
-                        if (tid < n) {
-                            const uint4 * kp = (const uint4 *) (tb + (size_t) tid * T3B_HD);
-                            float dot = 0.0f;
-#pragma unroll
-                            for (int cc = 0; cc < 8; ++cc) {
-                                const int c = (cc + tid) & 7;
-                                const uint4 uu = kp[c];
-                                const float4 qa = *(const float4 *) (qkvh + c * 8), qb = *(const float4 *) (qkvh + c * 8 + 4);
-                                const __half2 * hp = (const __half2 *) &uu;
-                                const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
-                                const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
-                                dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
-                                dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
-                                dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
-                                dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
-                            }
-                            sc = dot * 0.125f;
-                        }
-                        const float lm = warp_max(sc);
-                        if (lane == 0) rf[w] = lm;
-                        __syncthreads();
-                        const float m_new = fmaxf(m_run, warp_max(rf[lane & 15]));
-                        const float resc = expf(m_run - m_new);   // 0 for the first tile
-                        m_run = m_new;
-                        const float p = tid < n ? expf(sc - m_new) : 0.0f;
-                        if (tid < n) pw[tid] = p;
-                        l_t = __fmaf_rn(l_t, resc, p);
-                        __syncthreads();
-                        const __half * vt = tb + (size_t) MK_TP * T3B_HD;
-                        o0.x *= resc; o0.y *= resc; o1.x *= resc; o1.y *= resc;
-                        int j = w;
-                        for (; j + 16 < n; j += 32) {
-                            const float2 v0 = __half22float2(*(const __half2 *) (vt + (size_t) j * T3B_HD + 2 * lane));
-                            const float2 v1 = __half22float2(*(const __half2 *) (vt + (size_t) (j + 16) * T3B_HD + 2 * lane));
-                            const float p0 = pw[j], p1 = pw[j + 16];
-                            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
-                            o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
-                        }
-                        if (j < n) {
-                            const float2 v0 = __half22float2(*(const __half2 *) (vt + (size_t) j * T3B_HD + 2 * lane));
-                            const float p0 = pw[j];
-                            o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
-                        }
-                        __syncthreads();   // tile buffer, pw and rf free again
-                        if (i + 2 < nt) issue_tile(i + 2, pos, kb, inB);
-                    }
-                    const float ls = warp_sum(l_t);
-                    if (lane == 0) rf[32 + w] = ls;
-                    __syncthreads();
-                    lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
+                    // L > MK_MAX_POS: K/V streamed in tiles (out of line)
+                    lsum = mk_attend_tiled(&cp, OWN, pos, kb, a.v_off, qkvh, kst, vst, pw, rf, att_s + 256 + MK_MAX_POS,
+                                           mbar, &okf, a.spin, a.err, a.abort_flag);
+                    if (lsum < 0.0f) MK_BAIL;
                     MK_STAMP(l * 20 + 9);
                 }
                 {
                     float * og = att_s + 256 + MK_MAX_POS;   // [16][64]
-                    og[w * 64 + 2 * lane] = o0.x + o1.x;
-                    og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
+                    if (!tiled(pos)) {
+                        og[w * 64 + 2 * lane] = o0.x + o1.x;
+                        og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
+                    }
                     __syncthreads();
                     MK_STAMP(l * 20 + 17);
 
@@ -1513,7 +1558,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
             else
                 ok = mk_head<T3B_Q4_0>(a, step, GW, act, part, rowsum, redd, xres, LLX, hstage ? (const unsigned char *) kst : nullptr,
                                        &mbar[2], (unsigned) step & 1u);
-            if (ok) hd_out = -1;
+            if (ok) CP_DONE(2);
             if (!ok) MK_BAIL;
         }
         // OWN: layer 0 of the next step (K rows up to this step's position)

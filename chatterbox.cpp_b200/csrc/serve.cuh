@@ -45,6 +45,8 @@ struct ServeState {
     bool dirty = true;              // active list changed since the last upload
     int * tok_pin = nullptr;        // pinned copy of the step's sampled tokens
     int tok_cap = 0;
+    long long step_tokens = 0;      // tokens sampled by batched steps since the slots were allocated
+    double step_ms = 0.0;           // device time of those steps
 };
 
 ServeState * serve_create() { return new ServeState(); }
@@ -197,6 +199,8 @@ int t3b_serve_run(t3b_ctx * ctx, int max_iters, int32_t * n_active, int32_t * n_
         float ms = 0.0f;
         cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1);
         total_ms += ms;
+        S.step_ms += ms;
+        S.step_tokens += n;
         rc = check_dev_err(ctx);
         if (rc != T3B_OK) return rc;
         for (int i = 0; i < n; ++i) {
@@ -233,6 +237,13 @@ int t3b_serve_result(t3b_ctx * ctx, int id, int32_t * tokens_out, int cap, int32
     if (n_out) *n_out = n;
     if (cap > 0) std::memcpy(tokens_out, q.result.data(), sizeof(int32_t) * (size_t) std::min(n, cap));
     return 1;
+}
+
+int t3b_serve_stats(const t3b_ctx * ctx, long long * step_tokens, double * step_ms) {
+    if (!ctx || !ctx->serve) return T3B_ERR_ARG;
+    if (step_tokens) *step_tokens = ctx->serve->step_tokens;
+    if (step_ms) *step_ms = ctx->serve->step_ms;
+    return T3B_OK;
 }
 
 }  // extern "C"

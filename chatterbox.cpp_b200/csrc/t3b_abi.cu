@@ -310,7 +310,7 @@ GemvEpi epi_plain(int kind, float * y, int ldy, const float * bias, const float 
 // rows of the M), written to logits_out rows y_row[...] (device array) or
 // consecutively when y_row is null.
 void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int head_first, int head_rows,
-                float * logits_out, const int * y_row, cudaStream_t st, float * htrace = nullptr) {
+                float * logits_out, const int * y_row, cudaStream_t st, float * htrace = nullptr, bool prompt = false) {
     const int D = ctx->hp.n_embd, H = ctx->hp.n_head;
     if (htrace) cudaMemcpyAsync(htrace, ctx->x, sizeof(float) * D, cudaMemcpyDeviceToDevice, st);
     for (int il = 0; il < ctx->hp.n_layer; ++il) {
@@ -330,9 +330,11 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         a.row_of = row_of; a.len = pos; a.len_add = 1; a.max_ctx = ctx->max_ctx; a.n_head = H;
         a.out = ctx->attn; a.ldo = D; a.part = ctx->part; a.cnt = ctx->cnt; a.s_max = ctx->s_max; a.err = ctx->err_word;
         // many rows: the attention kernel writes the proj GEMM's Q8_0 input itself
-        const bool q_attn = M >= T3B_ATTN_ROWS_MIN && Ly.proj.type != T3B_F16;
+        const bool q_attn = (M >= T3B_ATTN_ROWS_MIN || prompt) && Ly.proj.type != T3B_F16;
         if (q_attn) { a.qx = ctx->xq; a.qd = ctx->xd; a.qs = ctx->xs; }
-        if (M >= T3B_ATTN_ROWS_MIN) attn_rows_kernel<<<dim3(H, M), 128, 0, st>>>(a);
+        // a prompt chunk: consecutive positions of one cache row, causal
+        if (prompt) attn_prefill_kernel<<<dim3(H, (M + T3B_PF_T - 1) / T3B_PF_T), 256, T3B_PREFILL_SMEM, st>>>(a, M);
+        else if (M >= T3B_ATTN_ROWS_MIN) attn_rows_kernel<<<dim3(H, M), 128, 0, st>>>(a);
         else attn_decode_kernel<<<dim3(H, M, ctx->s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
         // proj + bias + residual
         if (!q_attn) launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
@@ -398,6 +400,8 @@ t3b_ctx * t3b_create(int device, const t3b_model_desc * desc) {
     if (fix_table(device, &ctx->fx, &ctx->err) != T3B_OK) return fail("exp table");
     if (cudaFuncSetAttribute(sampler_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T3B_SAMPLER_SMEM) != cudaSuccess)
         return fail("sampler shared memory attribute");
+    if (cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T3B_PREFILL_SMEM) != cudaSuccess)
+        return fail("prefill attention shared memory attribute");
     if (dalloc(ctx, ctx->allocs, &ctx->err_word, 1) != T3B_OK) return fail("alloc");
     cudaMemset(ctx->err_word, 0, sizeof(unsigned));
     if (cudaHostAlloc((void **) &ctx->err_pin, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess) return fail("alloc");
@@ -713,7 +717,8 @@ int t3b_prefill(t3b_ctx * ctx, int stream, const int32_t * text, int n_text, con
             CK(cudaMemcpyAsync(ctx->pos, pos.data(), sizeof(int) * n, cudaMemcpyHostToDevice, st));
             embed_prompt_kernel<<<n, 256, 0, st>>>(ctx->semb, ctx->temb, ctx->wpe, ctx->spk, ctx->pk_kind, ctx->pk_id, c0, D, ctx->x);
             const bool last = c0 + n == P;
-            run_layers(ctx, n, ctx->row_of, ctx->pos, n - 1, last ? 1 : 0, ctx->logits + (size_t) crow * V, nullptr, st);
+            run_layers(ctx, n, ctx->row_of, ctx->pos, n - 1, last ? 1 : 0, ctx->logits + (size_t) crow * V, nullptr, st,
+                       nullptr, true);
             CK(cudaStreamSynchronize(st));   // host vectors above are reused per chunk
         }
         ctx->pos_host[crow] = P;
@@ -824,6 +829,16 @@ bool mega_eligible(t3b_ctx * ctx, int n, int max_pos_after) {
     return T == T3B_Q4_0 || T == T3B_Q8_0 || T == T3B_F16;
 }
 
+const void * mega_fn(int T, bool lng) {
+    if (lng)
+        return T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0, true>
+             : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0, true>
+                             : (const void *) t3_decode_megakernel<T3B_F16, true>;
+    return T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0, false>
+         : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0, false>
+                         : (const void *) t3_decode_megakernel<T3B_F16, false>;
+}
+
 int mega_prepare(t3b_ctx * ctx) {
     MegaState & m = ctx->mega;
     if (m.ready) return T3B_OK;
@@ -867,13 +882,13 @@ int mega_prepare(t3b_ctx * ctx) {
     CK(cudaHostGetDevicePointer(&m.cancel_dev, m.cancel_host, 0));
     m.smem = mk_smem_bytes();
     const int T = ctx->L[0].attn.type;
-    const void * fn = T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0>
-                    : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0>
-                                    : (const void *) t3_decode_megakernel<T3B_F16>;
-    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) m.smem));
-    int per_sm = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, MK_THREADS, m.smem));
-    if (per_sm < 1) { set_err(&ctx->err, "megakernel: does not fit on an SM"); return T3B_ERR_STATE; }
+    for (int lg = 0; lg < 2; ++lg) {
+        const void * fn = mega_fn(T, lg != 0);
+        CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) m.smem));
+        int per_sm = 0;
+        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, MK_THREADS, m.smem));
+        if (per_sm < 1) { set_err(&ctx->err, "megakernel: does not fit on an SM"); return T3B_ERR_STATE; }
+    }
     m.grid = G;
     m.ready = 1;
     return T3B_OK;
@@ -921,10 +936,9 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
         a.tl_step = getenv("T3B_MK_TIMELINE_STEP") ? atoi(getenv("T3B_MK_TIMELINE_STEP")) : 2;
     }
     void * args[] = {&a};
-    const int T = ctx->L[0].attn.type;
-    const void * fn = T == T3B_Q4_0 ? (const void *) t3_decode_megakernel<T3B_Q4_0>
-                    : T == T3B_Q8_0 ? (const void *) t3_decode_megakernel<T3B_Q8_0>
-                                    : (const void *) t3_decode_megakernel<T3B_F16>;
+    // positions p0 .. p0 + max_steps - 1: past MK_MAX_POS only the LONG
+    // instantiation streams K/V in tiles
+    const void * fn = mega_fn(ctx->L[0].attn.type, p0 + max_steps > MK_MAX_POS);
     CK(cudaLaunchCooperativeKernel(fn, dim3(m.grid), dim3(MK_THREADS), args, m.smem, st));
     ctx->launches += 1;
     if (steps) CK(cudaMemcpyAsync(steps, m.steps_done, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -1216,6 +1230,7 @@ namespace {
 struct OpScratch { int8_t * xq = nullptr; float * xd = nullptr; int * xs = nullptr; __half * xh = nullptr; size_t cap = 0;
                    float * part = nullptr; unsigned * cnt = nullptr; size_t pcap = 0, ccap = 0;
                    unsigned * errw = nullptr;   // device error word of the op-level attention on this device
+                   bool pf_attr = false;        // attn_prefill_kernel's shared-memory attribute set on this device
                  };
 std::mutex g_op_mu;
 std::map<int, OpScratch> g_op;
@@ -1300,6 +1315,42 @@ int t3b_op_attention(const float * q_dev, const void * k_dev, const void * v_dev
     else attn_decode_kernel<<<dim3(n_head, M, s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
+    return T3B_OK;
+}
+
+int t3b_op_attention_prompt(const float * q_dev, const void * k_dev, const void * v_dev, int M, int n_head, int max_ctx,
+                            const int32_t * pos_dev, float * out_dev, void * cuda_stream) {
+    if (!q_dev || !k_dev || !v_dev || !pos_dev || !out_dev || M <= 0 || n_head <= 0 || max_ctx <= 0) {
+        set_err(nullptr, "t3b_op_attention_prompt: bad args");
+        return T3B_ERR_ARG;
+    }
+    cudaStream_t st = (cudaStream_t) cuda_stream;
+    int dev = 0; cudaGetDevice(&dev);
+    OpScratch * sc;
+    {
+        std::lock_guard<std::mutex> lk(g_op_mu);
+        sc = &g_op[dev];
+        if (!sc->errw) {
+            if (cudaMalloc(&sc->errw, 4) != cudaSuccess) { set_err(nullptr, "t3b_op_attention_prompt: scratch allocation failed"); return T3B_ERR_OOM; }
+            if (cudaMemsetAsync(sc->errw, 0, 4, st) != cudaSuccess) { set_err(nullptr, "t3b_op_attention_prompt: memset failed"); return T3B_ERR_CUDA; }
+        }
+        if (!sc->pf_attr) {
+            if (cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T3B_PREFILL_SMEM) != cudaSuccess) {
+                set_err(nullptr, "t3b_op_attention_prompt: shared memory attribute");
+                return T3B_ERR_CUDA;
+            }
+            sc->pf_attr = true;
+        }
+    }
+    AttnArgs a{};
+    a.q = q_dev; a.ldq = n_head * T3B_HD;
+    a.kv = (const __half *) k_dev; a.row_elems = 0; a.layer_off = 0;
+    a.v_off = (size_t) ((const __half *) v_dev - (const __half *) k_dev);
+    a.row_of = nullptr; a.len = pos_dev; a.len_add = 1; a.max_ctx = max_ctx; a.n_head = n_head;
+    a.out = out_dev; a.ldo = n_head * T3B_HD; a.err = sc->errw;
+    attn_prefill_kernel<<<dim3(n_head, (M + T3B_PF_T - 1) / T3B_PF_T), 256, T3B_PREFILL_SMEM, st>>>(a, M);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_err(nullptr, "t3b_op_attention_prompt: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
     return T3B_OK;
 }
 

@@ -197,6 +197,10 @@ int t3b_serve_run(t3b_ctx * ctx, int max_iters, int32_t * n_active, int32_t * n_
  * longer than the context) finishes with that error code. */
 int t3b_serve_result(t3b_ctx * ctx, int id, int32_t * tokens_out, int cap, int32_t * n_out, int32_t * attempts);
 
+/* Tokens sampled by t3b_serve_run's batched steps since t3b_stream_alloc,
+ * and the device time of those steps (ms). */
+int t3b_serve_stats(const t3b_ctx * ctx, long long * step_tokens, double * step_ms);
+
 /* Engine::cancel() equivalent (chatterbox_engine.cpp:546-548). */
 void t3b_cancel(t3b_ctx * ctx);
 
@@ -273,6 +277,15 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
 int t3b_op_attention(const float * q_dev, const void * k_dev, const void * v_dev, int M,
                      int n_head, int max_ctx, const int32_t * len_dev, float * out_dev,
                      void * cuda_stream);
+
+/* Causal attention of a prompt chunk (ggml_flash_attn_ext with eval_prompt's
+ * causal mask, main.cpp:548-560,663-677): M query rows of ONE cache, row m
+ * at position pos[m] attending keys 0 .. pos[m]; q [M][n_head*64] f32,
+ * caches [n_head][max_ctx][64] f16 (K and V given separately), scale 1/8,
+ * out [M][n_head*64] f32.  Flash-attention tiling (64 queries x 64 keys
+ * per step).  Length errors are kept for t3b_op_check. */
+int t3b_op_attention_prompt(const float * q_dev, const void * k_dev, const void * v_dev, int M, int n_head,
+                            int max_ctx, const int32_t * pos_dev, float * out_dev, void * cuda_stream);
 
 /* The fused sampler on device buffers: cond/uncond logits [rows][V] f32
  * (uncond nullable), history [rows][hist_stride] i32 with hist_len[rows],

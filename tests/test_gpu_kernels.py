@@ -246,3 +246,32 @@ def test_attention_length_error_is_reported(pkg):
     assert L.t3b_op_check(st) == -5
     assert "length-out-of-range" in pkg.last_error()
     assert L.t3b_op_check(st) == 0
+
+
+@pytest.mark.parametrize("M,p0", [(1, 0), (37, 0), (64, 0), (150, 0), (100, 900), (300, 1748)])
+def test_prompt_attention_matches_fp64(pkg, M, p0):
+    """Causal flash attention of a prompt chunk (t3b_op_attention_prompt):
+    rows at positions p0 .. p0+M-1 of one cache, each over keys 0 .. its
+    position, against the fp64 attention (1e-5 of max |out| per head)."""
+    L = pkg.lib()
+    H, T = 16, 2048
+    rng = np.random.default_rng(M * 7 + p0)
+    q = rng.standard_normal((M, H * 64)).astype(np.float32)
+    k = (rng.standard_normal((H, T, 64)) * 0.5).astype(np.float16)
+    v = rng.standard_normal((H, T, 64)).astype(np.float16)
+    pos = (p0 + np.arange(M)).astype(np.int32)
+    kv = torch.from_numpy(np.stack([k, v])).cuda()
+    qd = torch.from_numpy(q).cuda()
+    pd = torch.from_numpy(pos).cuda()
+    od = torch.full((M, H * 64), float("nan"), dtype=torch.float32, device="cuda")
+    pkg.check(L.t3b_op_attention_prompt(_p(qd), _p(kv[0]), _p(kv[1]), M, H, T, _p(pd), _p(od), _stream()))
+    assert L.t3b_op_check(_stream()) == 0
+    out = od.cpu().numpy()
+    kf, vf = k.astype(np.float64), v.astype(np.float64)
+    for m in range(0, M, max(1, M // 12)):
+        n = int(pos[m]) + 1
+        for h in range(H):
+            s = (kf[h, :n] @ q[m, h * 64:(h + 1) * 64].astype(np.float64)) / 8.0
+            w = np.exp(s - s.max())
+            ref = (w[:, None] * vf[h, :n]).sum(0) / w.sum()
+            assert rel_err(out[m, h * 64:(h + 1) * 64], ref) < 1e-5, (m, h, n)
