@@ -487,63 +487,88 @@ def batched_cfg(pkg, torch, peak, steps=256, streams=64, seed=3):
 
 
 def batched_kernels(pkg, torch, peak, reps=50):
-    """The two kernels of the batched decode step alone, 128 rows: the Q8_0
-    fc GEMV of T3 (1024 -> 4096) through t3b_op_gemv (activation prep +
-    int8 tensor-core GEMM), and decode attention over 16 heads x 400 f16
-    positions per row through t3b_op_attention (one CTA per (row, head)).
-    CUDA events on the launching stream; the attention's K/V (268 MB)
-    exceed L2, the GEMM's weights (4.4 MB) stay in it (compute-bound)."""
+    """The batched decode step's kernels alone at 128 rows, device time per
+    call from a CUDA-graph replay of `reps` back-to-back calls (no host
+    launch overhead in the number): the fc (1024 -> 4096) and fc2 (4096 ->
+    1024) GEMMs of T3 through t3b_op_gemv (activation prep + GEMM) with Q8_0
+    weights (mma.sync int8 with the exact per-block rescale) and with F16
+    weights (tcgen05 tensor cores, TMA-fed, split-K), and decode attention
+    over 16 heads x 400 f16 positions per row through t3b_op_attention (one
+    CTA per (row, head)); the attention's K/V (268 MB) exceed L2."""
     import ctypes as C
     import gguf
     L = pkg.lib()
     s = torch.cuda.current_stream()
     sp = C.c_void_p(s.cuda_stream)
-    M, K, N = 128, 1024, 4096
-    w = (np.random.default_rng(2).standard_normal((N, K)) * 0.02).astype(np.float32)
-    q = np.ascontiguousarray(gguf.quants.quantize(w, gguf.GGMLQuantizationType.Q8_0))
-    rb = L.t3b_op_row_bytes(8, K)
-    wd = torch.empty(N * rb, dtype=torch.uint8, device="cuda")
-    pkg.check(L.t3b_op_repack(8, q.ctypes.data, N, K, C.c_void_p(wd.data_ptr())))
-    x = torch.randn(M, K, device="cuda")
-    y = torch.empty(M, N, device="cuda")
-    gemm_args = (8, C.c_void_p(wd.data_ptr()), N, K, C.c_void_p(x.data_ptr()), M, None, None, 1e-5, None, None, 0,
-                 C.c_void_p(y.data_ptr()), sp)
+    M = 128
+
+    def timed(fn, make_args):
+        for _ in range(5):
+            pkg.check(fn(*make_args(sp)))                     # warm-up (scratch allocated here)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for _ in range(reps):
+                fn(*make_args(cs))
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1000.0 / reps
+
+    res = {}
+    for ty, tname in ((8, "q8_0"), (1, "f16")):
+        for K, N in ((1024, 4096), (4096, 1024)):   # fc and fc2 of T3
+            w = (np.random.default_rng(2).standard_normal((N, K)) * 0.02).astype(np.float32)
+            if ty == 1:
+                q = np.ascontiguousarray(w.astype(np.float16))
+            else:
+                q = np.ascontiguousarray(gguf.quants.quantize(w, gguf.GGMLQuantizationType.Q8_0))
+            rb = L.t3b_op_row_bytes(ty, K)
+            wd = torch.empty(N * rb, dtype=torch.uint8, device="cuda")
+            pkg.check(L.t3b_op_repack(ty, q.ctypes.data, N, K, C.c_void_p(wd.data_ptr())))
+            x = torch.randn(M, K, device="cuda")
+            y = torch.empty(M, N, device="cuda")
+
+            def args(stream, ty=ty, wd=wd, N=N, K=K, x=x, y=y):
+                return (ty, C.c_void_p(wd.data_ptr()), N, K, C.c_void_p(x.data_ptr()), M, None, None, 1e-5, None, None,
+                        0, C.c_void_p(y.data_ptr()), stream)
+            us = timed(L.t3b_op_gemv, args)
+            wbytes = N * rb
+            res[f"gemm_{tname}_m128_{'fc' if N > K else 'fc2'}"] = {
+                "shape": f"M={M} K={K} N={N}", "us_per_call": us, "tops": 2.0 * M * N * K / (us * 1e-6) / 1e12,
+                "weight_gbs": wbytes / (us * 1e-6) / 1e9,
+                "kernel": "prep_act + " + ("gemm_f16_tc_kernel (tcgen05)" if ty == 1 else "gemm_q_mma_kernel")}
+            del wd
     H, T, Lk = 16, 512, 400
     kv = torch.randn(2, M, H, T, 64, device="cuda").half()
     qa = torch.randn(M, H * 64, device="cuda")
     ln = torch.full((M,), Lk, dtype=torch.int32, device="cuda")
     out = torch.empty(M, H * 64, device="cuda")
-    attn_args = (C.c_void_p(qa.data_ptr()), C.c_void_p(kv[0].data_ptr()), C.c_void_p(kv[1].data_ptr()), M, H, T,
-                 C.c_void_p(ln.data_ptr()), C.c_void_p(out.data_ptr()), sp)
 
-    def timed(fn, args):
-        for _ in range(5):
-            pkg.check(fn(*args))
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        for _ in range(reps):
-            pkg.check(fn(*args))
-        e1.record(s)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) * 1000.0 / reps
-
-    g_us = timed(L.t3b_op_gemv, gemm_args)
+    def attn_args(stream):
+        return (C.c_void_p(qa.data_ptr()), C.c_void_p(kv[0].data_ptr()), C.c_void_p(kv[1].data_ptr()), M, H, T,
+                C.c_void_p(ln.data_ptr()), C.c_void_p(out.data_ptr()), stream)
     a_us = timed(L.t3b_op_attention, attn_args)
     a_bytes = M * H * Lk * 64 * 2 * 2 + M * H * 64 * 8
-    return {"gemm_q8_0_m128": {"shape": f"M={M} K={K} N={N}", "us_per_call": g_us,
-                               "int8_tops": 2.0 * M * N * K / (g_us * 1e-6) / 1e12,
-                               "note": "t3b_op_gemv = prep_act + gemm_q_mma_kernel"},
-            "attn_rows_m128": {"shape": f"M={M} heads={H} L={Lk}", "us_per_call": a_us, "bytes": a_bytes,
-                               "achieved_gbs": a_bytes / (a_us * 1e-6) / 1e9, "peak": peak,
-                               "frac": a_bytes / (a_us * 1e-6) / 1e9 / peak}}
+    res["attn_rows_m128"] = {"shape": f"M={M} heads={H} L={Lk}", "us_per_call": a_us, "bytes": a_bytes,
+                             "achieved_gbs": a_bytes / (a_us * 1e-6) / 1e9, "peak": peak,
+                             "frac": a_bytes / (a_us * 1e-6) / 1e9 / peak}
+    return res
 
 
 def gemv_sweep(pkg, torch, peak, reps=20):
     """the four T3 layer shapes x {Q4_0, Q8_0, F16} x
     M in {1, 2, 8, 32, 128} through t3b_op_gemv (activation prep + GEMV for
-    M < 16, int8 tensor-core GEMM for M >= 16).  Device time per call (CUDA
-    events, weights cycled over enough copies to exceed L2), algorithmic
-    bytes N*K*{0.5625, 1.0625, 2} + M*K*4 + M*N*4."""
+    M < 16; M >= 16: int8 mma.sync (Q4_0/Q8_0) or tcgen05 (F16) GEMM).
+    Device time per call: `reps` calls on weights cycled over enough copies
+    to exceed L2 are captured into a CUDA graph and replayed, so host launch
+    overhead is not in the number.  Algorithmic bytes
+    N*K*{0.5625, 1.0625, 2} + M*K*4 + M*N*4."""
     import ctypes as C
     import gguf
     L = pkg.lib()
@@ -567,24 +592,33 @@ def gemv_sweep(pkg, torch, peak, reps=20):
                 x = torch.randn(M, K, device="cuda")
                 y = torch.empty(M, N, device="cuda")
 
-                def call(i):
-                    pkg.check(L.t3b_op_gemv(ty, C.c_void_p(wd[i % copies].data_ptr()), N, K, C.c_void_p(x.data_ptr()),
-                                            M, None, None, 1e-5, None, None, 0, C.c_void_p(y.data_ptr()), sp))
+                def call(i, stream):
+                    return L.t3b_op_gemv(ty, C.c_void_p(wd[i % copies].data_ptr()), N, K, C.c_void_p(x.data_ptr()),
+                                         M, None, None, 1e-5, None, None, 0, C.c_void_p(y.data_ptr()), stream)
                 for i in range(3):
-                    call(i)
+                    pkg.check(call(i, sp))
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    for i in range(reps):
+                        call(i, cs)
+                g.replay()
+                torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(s)
-                for i in range(reps):
-                    call(i)
+                g.replay()
                 e1.record(s)
                 torch.cuda.synchronize()
                 us = e0.elapsed_time(e1) * 1000.0 / reps
                 byts = N * rb + M * K * 4 + M * N * 4
                 out.append([name, K, N, M, round(us, 2), round(byts / (us * 1e-6) / 1e9, 1),
                             round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)])
+                del g
             del wd
     return {"columns": ["type", "K", "N", "M", "us_per_call", "GB/s", "TOP/s"], "rows": out, "peak": peak,
-            "note": "t3b_op_gemv: activation prep (LN off) + GEMV (M < 16) or int8 tensor-core GEMM (M >= 16)"}
+            "note": "t3b_op_gemv: activation prep (LN off) + GEMV (M < 16); M >= 16: int8 mma.sync GEMM (Q4_0/Q8_0), "
+                    "tcgen05 GEMM (F16); device time per call from CUDA-graph replay"}
 
 
 def phase_timeline(pkg, step=5):

@@ -14,6 +14,7 @@
 #include "common.cuh"
 #include "t3_expf.h"
 #include "../../include/t3b200.h"
+#include <cuda.h>   // CUtensorMap (TMA descriptors)
 
 // ---------------------------------------------------------------------------
 // GEMV epilogue
@@ -477,6 +478,208 @@ __global__ __launch_bounds__(256) void gemv_f16_kernel(
             if (lane == 0 && r < N && m < mt) epi_store(e, m0 + m, r, v);
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// F16-weight GEMM on the 5th-generation tensor cores (tcgen05), M >= 16
+// activation rows (batched decode, prefill): Y = W . xh with f16 weights and
+// f16-rounded activations (ggml's F16 mul_mat arithmetic: every f16 x f16
+// product is exact in f32), f32 accumulation in tensor memory.
+//
+// * Operands reach shared memory by TMA (cp.async.bulk.tensor, 2-D tensor
+//   maps, no multicast) in the canonical K-major layout with the 128-byte
+//   swizzle: one box of 64 halves x R rows per operand and stage, rows of
+//   128 bytes, 8-row atoms of 1024 bytes whose 16-byte chunks the TMA unit
+//   permutes by row (chunk ^ row % 8) and the MMA unit reads back the same
+//   way.  The MMA for K columns 16 j .. 16 j + 15 starts 32 j bytes into the
+//   atom.
+// * A 4-stage ring with full/empty mbarriers: one thread issues the TMA
+//   loads, waits for a stage, issues its four K = 16 MMAs (M = 128,
+//   N = TF_BN) and commits them to the stage's empty barrier; a slot is
+//   refilled once the MMAs that read it have completed.
+// * Split-K over gridDim.z when the tiles alone do not fill the GPU: each
+//   CTA writes its partial tile to a workspace and the last CTA of a tile
+//   (completion counter) adds the partials in split order, so the result is
+//   the same for every run.  The epilogue (bias / GELU / residual / K-V
+//   append) runs once per output element.
+// grid = (ceil(N / TF_BN), ceil(M / 128), splits), 128 threads: after the
+// MMAs, thread t reads row t's accumulators with tcgen05.ld.
+// ---------------------------------------------------------------------------
+#define TF_BM 128
+#define TF_BN 64
+#define TF_BK 64                             // K elements per stage
+#define TF_NS 4                              // stages in the ring
+#define TF_A_STAGE (TF_BM * TF_BK * 2)       // 16 KB
+#define TF_B_STAGE (TF_BN * TF_BK * 2)       // 8 KB
+#define TF_SMEM (TF_NS * (TF_A_STAGE + TF_B_STAGE) + 256 + 1024)   // + alignment of the ring to 1024 bytes
+#define TF_SPIN (1u << 22)
+
+struct TfArgs {
+    int M, N, K;
+    int kchunk;           // K elements per split (a multiple of TF_BK)
+    int splits;
+    GemvEpi e;
+    float * ws;           // splits > 1: [splits][M][N] partial tiles
+    unsigned * cnt;       // splits > 1: per-tile completion counters (zero; reset by the last CTA)
+};
+
+// UMMA shared-memory descriptor, K-major, 128-byte swizzle (sm_100 version
+// 1): 8-row groups 1024 bytes apart (SBO), leading offset unused (1)
+__device__ __forceinline__ unsigned long long tf_desc(unsigned saddr) {
+    return (unsigned long long) ((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((unsigned long long) (1024u >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+// instruction descriptor: kind::f16, A = B = f16, D = f32, both K-major, M = 128, N = TF_BN
+#define TF_IDESC ((1u << 4) | ((unsigned) (TF_BN >> 3) << 17) | ((unsigned) (TF_BM >> 4) << 24))
+
+__device__ __forceinline__ bool tf_wait(unsigned addr, unsigned parity) {
+    for (unsigned spins = 0;; ++spins) {
+        unsigned done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return true;
+        if (spins >= TF_SPIN) return false;
+        __nanosleep(32);
+    }
+}
+__device__ __forceinline__ void tf_tma(unsigned dst, const void * tmap, int x, int y, unsigned mbar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"(tmap), "r"(x), "r"(y), "r"(mbar) : "memory");
+}
+
+__global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap ta,
+                                                             const __grid_constant__ CUtensorMap tb, TfArgs p) {
+    extern __shared__ __align__(1024) unsigned char tf_raw[];
+    // swizzle atoms need 1024-byte aligned stage buffers
+    unsigned char * tf_sm = tf_raw + ((1024u - ((unsigned) __cvta_generic_to_shared(tf_raw) & 1023u)) & 1023u);
+    unsigned char * As = tf_sm;                                   // [TF_NS][TF_A_STAGE]
+    unsigned char * Bs = tf_sm + TF_NS * TF_A_STAGE;              // [TF_NS][TF_B_STAGE]
+    unsigned long long * full = (unsigned long long *) (Bs + TF_NS * TF_B_STAGE);
+    unsigned long long * empty = full + TF_NS;
+    unsigned long long * done = empty + TF_NS;
+    unsigned * tslot = (unsigned *) (done + 1);
+    __shared__ int tf_ok, tf_last;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * TF_BM, n0 = blockIdx.x * TF_BN, split = blockIdx.z;
+    const int kbeg = split * p.kchunk, nk = p.kchunk / TF_BK;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"((unsigned) __cvta_generic_to_shared(tslot)), "r"((unsigned) TF_BN) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int i = 0; i < 2 * TF_NS + 1; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((unsigned) __cvta_generic_to_shared(full + i)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        tf_ok = 1;
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tbase = *tslot;
+
+    // lane 0 of warp 0 drives the loads and MMAs; the rest of its warp waits
+    // at __syncwarp (a spin of theirs would share the warp's issue with it)
+    if (tid == 0) {
+        const unsigned a0 = (unsigned) __cvta_generic_to_shared(As), b0 = (unsigned) __cvta_generic_to_shared(Bs);
+        // stage i: the A box (64 halves x 128 rows) and the B box (64 x
+        // TF_BN) of K columns kbeg + 64 i ..
+        auto load = [&](int i) {
+            const int sl = i % TF_NS, k = kbeg + i * TF_BK;
+            const unsigned fb = (unsigned) __cvta_generic_to_shared(full + sl);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb),
+                         "r"((unsigned) (TF_A_STAGE + TF_B_STAGE)) : "memory");
+            tf_tma(a0 + sl * TF_A_STAGE, &ta, k, m0, fb);
+            tf_tma(b0 + sl * TF_B_STAGE, &tb, k, n0, fb);
+        };
+        for (int i = 0; i < TF_NS && i < nk; ++i) load(i);
+        bool ok = true;
+        for (int i = 0; i < nk && ok; ++i) {
+            const int sl = i % TF_NS;
+            ok = tf_wait((unsigned) __cvta_generic_to_shared(full + sl), (unsigned) (i / TF_NS) & 1u);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+            for (int j = 0; j < TF_BK / 16; ++j) {   // MMA j: K columns 16 j .. 16 j + 15, 32 j bytes into each row
+                const unsigned long long da = tf_desc(a0 + sl * TF_A_STAGE + 32 * j);
+                const unsigned long long db = tf_desc(b0 + sl * TF_B_STAGE + 32 * j);
+                const unsigned acc = (i > 0 || j > 0) ? 1u : 0u;
+                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+                             ::"r"(tbase), "l"(da), "l"(db), "r"((unsigned) TF_IDESC), "r"(acc) : "memory");
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"((unsigned) __cvta_generic_to_shared(empty + sl)) : "memory");
+            // refill the slot of stage i - 1 once its MMAs are done
+            if (i >= 1 && i - 1 + TF_NS < nk) {
+                const int ps = (i - 1) % TF_NS;
+                ok = tf_wait((unsigned) __cvta_generic_to_shared(empty + ps), (unsigned) ((i - 1) / TF_NS) & 1u);
+                if (ok) load(i - 1 + TF_NS);
+            }
+        }
+        if (!ok) { tf_ok = 0; if (p.e.err) atomicOr(p.e.err, T3B_DEVERR_TIMEOUT); }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     ::"r"((unsigned) __cvta_generic_to_shared(done)) : "memory");
+    }
+    if (warp == 0) __syncwarp();
+    // every MMA of this CTA complete (a commit tracks all earlier MMAs)
+    if (!tf_wait((unsigned) __cvta_generic_to_shared(done), 0u)) tf_ok = 0;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    float v[TF_BN];
+#pragma unroll
+    for (int c = 0; c < TF_BN / 32; ++c) {
+        unsigned r[32];
+        const unsigned ta_ = tbase + ((unsigned) (warp * 32) << 16) + (unsigned) (c * 32);
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                     "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                       "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                       "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                       "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                     : "r"(ta_) : "memory");
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[c * 32 + j] = __uint_as_float(r[j]);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"((unsigned) TF_BN) : "memory");
+    }
+    const int m = m0 + tid;
+    const bool mrow = m < p.M && tf_ok;
+    if (p.splits > 1) {
+        if (mrow) {
+            float * w = p.ws + ((size_t) split * p.M + m) * p.N + n0;
+#pragma unroll
+            for (int j = 0; j < TF_BN; ++j)
+                if (n0 + j < p.N) w[j] = v[j];
+        }
+        __threadfence();
+        __syncthreads();
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        if (tid == 0) tf_last = atomicAdd(&p.cnt[tile], 1u) == (unsigned) (p.splits - 1);
+        __syncthreads();
+        if (!tf_last) return;
+        __threadfence();
+        if (mrow) {
+#pragma unroll
+            for (int j = 0; j < TF_BN; ++j) {
+                if (n0 + j >= p.N) continue;
+                float t = 0.0f;
+                for (int sp = 0; sp < p.splits; ++sp) t += __ldcg(p.ws + ((size_t) sp * p.M + m) * p.N + n0 + j);
+                v[j] = t;
+            }
+        }
+        if (tid == 0) p.cnt[tile] = 0u;
+    }
+    if (!mrow) return;
+#pragma unroll
+    for (int j = 0; j < TF_BN; ++j)
+        if (n0 + j < p.N) epi_store(p.e, m, n0 + j, v[j]);
 }
 
 // Plain f32 matvec for the speaker projection (cond_spkr: K = 256).

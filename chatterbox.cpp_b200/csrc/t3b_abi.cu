@@ -8,6 +8,7 @@
 // device), so the host issues one launch per step.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>   // PFN_cuTensorMapEncodeTiled
 
 #include <algorithm>
 #include <cmath>
@@ -133,6 +134,11 @@ struct Layer {
     Mat attn, proj, fc, fc2;
 };
 
+// Split-K workspace of the tensor-core F16 GEMM: partial tiles and per-tile
+// completion counters (zero at allocation; the kernel leaves them zero)
+struct GemmWs { float * ws = nullptr; size_t cap = 0; unsigned * cnt = nullptr; int ccap = 0; };
+#define TF_CNT 4096
+
 struct StepGraph {
     cudaGraph_t g = nullptr;
     cudaGraphExec_t ge = nullptr;
@@ -199,6 +205,7 @@ struct t3b_ctx {
     float * trace = nullptr; int trace_cap = 0;
     // continuous batching over the stream slots (t3b_serve_*)
     ServeState * serve = nullptr;
+    GemmWs gws;                     // split-K workspace of the tensor-core F16 GEMM
 };
 
 #undef ERRP
@@ -243,7 +250,7 @@ void free_streams(t3b_ctx * ctx) {
     ctx->maps_slots.clear();
     for (void * p : ctx->sallocs) cudaFree(p);
     ctx->sallocs.clear();
-    ctx->S = 0; ctx->R = 0; ctx->kv = nullptr;
+    ctx->S = 0; ctx->R = 0; ctx->kv = nullptr; ctx->gws = GemmWs();
     mega_free(ctx->mega);
     serve_destroy(ctx->serve);
     ctx->serve = nullptr;
@@ -287,11 +294,77 @@ void launch_gemv_q(const Mat & W, const int8_t * xq, const float * xd, const int
     else if (M <= 4) launch_gemv_q_t<WT, 4>(W, xq, xd, xs, M, e, st);
     else launch_gemv_q_t<WT, 8>(W, xq, xd, xs, M, e, st);
 }
+// activation rows from which the F16 GEMMs run on the tensor cores
+#define TC_MIN_M 16
+
+// cuTensorMapEncodeTiled from the driver, resolved once; the attribute for
+// gemm_f16_tc_kernel's dynamic shared memory set once per device
+PFN_cuTensorMapEncodeTiled_v12000 tf_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void * f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000) f;
+    });
+    return fn;
+}
+bool tf_attr_ready() {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(gemm_f16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TF_SMEM) != cudaSuccess)
+            return false;
+        done[dev] = true;
+    }
+    return true;
+}
+// 2-D f16 tensor [rows][K] (row stride K halves), boxes of 64 halves (128
+// bytes) x box_rows written with the 128-byte swizzle the MMA descriptors use
+bool tf_map(CUtensorMap * map, const void * base, int K, int rows, int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tf_encode();
+    if (!enc || ((uintptr_t) base & 15) || (K * 2) % 16) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t) K, (cuuint64_t) rows};
+    const cuuint64_t strides[1] = {(cuuint64_t) K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t) TF_BK, (cuuint32_t) box_rows};
+    const cuuint32_t es[2] = {1u, 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// F16 weights x f16 activations on the tensor cores (M >= TC_MIN_M rows).
+// Split-K (deterministic) when the output tiles alone leave SMs idle.
+// Returns false when the shape or the environment does not allow it.
+bool launch_gemm_f16_tc(const Mat & W, const __half * xh, int M, const GemvEpi & e, const GemmWs * gw, cudaStream_t st) {
+    if (M < TC_MIN_M || !xh || W.K % TF_BK != 0 || !tf_attr_ready()) return false;
+    CUtensorMap ta, tb;
+    if (!tf_map(&ta, xh, W.K, M, TF_BM) || !tf_map(&tb, W.p, W.K, W.N, TF_BN)) return false;
+    const int tx = (W.N + TF_BN - 1) / TF_BN, ty = (M + TF_BM - 1) / TF_BM, tiles = tx * ty;
+    const int nkb = W.K / TF_BK;
+    int splits = 1;
+    if (gw && gw->ws && gw->cnt && tiles <= gw->ccap && tiles < 120) {
+        splits = std::min(std::max(1, 148 / tiles), 8);
+        while (splits > 1 && (nkb % splits != 0 || (size_t) splits * M * W.N > gw->cap)) --splits;
+    }
+    TfArgs p{};
+    p.M = M; p.N = W.N; p.K = W.K; p.kchunk = W.K / splits; p.splits = splits; p.e = e;
+    p.ws = splits > 1 ? gw->ws : nullptr; p.cnt = splits > 1 ? gw->cnt : nullptr;
+    gemm_f16_tc_kernel<<<dim3(tx, ty, splits), 128, TF_SMEM, st>>>(ta, tb, p);
+    return true;
+}
+
 void launch_gemv(const Mat & W, const int8_t * xq, const float * xd, const int * xs, const __half * xh, int M,
-                 const GemvEpi & e, cudaStream_t st) {
+                 const GemvEpi & e, cudaStream_t st, const GemmWs * gw = nullptr) {
     if (W.type == T3B_Q4_0) launch_gemv_q<T3B_Q4_0>(W, xq, xd, xs, M, e, st);
     else if (W.type == T3B_Q8_0) launch_gemv_q<T3B_Q8_0>(W, xq, xd, xs, M, e, st);
     else {
+        if (launch_gemm_f16_tc(W, xh, M, e, gw, st)) return;
         if (M <= 1) launch_gemv_h_t<1>(W, xh, M, e, st);
         else if (M <= 2) launch_gemv_h_t<2>(W, xh, M, e, st);
         else launch_gemv_h_t<4>(W, xh, M, e, st);   // 4 x K=4096 halves = 32 KB smem
@@ -322,7 +395,7 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         e.layer_off = (size_t) il * 2 * H * ctx->max_ctx * T3B_HD;
         e.v_off = (size_t) H * ctx->max_ctx * T3B_HD;
         e.row_of = row_of; e.pos = pos; e.max_ctx = ctx->max_ctx; e.D = D; e.err = ctx->err_word;
-        launch_gemv(Ly.attn, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, e, st);
+        launch_gemv(Ly.attn, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, e, st, &ctx->gws);
         // attention
         AttnArgs a{};
         a.q = ctx->qkv; a.ldq = 3 * D;
@@ -338,7 +411,7 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         else attn_decode_kernel<<<dim3(H, M, ctx->s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
         // proj + bias + residual
         if (!q_attn) launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
-        launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_RESID, ctx->x, D, Ly.proj_b, ctx->x, D), st);
+        launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_RESID, ctx->x, D, Ly.proj_b, ctx->x, D), st, &ctx->gws);
         // LN2 + fc + GELU; with the tensor-core GEMM (M >= 16) its epilogue
         // writes fc2's Q8_0 input (separate buffers: fc is still reading xq)
         launch_prep(ctx, ctx->x, D, M, D, Ly.ln2g, Ly.ln2b, Ly.fc.type, st);
@@ -346,11 +419,11 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         const bool q_fc = M >= 16 && Ly.fc.type != T3B_F16 && Ly.fc2.type != T3B_F16 &&
                           Ly.fc.K % (32 * GQ_KB) == 0 && (4 * D) % GQ_BN == 0;
         if (q_fc) { ef.qx = ctx->xq2; ef.qd = ctx->xd2; ef.qs = ctx->xs2; ef.qK = 4 * D; }
-        launch_gemv(Ly.fc, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ef, st);
+        launch_gemv(Ly.fc, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ef, st, &ctx->gws);
         // fc2 + bias + residual
         if (!q_fc) launch_prep(ctx, ctx->h, 4 * D, M, 4 * D, nullptr, nullptr, Ly.fc2.type, st);
         launch_gemv(Ly.fc2, q_fc ? ctx->xq2 : ctx->xq, q_fc ? ctx->xd2 : ctx->xd, q_fc ? ctx->xs2 : ctx->xs, ctx->xh, M,
-                    epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D), st);
+                    epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D), st, &ctx->gws);
         if (htrace)
             cudaMemcpyAsync(htrace + (size_t) (il + 1) * D, ctx->x, sizeof(float) * D, cudaMemcpyDeviceToDevice, st);
     }
@@ -358,7 +431,7 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         launch_prep(ctx, ctx->x + (size_t) head_first * D, D, head_rows, D, ctx->lnf_g, ctx->lnf_b, ctx->head.type, st);
         GemvEpi e = epi_plain(EPI_BIAS, logits_out, ctx->hp.n_speech_vocab, ctx->head_b, nullptr, 0);
         e.y_row = y_row;
-        launch_gemv(ctx->head, ctx->xq, ctx->xd, ctx->xs, ctx->xh, head_rows, e, st);
+        launch_gemv(ctx->head, ctx->xq, ctx->xd, ctx->xs, ctx->xh, head_rows, e, st, &ctx->gws);
     }
 }
 
@@ -602,9 +675,13 @@ int t3b_stream_alloc(t3b_ctx * ctx, int n_streams, int max_ctx, int cfg) {
     A(&ctx->xq2, (size_t) R * 4 * D); A(&ctx->xd2, (size_t) R * 4 * D / 32); A(&ctx->xs2, (size_t) R * 4 * D / 32);
     A(&ctx->part, (size_t) R * H * ctx->s_max * (T3B_HD + 2)); A(&ctx->cnt, (size_t) R * H);
     A(&ctx->row_slot, R); A(&ctx->pos, R); A(&ctx->row_of, R); A(&ctx->y_row, R);
+    ctx->gws.cap = (size_t) R * 4 * D * 4;   // four splits of an R x 4096 output
+    A(&ctx->gws.ws, ctx->gws.cap); A(&ctx->gws.cnt, TF_CNT);
+    ctx->gws.ccap = TF_CNT;
     A(&ctx->pk_kind, R); A(&ctx->pk_id, R);
     if (rc != T3B_OK) { free_streams(ctx); return rc; }
     CK(cudaMemsetAsync(ctx->cnt, 0, sizeof(unsigned) * R * H, ctx->st));
+    CK(cudaMemsetAsync(ctx->gws.cnt, 0, sizeof(unsigned) * TF_CNT, ctx->st));
     CK(cudaMemsetAsync(ctx->hist_len, 0, sizeof(int) * n_streams, ctx->st));
     CK(cudaMemsetAsync(ctx->done, 0, sizeof(int) * n_streams, ctx->st));
     CK(cudaMemsetAsync(ctx->step_tok, 0, sizeof(int) * n_streams, ctx->st));
@@ -1230,6 +1307,7 @@ namespace {
 struct OpScratch { int8_t * xq = nullptr; float * xd = nullptr; int * xs = nullptr; __half * xh = nullptr; size_t cap = 0;
                    float * part = nullptr; unsigned * cnt = nullptr; size_t pcap = 0, ccap = 0;
                    unsigned * errw = nullptr;   // device error word of the op-level attention on this device
+                   GemmWs gws;                  // split-K workspace of the tensor-core F16 GEMM
                    bool pf_attr = false;        // attn_prefill_kernel's shared-memory attribute set on this device
                  };
 std::mutex g_op_mu;
@@ -1261,12 +1339,26 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
             }
             sc->cap = need;
         }
+        if (dtype == T3B_F16 && M >= TC_MIN_M && sc->gws.cap < (size_t) 8 * M * N) {
+            cudaFree(sc->gws.ws);
+            if (!sc->gws.cnt) {
+                if (cudaMalloc(&sc->gws.cnt, sizeof(unsigned) * TF_CNT) != cudaSuccess ||
+                    cudaMemsetAsync(sc->gws.cnt, 0, sizeof(unsigned) * TF_CNT, st) != cudaSuccess) {
+                    set_err(nullptr, "t3b_op_gemv: scratch allocation failed"); return T3B_ERR_OOM;
+                }
+                sc->gws.ccap = TF_CNT;
+            }
+            if (cudaMalloc(&sc->gws.ws, sizeof(float) * 8 * M * N) != cudaSuccess) {
+                sc->gws.ws = nullptr; sc->gws.cap = 0; set_err(nullptr, "t3b_op_gemv: scratch allocation failed"); return T3B_ERR_OOM;
+            }
+            sc->gws.cap = (size_t) 8 * M * N;
+        }
     }
     const int qmode = dtype == T3B_F16 ? 2 : 1;
     prep_act_kernel<<<M, 256, K * sizeof(float), st>>>(x_dev, K, K, ln_g, ln_b, eps, qmode, sc->xq, sc->xd, sc->xs, sc->xh);
     Mat W; W.type = dtype; W.N = N; W.K = K; W.rb = (int) row_bytes(dtype, K); W.p = (uint8_t *) w_dev;
     const int kind = epilogue == 0 ? EPI_BIAS : (epilogue == 1 ? EPI_GELU : EPI_RESID);
-    launch_gemv(W, sc->xq, sc->xd, sc->xs, sc->xh, M, epi_plain(kind, y_dev, N, bias_dev, residual_dev, N), st);
+    launch_gemv(W, sc->xq, sc->xd, sc->xs, sc->xh, M, epi_plain(kind, y_dev, N, bias_dev, residual_dev, N), st, &sc->gws);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_gemv: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
     return T3B_OK;
