@@ -219,7 +219,9 @@ def main():
             import torch
             r = batched_kernels(pkg, torch, peak)
         elif args.only in ("serve3", "serve4"):
-            r = serving(pkg, torch, peak, int(args.only[-1]), None, 1, 0, 0, steps=args.steps if args.steps != 256 else None)
+            # serve4 alone: rank 0's share of the 8-GPU configuration
+            ws_ = 8 if args.only == "serve4" else 1
+            r = serving(pkg, torch, peak, int(args.only[-1]), None, ws_, 0, 0, steps=args.steps if args.steps != 256 else None)
         elif args.only == "sweep":
             import torch
             r = gemv_sweep(pkg, torch, peak)

@@ -512,14 +512,14 @@ __global__ __launch_bounds__(256) void gemv_f16_kernel(
 #define TF_A_STAGE (TF_BM * TF_BK * 2)       // 16 KB
 #define TF_B_STAGE (TF_BN * TF_BK * 2)       // 8 KB
 #define TF_SMEM (TF_NS * (TF_A_STAGE + TF_B_STAGE) + 256 + 1024)   // + alignment of the ring to 1024 bytes
-#define TF_SPIN (1u << 22)
+#define TF_SPIN (1u << 26)   // polls before a wait gives up (well above a second of polling)
 
 struct TfArgs {
     int M, N, K;
     int kchunk;           // K elements per split (a multiple of TF_BK)
     int splits;
     GemvEpi e;
-    float * ws;           // splits > 1: [splits][M][N] partial tiles
+    float * ws;           // splits > 1: [splits][M][N rounded up to TF_BN] partial tiles
     unsigned * cnt;       // splits > 1: per-tile completion counters (zero; reset by the last CTA)
 };
 
@@ -532,14 +532,16 @@ __device__ __forceinline__ unsigned long long tf_desc(unsigned saddr) {
 // instruction descriptor: kind::f16, A = B = f16, D = f32, both K-major, M = 128, N = TF_BN
 #define TF_IDESC ((1u << 4) | ((unsigned) (TF_BN >> 3) << 17) | ((unsigned) (TF_BM >> 4) << 24))
 
-__device__ __forceinline__ bool tf_wait(unsigned addr, unsigned parity) {
+// bounded wait for phase `parity` of an mbarrier: non-blocking test_wait
+// polls (the producer polls without sleeping; waiters in other warps back off)
+__device__ __forceinline__ bool tf_wait(unsigned addr, unsigned parity, bool backoff = false) {
     for (unsigned spins = 0;; ++spins) {
         unsigned done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                      : "=r"(done) : "r"(addr), "r"(parity) : "memory");
         if (done) return true;
         if (spins >= TF_SPIN) return false;
-        __nanosleep(32);
+        if (backoff) __nanosleep(64);
     }
 }
 __device__ __forceinline__ void tf_tma(unsigned dst, const void * tmap, int x, int y, unsigned mbar) {
@@ -625,7 +627,7 @@ __global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_consta
     }
     if (warp == 0) __syncwarp();
     // every MMA of this CTA complete (a commit tracks all earlier MMAs)
-    if (!tf_wait((unsigned) __cvta_generic_to_shared(done), 0u)) tf_ok = 0;
+    if (!tf_wait((unsigned) __cvta_generic_to_shared(done), 0u, true)) tf_ok = 0;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     float v[TF_BN];
 #pragma unroll
@@ -652,11 +654,13 @@ __global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_consta
     const int m = m0 + tid;
     const bool mrow = m < p.M && tf_ok;
     if (p.splits > 1) {
+        // partial tile of this split: [split][M][ldw] with the row padded to
+        // a multiple of TF_BN columns, written and read as float4
+        const int ldw = (p.N + TF_BN - 1) / TF_BN * TF_BN;
         if (mrow) {
-            float * w = p.ws + ((size_t) split * p.M + m) * p.N + n0;
+            float4 * w = (float4 *) (p.ws + ((size_t) split * p.M + m) * ldw + n0);
 #pragma unroll
-            for (int j = 0; j < TF_BN; ++j)
-                if (n0 + j < p.N) w[j] = v[j];
+            for (int j = 0; j < TF_BN / 4; ++j) w[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
         __threadfence();
         __syncthreads();
@@ -666,12 +670,18 @@ __global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_consta
         if (!tf_last) return;
         __threadfence();
         if (mrow) {
+            // splits added in split order; every column of a split in flight at once
 #pragma unroll
-            for (int j = 0; j < TF_BN; ++j) {
-                if (n0 + j >= p.N) continue;
-                float t = 0.0f;
-                for (int sp = 0; sp < p.splits; ++sp) t += __ldcg(p.ws + ((size_t) sp * p.M + m) * p.N + n0 + j);
-                v[j] = t;
+            for (int j = 0; j < TF_BN; ++j) v[j] = 0.0f;
+            for (int sp = 0; sp < p.splits; ++sp) {
+                const float4 * w = (const float4 *) (p.ws + ((size_t) sp * p.M + m) * ldw + n0);
+                float4 t[TF_BN / 4];
+#pragma unroll
+                for (int j = 0; j < TF_BN / 4; ++j) t[j] = __ldcg(w + j);
+#pragma unroll
+                for (int j = 0; j < TF_BN / 4; ++j) {
+                    v[4 * j] += t[j].x; v[4 * j + 1] += t[j].y; v[4 * j + 2] += t[j].z; v[4 * j + 3] += t[j].w;
+                }
             }
         }
         if (tid == 0) p.cnt[tile] = 0u;

@@ -350,7 +350,8 @@ bool launch_gemm_f16_tc(const Mat & W, const __half * xh, int M, const GemvEpi &
     int splits = 1;
     if (gw && gw->ws && gw->cnt && tiles <= gw->ccap && tiles < 120) {
         splits = std::min(std::max(1, 148 / tiles), 8);
-        while (splits > 1 && (nkb % splits != 0 || (size_t) splits * M * W.N > gw->cap)) --splits;
+        const size_t ldw = (size_t) tx * TF_BN;
+        while (splits > 1 && (nkb % splits != 0 || (size_t) splits * M * ldw > gw->cap)) --splits;
     }
     TfArgs p{};
     p.M = M; p.N = W.N; p.K = W.K; p.kchunk = W.K / splits; p.splits = splits; p.e = e;
@@ -1339,7 +1340,8 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
             }
             sc->cap = need;
         }
-        if (dtype == T3B_F16 && M >= TC_MIN_M && sc->gws.cap < (size_t) 8 * M * N) {
+        const size_t wsn = (size_t) 8 * M * ((N + TF_BN - 1) / TF_BN * TF_BN);
+        if (dtype == T3B_F16 && M >= TC_MIN_M && sc->gws.cap < wsn) {
             cudaFree(sc->gws.ws);
             if (!sc->gws.cnt) {
                 if (cudaMalloc(&sc->gws.cnt, sizeof(unsigned) * TF_CNT) != cudaSuccess ||
@@ -1348,10 +1350,10 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
                 }
                 sc->gws.ccap = TF_CNT;
             }
-            if (cudaMalloc(&sc->gws.ws, sizeof(float) * 8 * M * N) != cudaSuccess) {
+            if (cudaMalloc(&sc->gws.ws, sizeof(float) * wsn) != cudaSuccess) {
                 sc->gws.ws = nullptr; sc->gws.cap = 0; set_err(nullptr, "t3b_op_gemv: scratch allocation failed"); return T3B_ERR_OOM;
             }
-            sc->gws.cap = (size_t) 8 * M * N;
+            sc->gws.cap = wsn;
         }
     }
     const int qmode = dtype == T3B_F16 ? 2 : 1;
