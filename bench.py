@@ -546,6 +546,39 @@ def batched_kernels(pkg, torch, peak, reps=50):
                 "weight_gbs": wbytes / (us * 1e-6) / 1e9,
                 "kernel": "prep_act + " + ("gemm_f16_tc_kernel (tcgen05)" if ty == 1 else "gemm_q_mma_kernel")}
             del wd
+    # batch-1 / few-row decode attention (split-key kernel, M < 8): one row
+    # over 1024 cached positions per head
+    H1, T1, L1 = 16, 1024, 1024
+    kv1 = torch.randn(2, 1, H1, T1, 64, device="cuda").half()
+    q1 = torch.randn(1, H1 * 64, device="cuda")
+    ln1 = torch.full((1,), L1, dtype=torch.int32, device="cuda")
+    o1 = torch.empty(1, H1 * 64, device="cuda")
+
+    def attn1_args(stream):
+        return (C.c_void_p(q1.data_ptr()), C.c_void_p(kv1[0].data_ptr()), C.c_void_p(kv1[1].data_ptr()), 1, H1, T1,
+                C.c_void_p(ln1.data_ptr()), C.c_void_p(o1.data_ptr()), stream)
+    a1_us = timed(L.t3b_op_attention, attn1_args)
+    a1_bytes = H1 * L1 * 64 * 2 * 2 + H1 * 64 * 8
+    res["attn_decode_m1"] = {"shape": f"M=1 heads={H1} L={L1}", "us_per_call": a1_us, "bytes": a1_bytes,
+                             "achieved_gbs": a1_bytes / (a1_us * 1e-6) / 1e9, "peak": peak,
+                             "kernel": "attn_decode_kernel (split over 128-key chunks, last CTA merges)"}
+    del kv1
+    # prompt attention (eval_prompt's causal mask) over a 2048-position prompt
+    P_, Hp = 2048, 16
+    kvp = torch.randn(2, Hp, P_, 64, device="cuda").half()
+    qp = torch.randn(P_, Hp * 64, device="cuda")
+    posp = torch.arange(P_, dtype=torch.int32, device="cuda")
+    op_ = torch.empty(P_, Hp * 64, device="cuda")
+
+    def prompt_args(stream):
+        return (C.c_void_p(qp.data_ptr()), C.c_void_p(kvp[0].data_ptr()), C.c_void_p(kvp[1].data_ptr()), P_, Hp, P_,
+                C.c_void_p(posp.data_ptr()), C.c_void_p(op_.data_ptr()), stream)
+    p_us = timed(L.t3b_op_attention_prompt, prompt_args)
+    p_flops = 4.0 * Hp * 64 * (P_ * (P_ + 1) / 2)
+    res["attn_prompt_p2048"] = {"shape": f"P={P_} heads={Hp} causal", "us_per_call": p_us,
+                                "tflops": p_flops / (p_us * 1e-6) / 1e12,
+                                "kernel": "attn_prefill_kernel (64 x 64 flash tiles, f32 on CUDA cores)"}
+    del kvp
     H, T, Lk = 16, 512, 400
     kv = torch.randn(2, M, H, T, 64, device="cuda").half()
     qa = torch.randn(M, H * 64, device="cuda")

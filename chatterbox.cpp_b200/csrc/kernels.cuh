@@ -747,7 +747,11 @@ __global__ void embed_prompt_kernel(const __half * __restrict__ semb, const __ha
 // ---------------------------------------------------------------------------
 // Decode attention over per-row f16 caches (ggml_flash_attn_ext, N query
 // rows, no mask: each row attends its own positions 0..len-1).
-// grid = (n_head, M, s_max), 128 threads, one key per thread per CTA; the
+// grid = (n_head, M, s_max), 128 threads, one key per thread per CTA for the
+// scores; for P.V the threads form 16 groups of 8 lanes, a group takes every
+// 16th key and a lane 8 of its 64 dims (one 16-byte load per key).  Each
+// thread issues its V loads before the K loads, so both reads of the chunk
+// are in flight together; the 16 group sums are added in group order.  The
 // last CTA of a (row, head) merges the split partials (m, l, o[64]).
 // ---------------------------------------------------------------------------
 struct AttnArgs {
@@ -765,10 +769,12 @@ struct AttnArgs {
 };
 
 __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a) {
+    constexpr int NG = T3B_ATTN_CHUNK / 8;          // lane groups for P.V
+    constexpr int KPG = T3B_ATTN_CHUNK / NG;        // keys per group
     __shared__ float qs[T3B_HD];
     __shared__ float ps[T3B_ATTN_CHUNK];
     __shared__ float red[32];
-    __shared__ float oacc[2][T3B_HD];
+    __shared__ __align__(16) float oacc[NG][T3B_HD];
     __shared__ int last;
     const int h = blockIdx.x, m = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
     const int L = a.len[m] + a.len_add;
@@ -778,13 +784,20 @@ __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a)
     }
     const int ns = (L + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;
     if (sp >= ns) return;
-    if (tid < T3B_HD) qs[tid] = a.q[(size_t) m * a.ldq + h * T3B_HD + tid];
-    __syncthreads();
     const int crow = a.row_of ? a.row_of[m] : m;
     const __half * kb = a.kv + (size_t) crow * a.row_elems + a.layer_off + (size_t) h * a.max_ctx * T3B_HD;
     const __half * vb = kb + a.v_off;
     const int j0 = sp * T3B_ATTN_CHUNK;
     const int nk = min(T3B_ATTN_CHUNK, L - j0);
+    const int g = tid >> 3, e = tid & 7;
+    uint4 vr[KPG];
+#pragma unroll
+    for (int i = 0; i < KPG; ++i) {
+        const int t = g + NG * i;
+        vr[i] = t < nk ? __ldg((const uint4 *) (vb + (size_t) (j0 + t) * T3B_HD + e * 8)) : make_uint4(0, 0, 0, 0);
+    }
+    if (tid < T3B_HD) qs[tid] = a.q[(size_t) m * a.ldq + h * T3B_HD + tid];
+    __syncthreads();
     float sc = -INFINITY;
     if (tid < nk) {
         const uint4 * kp = (const uint4 *) (kb + (size_t) (j0 + tid) * T3B_HD);
@@ -808,18 +821,35 @@ __global__ __launch_bounds__(T3B_ATTN_CHUNK) void attn_decode_kernel(AttnArgs a)
     const float l = block_sum(p, red);
     __syncthreads();
     {
-        const int d = tid & (T3B_HD - 1), half = tid >> 6;
-        float o = 0.0f;
-        for (int t = half; t < nk; t += 2) o = fmaf(ps[t], __half2float(vb[(size_t) (j0 + t) * T3B_HD + d]), o);
-        oacc[half][d] = o;
+        float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < KPG; ++i) {
+            const int t = g + NG * i;
+            const float pt = t < nk ? ps[t] : 0.0f;
+            const __half2 * hp = (const __half2 *) &vr[i];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(hp[k]);
+                o[2 * k] = fmaf(pt, f.x, o[2 * k]);
+                o[2 * k + 1] = fmaf(pt, f.y, o[2 * k + 1]);
+            }
+        }
+        float4 * dst = (float4 *) &oacc[g][e * 8];
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
     }
     __syncthreads();
+    float osum = 0.0f;
+    if (tid < T3B_HD) {
+#pragma unroll
+        for (int gg = 0; gg < NG; ++gg) osum += oacc[gg][tid];
+    }
     if (ns == 1) {
-        if (tid < T3B_HD) a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = (oacc[0][tid] + oacc[1][tid]) / l;
+        if (tid < T3B_HD) a.out[(size_t) m * a.ldo + h * T3B_HD + tid] = osum / l;
         return;
     }
     float * P = a.part + (((size_t) m * a.n_head + h) * a.s_max + sp) * (T3B_HD + 2);
-    if (tid < T3B_HD) P[2 + tid] = oacc[0][tid] + oacc[1][tid];
+    if (tid < T3B_HD) P[2 + tid] = osum;
     if (tid == 0) { P[0] = mx; P[1] = l; }
     __threadfence();
     __syncthreads();

@@ -1372,6 +1372,10 @@ int t3b_op_attention(const float * q_dev, const void * k_dev, const void * v_dev
         set_err(nullptr, "t3b_op_attention: bad args");
         return T3B_ERR_ARG;
     }
+    if ((((uintptr_t) k_dev) | ((uintptr_t) v_dev)) & 15) {
+        set_err(nullptr, "t3b_op_attention: K and V caches must be 16-byte aligned");
+        return T3B_ERR_ARG;
+    }
     cudaStream_t st = (cudaStream_t) cuda_stream;
     int dev = 0; cudaGetDevice(&dev);
     const int s_max = (max_ctx + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;
@@ -1416,6 +1420,10 @@ int t3b_op_attention_prompt(const float * q_dev, const void * k_dev, const void 
                             const int32_t * pos_dev, float * out_dev, void * cuda_stream) {
     if (!q_dev || !k_dev || !v_dev || !pos_dev || !out_dev || M <= 0 || n_head <= 0 || max_ctx <= 0) {
         set_err(nullptr, "t3b_op_attention_prompt: bad args");
+        return T3B_ERR_ARG;
+    }
+    if ((((uintptr_t) k_dev) | ((uintptr_t) v_dev)) & 15) {
+        set_err(nullptr, "t3b_op_attention_prompt: K and V caches must be 16-byte aligned");
         return T3B_ERR_ARG;
     }
     cudaStream_t st = (cudaStream_t) cuda_stream;
@@ -1525,6 +1533,10 @@ extern "C" int t3b_op_attention_noalloc(const float * q_dev, const void * k_dev,
                                         void * cuda_stream) {
     if (!q_dev || !k_dev || !v_dev || !len_dev || !out_dev || M <= 0 || n_head <= 0 || max_ctx <= 0) {
         set_err(nullptr, "t3b_op_attention_noalloc: bad args");
+        return T3B_ERR_ARG;
+    }
+    if ((((uintptr_t) k_dev) | ((uintptr_t) v_dev)) & 15) {
+        set_err(nullptr, "t3b_op_attention_noalloc: K and V caches must be 16-byte aligned");
         return T3B_ERR_ARG;
     }
     const long long s_max = (max_ctx + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;

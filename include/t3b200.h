@@ -273,7 +273,10 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
 
 /* Decode attention (ggml_flash_attn_ext at N=1, main.cpp:548-560) for M
  * rows: q [M][n_head*64] f32, caches [M][n_head][max_ctx][64] f16, row m
- * attends positions 0 .. len[m]-1, scale 1/8.  out [M][n_head*64] f32. */
+ * attends positions 0 .. len[m]-1, scale 1/8.  out [M][n_head*64] f32.
+ * The K and V caches are read with 16-byte loads: both pointers must be
+ * 16-byte aligned (T3B_ERR_ARG otherwise; the same holds for the prompt and
+ * allocation-free variants). */
 int t3b_op_attention(const float * q_dev, const void * k_dev, const void * v_dev, int M,
                      int n_head, int max_ctx, const int32_t * len_dev, float * out_dev,
                      void * cuda_stream);

@@ -60,6 +60,19 @@ def test_bad_descriptor_is_rejected(pkg):
     assert "null" in pkg.last_error().lower()
 
 
+@pytest.mark.parametrize("fn", ["t3b_op_attention", "t3b_op_attention_prompt", "t3b_op_attention_noalloc"])
+def test_attention_ops_reject_unaligned_caches(pkg, fn):
+    """The argument checks run before any device call: an unaligned K or V
+    pointer (never dereferenced) is refused with T3B_ERR_ARG."""
+    L = pkg.lib()
+    f = getattr(L, fn)
+    dummy = C.c_void_p(0x1000)
+    for k, v in ((0x1008, 0x2000), (0x1000, 0x2002)):
+        rc = f(dummy, C.c_void_p(k), C.c_void_p(v), 1, 16, 128, dummy, dummy, None)
+        assert rc == -1                  # T3B_ERR_ARG
+        assert "16-byte aligned" in pkg.last_error()
+
+
 def test_gguf_roundtrip_keeps_converter_layout(pkg, tmp_path):
     g = pkg.t3_gguf
     hp = dict(g.T3_TURBO, n_layer=2, n_ctx=64, n_text_vocab=300)
