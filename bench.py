@@ -677,7 +677,8 @@ def phase_timeline(pkg, step=5):
     finally:
         os.environ.pop("T3B_MK_TIMELINE", None)
         os.environ.pop("T3B_MK_TIMELINE_STEP", None)
-    tl = np.fromfile(tl_path, dtype=np.uint64).reshape(-1, 512).astype(np.int64)
+    TL, TLL, TLH = 1024, 32, 800   # stamps per CTA, per layer, first head stamp (megakernel.cuh MK_TL*)
+    tl = np.fromfile(tl_path, dtype=np.uint64).reshape(-1, TL).astype(np.int64)
     t0 = tl[tl > 0].min()
     rel = np.where(tl > 0, tl - t0, -1)
 
@@ -690,15 +691,16 @@ def phase_timeline(pkg, step=5):
     names = {0: "P1 start", 1: "P1 x ready", 12: "P1 LN done", 14: "P1 K/W staged", 15: "P1 qkv dot done",
              16: "P1 V issued", 13: "P1 K/V appended", 9: "P2 softmax", 17: "P2 PV",
              18: "P2 head out Q8_0", 19: "P2 partials", 2: "P2 release barrier", 5: "P2 released",
-             4: "P2 next K/W issued", 6: "P4 xm ready", 10: "P4 fc dot done", 3: "P5 fc2 issued",
-             7: "P5 h ready", 11: "P5 dot done", 8: "P5 released"}
+             4: "P2 next K/W issued", 6: "P4 xm ready", 10: "P4 fc dot done", 20: "P4 h stored",
+             21: "P4 done", 3: "P5 start", 7: "P5 h ready", 22: "P5 dot", 11: "P5 dot + next weights issued",
+             8: "P5 released"}
     out = {"decode_16_steps_ms": ms, "step": step}
     for l in (1, 12):
-        out[f"layer{l}"] = {nm: med(l * 20 + i) for i, nm in names.items() if med(l * 20 + i) is not None}
-    out["head"] = {"start": med(480), "weights issued": med(489), "x ready": med(487), "dot done": med(488),
-                   "released": med(481), "sampler logits ready": med(482), "sampled": med(483),
-                   "token seen": med(484)}
-    st = tl[0, 490:512]
+        out[f"layer{l}"] = {nm: med(l * TLL + i) for i, nm in names.items() if med(l * TLL + i) is not None}
+    out["head"] = {"start": med(TLH), "weights issued": med(TLH + 9), "x ready": med(TLH + 7),
+                   "dot done": med(TLH + 8), "released": med(TLH + 1), "sampler logits ready": med(TLH + 2),
+                   "sampled": med(TLH + 3), "token seen": med(TLH + 4)}
+    st = tl[0, TLH + 10:TLH + 32]
     stages = ["start", "loaded", "min-p", "top-k", "top-p gathered", "sorted", "top-p exp", "top-p psum",
               "top-p cut", "penalty", "compacted", "final exp", "final psum", "rng", "dsum", "end",
               "k:hist", "k:scan", "k:scatter", "k:sort", "p:crossing", "p:fallback"]

@@ -90,7 +90,9 @@ struct MegaArgs {
     float * htrace;                // nullable: [n_layer + 1][1024] residual stream of step 0 (embedding, each layer's output)
     SampArgs samp;
 };
-#define MK_TL 512
+#define MK_TL 1024        // timeline stamps per CTA: layer l at l * MK_TLL + i, head and sampler from MK_TLH
+#define MK_TLL 32
+#define MK_TLH 800
 
 struct MegaState {
     int ready = 0;
@@ -524,7 +526,7 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 // phase timeline (debug): stamp point `i` of the traced step
-#define MK_STAMP(i) do { if (a.tl && step == a.tl_step && tid == 0) a.tl[(size_t) cta * MK_TL + (i)] = globaltimer_ns(); } while (0)
+#define MK_STAMP(i) do { if (a.tl && step == a.tl_step && tid == 0 && (i) < MK_TL) a.tl[(size_t) cta * MK_TL + (i)] = globaltimer_ns(); } while (0)
 
 
 // Dynamic shared memory.  Q4_0 layers (the attention CTAs compute their
@@ -541,6 +543,16 @@ constexpr size_t mk_smem_bytes() {
     return (size_t) MK_ATT_BYTES + MK_SCR_BYTES + MK_KV_BYTES + (MK_QKVW_BYTES > MK_KV_BYTES ? MK_QKVW_BYTES : MK_KV_BYTES);
 }
 static_assert(mk_smem_bytes() >= 2 * MK_KV_BYTES + MK_ATT_BYTES, "K/V stage layout must fit");
+// Q4_0 workers: their fc rows (one 32-row block, K = 1024) and fc2 rows (up
+// to 8 rows of K = 4096) of two layer uses, bulk-copied into the top of
+// shared memory one layer ahead; above the sampler's arrays (CTA 0) and the
+// staged head rows
+#define MK_FW_BYTES 18432                                     // 32 x 576 = 8 x 2304 bytes
+#define MK_SMEM_TOTAL (MK_ATT_BYTES + MK_SCR_BYTES + MK_KV_BYTES + (MK_QKVW_BYTES > MK_KV_BYTES ? MK_QKVW_BYTES : MK_KV_BYTES))
+#define MK_FW_OFF (MK_SMEM_TOTAL - 4 * MK_FW_BYTES)
+static_assert(MK_SMEM_TOTAL == mk_smem_bytes(), "layout total");
+static_assert(mk_smem_bytes() - 4 * MK_FW_BYTES >= T3B_SAMPLER_SMEM, "worker weight buffers must clear the sampler");
+static_assert(mk_smem_bytes() - 4 * MK_FW_BYTES >= MK_ATT_BYTES + MK_SCR_BYTES + MK_KV_BYTES, "and the head rows");
 static_assert(4096 + 1024 + 2048 + MK_MAXI * MK_THREADS / 32 * 4 <= MK_SCR_BYTES, "GEMV scratch must fit");
 
 // cp.async of n K or V rows (64 f16 each) into shared memory
@@ -682,6 +694,57 @@ __device__ __forceinline__ void mk_rows_q4_smem(const unsigned char * wst, int r
     if (c == 0 && row < rows) out[row] = t;
 }
 
+// Row sums of Q4_0 rows staged in shared memory (row stride rb bytes, K/32
+// blocks per row) in mk_dot's order: one warp takes a 32-block portion of a
+// row (lane = block), a butterfly adds the lanes, and each row adds its
+// portions in order.  At most 32 (row, portion) pairs: two per warp.
+__device__ __forceinline__ void mk_dot_q4_smem(const unsigned char * wst, int rb, int K, int rows, const MkAct & x,
+                                               float * part, float * rowsum) {
+    const int NB = K / 32, NP = NB / 32;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int npairs = rows * NP;
+    float v[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int pp = w + u * (MK_THREADS / 32);
+        v[u] = 0.0f;
+        if (pp < npairs) {
+            const int r = pp / NP, b = (pp % NP) * 32 + lane;
+            const unsigned char * rp = wst + (size_t) r * rb;
+            const int4 x0 = *(const int4 *) (x.q + b * 32), x1 = *(const int4 *) (x.q + b * 32 + 16);
+            const uint4 qv = *(const uint4 *) (rp + b * 16);
+            const float dw = __half2float(*(const __half *) (rp + K / 2 + b * 2));
+            int si = 0;
+            si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), x0.x, si);
+            si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), x1.x, si);
+            si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), x0.y, si);
+            si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), x1.y, si);
+            si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), x0.z, si);
+            si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), x1.z, si);
+            si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), x0.w, si);
+            si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), x1.w, si);
+            si -= 8 * x.s[b];
+            v[u] = __fmul_rn(__fmul_rn((float) si, dw), x.d[b]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) v[u] += __shfl_xor_sync(0xffffffffu, v[u], o);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int pp = w + u * (MK_THREADS / 32);
+        if (lane == 0 && pp < npairs) part[pp] = v[u];
+    }
+    __syncthreads();
+    for (int r = tid; r < rows; r += MK_THREADS) {
+        float acc = 0.0f;
+        for (int p = 0; p < NP; ++p) acc = __fadd_rn(acc, part[r * NP + p]);
+        rowsum[r] = acc;
+    }
+    __syncthreads();
+}
+
 // LN_f + speech_head rows of this CTA; the head keeps its own weight type.
 // hw (Q4_0 head, Q4_0 layers): this CTA's head rows, bulk-copied into
 // shared memory during the last layer (completion: phase `hpar` of hmb);
@@ -699,7 +762,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const
     const float hb = tid < r1 - r0 ? __ldg(a.headb + r0 + tid) : 0.0f;
     const unsigned kx = (unsigned) ((step + 1) * a.n_layer);           // x hand-offs so far
     const int cta = blockIdx.x;
-    MK_STAMP(489);
+    MK_STAMP(MK_TLH + 9);
     float2 xv;
     if (tagged) {
         if (!mk_wait_x((const unsigned long long *) (a.buf + MK_B_XT), mk_xtag(a.epoch, kx), xbuf, a)) return false;
@@ -708,7 +771,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const
         if (!mk_acquire(a.cnt + MK_C_X * MK_C_STRIDE, kx * GW, a)) return false;   // GW fc2 workers per layer
         xv = __ldcg((const float2 *) (a.buf + MK_B_X) + tid);
     }
-    MK_STAMP(487);
+    MK_STAMP(MK_TLH + 7);
     mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, HT == T3B_F16);
     if (hw) {
         __shared__ int okhd;
@@ -724,7 +787,7 @@ __device__ __noinline__ bool mk_head(const MegaArgs & a, int step, int GW, const
     } else {
         mk_dot<HT>(pf, D, r0, r1, act, part, rowsum);
     }
-    MK_STAMP(488);
+    MK_STAMP(MK_TLH + 8);
     float * tr = a.trace ? a.trace + (size_t) (step + 1) * a.V : nullptr;
     float * lg = a.buf + MK_B_LOG;
     if (tid < r1 - r0) {
@@ -767,9 +830,10 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
 
 // Bulk-copy bookkeeping of a CTA, one register (every thread holds the same
 // value): per mbarrier i (0: K rows + q/k/v weights, 1: V rows / tile
-// buffer B, 2: head rows, 3: tile buffer A) bit 2i = a phase was issued
-// and not yet waited for, bit 2i+1 = that phase's parity; bits 8 and 9 =
-// the parity of the next phase of mbarriers 1 and 3.
+// buffer B, 2: head rows, 3: tile buffer A, 4 and 5: a worker's fc + fc2
+// rows of even and odd layer uses) bit 2i = a phase was issued and not yet
+// waited for, bit 2i+1 = that phase's parity; bits 12 and 13 = the parity
+// of the next phase of mbarriers 1 and 3.
 #define CP_OUT(i) ((cp >> (2 * (i))) & 1u)
 #define CP_PAR(i) ((cp >> (2 * (i) + 1)) & 1u)
 #define CP_ISSUE(i, par) (cp = (cp & ~(3u << (2 * (i)))) | ((1u | (((unsigned) (par) & 1u) << 1)) << (2 * (i))))
@@ -778,16 +842,18 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
 #define CP_ISSUE_NEXT(i, nb) do { CP_ISSUE(i, (cp >> (nb)) & 1u); cp ^= 1u << (nb); } while (0)
 
 // waits (bounded, MK_SPIN polls each) for every copy phase still in flight
+#define MK_NMBAR 6
+#define CP_PENDING 0xfffu   // bits 0..11: phases issued per mbarrier
 __device__ __noinline__ void mk_drain(unsigned long long * mbar, unsigned cp) {
 #pragma unroll 1
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < MK_NMBAR; ++i)
         if (CP_OUT(i)) mk_mbar_wait(&mbar[i], CP_PAR(i));
 }
 
 // every exit first waits (bounded) for this CTA's copies still in flight
 #define MK_BAIL do {                                                                  \
         asm volatile("cp.async.wait_all;" ::: "memory");                              \
-        if (tid == 0 && (cp & 0xffu)) mk_drain(mbar, cp);                            \
+        if (tid == 0 && (cp & CP_PENDING)) mk_drain(mbar, cp);                       \
         return;                                                                       \
     } while (0)
 
@@ -815,8 +881,8 @@ __device__ __noinline__ unsigned mk_issue_tile(unsigned cp, int i, int npos, con
             mk_bulk_g2s(dst + (size_t) MK_TP * T3B_HD, kb + v_off + (size_t) t0 * T3B_HD, rb, mb);
         }
     }
-    if (inB) CP_ISSUE_NEXT(1, 8);
-    else CP_ISSUE_NEXT(3, 9);
+    if (inB) CP_ISSUE_NEXT(1, 12);
+    else CP_ISSUE_NEXT(3, 13);
     return cp;
 }
 
@@ -981,14 +1047,14 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // Contexts longer than MK_MAX_POS (any layout): K/V tiles stream through
     // buffer A (kst; mbar[3]) and buffer B (vst; mbar[1]).
     // cp: which phases are in flight and their parities (CP_* above).
-    __shared__ __align__(8) unsigned long long mbar[4];
+    // mbar[4], mbar[5] (Q4_0 workers): fc + fc2 rows of layer uses u with
+    // u & 1 = 0 and 1; use u completes phase u >> 1.
+    __shared__ __align__(8) unsigned long long mbar[MK_NMBAR];
     __shared__ int okf;
     unsigned cp = 0u;
     if (tid == 0) {
-        mk_mbar_init(&mbar[0]);
-        mk_mbar_init(&mbar[1]);
-        mk_mbar_init(&mbar[2]);
-        mk_mbar_init(&mbar[3]);
+#pragma unroll
+        for (int i = 0; i < MK_NMBAR; ++i) mk_mbar_init(&mbar[i]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -1029,6 +1095,34 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         }
         CP_ISSUE(0, u);
     };
+    // Q4_0 workers: fc rows (block mode) and fc2 rows of each layer use go
+    // into shared memory by bulk copies issued two uses ahead, when use u - 2's
+    // dots are done, so the weights are resident when a phase starts and no
+    // weight load sits in the load queue ahead of a hand-off poll
+    const int n_uses = a.n_steps * NL;
+    const int fr0 = mk_fc_r0(wi, GW, true), fr1 = mk_fc_r0(wi + 1, GW, true);
+    const int f2r0 = mk_r0(D, wi, GW), f2r1 = mk_r0(D, wi + 1, GW);
+    const bool wstage = OWN && worker && (fr1 - fr0) * MK_QKVW_ROW <= MK_FW_BYTES &&
+                        (f2r1 - f2r0) * 4 * MK_QKVW_ROW <= MK_FW_BYTES && a.layers[0].fc.rb == MK_QKVW_ROW &&
+                        a.layers[0].fc2.rb == 4 * MK_QKVW_ROW;
+    unsigned char * const wbuf = smem + MK_FW_OFF;   // [fc | fc2] of uses u & 1 = 0, then 1
+    auto issue_w = [&](int u) {
+        const int j = u & 1;
+        if (tid == MK_THREADS - 32) {
+            const MkLayer & Lu = a.layers[u % NL];
+            const unsigned b1 = (unsigned) (fr1 - fr0) * MK_QKVW_ROW, b2 = (unsigned) (f2r1 - f2r0) * 4 * MK_QKVW_ROW;
+            mk_fence_proxy_async();   // the buffers were last read by generic loads
+            mk_mbar_expect(&mbar[4 + j], b1 + b2);
+            if (b1) mk_bulk_g2s_w(wbuf + 2 * j * MK_FW_BYTES, Lu.fc.w + (size_t) fr0 * MK_QKVW_ROW, b1, &mbar[4 + j]);
+            if (b2) mk_bulk_g2s_w(wbuf + (2 * j + 1) * MK_FW_BYTES, Lu.fc2.w + (size_t) f2r0 * 4 * MK_QKVW_ROW, b2,
+                                  &mbar[4 + j]);
+        }
+        CP_ISSUE(4 + j, (u >> 1) & 1);
+    };
+    if (wstage) {
+        issue_w(0);
+        if (n_uses > 1) issue_w(1);
+    }
     unsigned * cQKV = a.cnt + MK_C_QKV * MK_C_STRIDE, * cATT = a.cnt + MK_C_ATT * MK_C_STRIDE;
     unsigned * cXM = a.cnt + MK_C_XM * MK_C_STRIDE, * cH = a.cnt + MK_C_H * MK_C_STRIDE;
     unsigned * cX = a.cnt + MK_C_X * MK_C_STRIDE, * cLOG = a.cnt + MK_C_LOG * MK_C_STRIDE;
@@ -1094,7 +1188,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 // rows from the staged weights, then append K/V at pos
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bq = att && tid < 3 * T3B_HD ? __ldg(Ly.bqkv + (tid >> 6) * D + hh_ * T3B_HD + (tid & 63)) : 0.0f;
-                MK_STAMP(l * 20 + 0);
+                MK_STAMP(l * MK_TLL + 0);
                 float2 xv;
                 if (l > 0 && LLX) {
                     if (!mk_wait_x(bXT, mk_xtag(a.epoch, k - 1u), xres, a)) MK_BAIL;
@@ -1106,12 +1200,12 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 } else {
                     xv = *(const float2 *) (xres + 2 * tid);
                 }
-                MK_STAMP(l * 20 + 1);
+                MK_STAMP(l * MK_TLL + 1);
                 if (att) {
                     float * qkvh = att_s;   // [192]
                     const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
                     mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, false);
-                    MK_STAMP(l * 20 + 12);
+                    MK_STAMP(l * MK_TLL + 12);
                     if (tid == 0) {   // K rows and q/k/v weights of this use
                         const bool ok = mk_mbar_wait(&mbar[0], (unsigned) (k - 1u) & 1u, a.spin);
                         if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
@@ -1120,10 +1214,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     __syncthreads();
                     if (!okf) MK_BAIL;
                     CP_DONE(0);
-                    MK_STAMP(l * 20 + 14);
+                    MK_STAMP(l * MK_TLL + 14);
                     mk_qkv_own(qkvw, act, qkvh);
                     __syncthreads();
-                    MK_STAMP(l * 20 + 15);
+                    MK_STAMP(l * MK_TLL + 15);
                     const bool pk = packed(pos);
                     __half * vrow = pk ? kst + (size_t) (pos + 1) * T3B_HD : vst;
                     if (tiled(pos)) {
@@ -1137,9 +1231,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             mk_mbar_expect(&mbar[1], (unsigned) pos * T3B_HD * 2);
                             if (pos > 0) mk_bulk_g2s(vst, kb + a.v_off, (unsigned) pos * T3B_HD * 2, &mbar[1]);
                         }
-                        CP_ISSUE_NEXT(1, 8);
+                        CP_ISSUE_NEXT(1, 12);
                     }
-                    MK_STAMP(l * 20 + 16);
+                    MK_STAMP(l * MK_TLL + 16);
                     if (tid < 3 * T3B_HD) {
                         const float v = __fadd_rn(__fadd_rn(0.0f, qkvh[tid]), bq);   // mk_dot's row sum + bias
                         qkvh[tid] = v;
@@ -1151,7 +1245,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         }
                     }
                     __syncthreads();
-                    MK_STAMP(l * 20 + 13);
+                    MK_STAMP(l * MK_TLL + 13);
                 }
             } else {
                 MK_GEMV_BEGIN(Ly.qkv, D, 3 * D)
@@ -1159,7 +1253,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 else mk_l2_prefetch(Ly.o, D);
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bqkv + r0_ + tid) : 0.0f;
-                MK_STAMP(l * 20 + 0);
+                MK_STAMP(l * MK_TLL + 0);
                 // layer input: this thread's elements 2*tid, 2*tid+1 (the
                 // embedding of layer 0 is already in xres)
                 float2 xv;
@@ -1170,11 +1264,11 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 } else {
                     xv = *(const float2 *) (xres + 2 * tid);
                 }
-                MK_STAMP(l * 20 + 1);
+                MK_STAMP(l * MK_TLL + 1);
                 mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, T == T3B_F16);
-                MK_STAMP(l * 20 + 14);
+                MK_STAMP(l * MK_TLL + 14);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
-                MK_STAMP(l * 20 + 15);
+                MK_STAMP(l * MK_TLL + 15);
                 __half * kb = a.kv + (size_t) l * a.layer_stride;
                 if (tid < r1_ - r0_) {
                     const int n = r0_ + tid;
@@ -1186,9 +1280,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     }
                     bQKV[n] = v;
                 }
-                MK_STAMP(l * 20 + 16);
+                MK_STAMP(l * MK_TLL + 16);
                 mk_release(cQKV);
-                MK_STAMP(l * 20 + 2);
+                MK_STAMP(l * MK_TLL + 2);
             }
             // ---------------- P2: attention (one CTA per head) ----------------
             if (att) {
@@ -1208,18 +1302,18 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 float * qkvh = att_s;   // [192]
                 if (!OWN) {
                     const bool ok = mk_acquire(cQKV, k * G, a);
-                    MK_STAMP(l * 20 + 12);
+                    MK_STAMP(l * MK_TLL + 12);
                     if (tid < 192) qkvh[tid] = __ldcg(bQKV + (tid / 64) * D + h * 64 + (tid & 63));
                     asm volatile("cp.async.wait_all;" ::: "memory");
                     __syncthreads();
                     if (!ok) MK_BAIL;
-                    MK_STAMP(l * 20 + 3);
+                    MK_STAMP(l * MK_TLL + 3);
                     if (tid < T3B_HD && !tiled(pos)) {
                         kst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[64 + tid]);
                         vst[(size_t) pos * T3B_HD + tid] = __float2half_rn(qkvh[128 + tid]);
                     }
                     __syncthreads();
-                    MK_STAMP(l * 20 + 13);
+                    MK_STAMP(l * MK_TLL + 13);
                 }
                 const int L = pos + 1;
                 const int lane = tid & 31, w = tid >> 5;
@@ -1274,7 +1368,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         const bool ok = mk_mbar_wait(&mbar[1], CP_PAR(1), a.spin);
                         if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
                         okf = ok;
-                        MK_STAMP(l * 20 + 3);
+                        MK_STAMP(l * MK_TLL + 3);
                     }
                     __syncthreads();
                     if (vwait) {
@@ -1283,7 +1377,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     }
                     const __half * vsrc = (OWN && packed(pos)) ? kst + (size_t) (pos + 1) * T3B_HD : vst;
                     lsum = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
-                    MK_STAMP(l * 20 + 9);
+                    MK_STAMP(l * MK_TLL + 9);
                     // o[d] = sum_j p_j v_j[d]: warp w takes keys j = w (mod 16), lane l
                     // dims 2l, 2l+1; two accumulators hide the load latency
                     {
@@ -1306,7 +1400,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     lsum = mk_attend_tiled(&cp, OWN, pos, kb, a.v_off, qkvh, kst, vst, pw, rf, att_s + 256 + MK_MAX_POS,
                                            mbar, &okf, a.spin, a.err, a.abort_flag);
                     if (lsum < 0.0f) MK_BAIL;
-                    MK_STAMP(l * 20 + 9);
+                    MK_STAMP(l * MK_TLL + 9);
                 }
                 {
                     float * og = att_s + 256 + MK_MAX_POS;   // [16][64]
@@ -1315,7 +1409,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
                     }
                     __syncthreads();
-                    MK_STAMP(l * 20 + 17);
+                    MK_STAMP(l * MK_TLL + 17);
 
                     float * ho = og + 16 * 64;   // this head's 64 outputs
                     if (tid < 64) {
@@ -1350,7 +1444,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             }
                         }
                         __syncthreads();
-                        MK_STAMP(l * 20 + 18);
+                        MK_STAMP(l * MK_TLL + 18);
                         const int4 xa = *(const int4 *) hq, xb = *(const int4 *) (hq + 16);
                         const int4 xc = *(const int4 *) (hq + 32), xe = *(const int4 *) (hq + 48);
                         const float dx0 = hd[0], dx1 = hd[1];
@@ -1389,11 +1483,11 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         }
                     }
                 }
-                MK_STAMP(l * 20 + 19);
+                MK_STAMP(l * MK_TLL + 19);
                 __syncthreads();
-                MK_STAMP(l * 20 + 2);
+                MK_STAMP(l * MK_TLL + 2);
                 mk_release(cATT);
-                MK_STAMP(l * 20 + 5);
+                MK_STAMP(l * MK_TLL + 5);
                 // K and V rows are consumed (the release's barrier): stage the
                 // next layer's (use k); layer 0 of the next step is staged
                 // after the head, whose release would otherwise wait for it
@@ -1404,7 +1498,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     if (l + 1 < NL) issue_kw((int) k, l + 1, pos);
                     else issue_head(step);
                 }
-                MK_STAMP(l * 20 + 4);
+                MK_STAMP(l * MK_TLL + 4);
             }
             // ---------------- P3: proj + bias + residual (F16 weights) --------
             if (!FUSE) {
@@ -1412,7 +1506,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 mk_l2_prefetch(Ly.fc, 4 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bo + r0_ + tid) : 0.0f;
                 if (!mk_wait_vec(cATT, k * Hn, bATT, D, vec, a)) MK_BAIL;
-                MK_STAMP(l * 20 + 5);
+                MK_STAMP(l * MK_TLL + 5);
                 mk_quantize(act, D, T == T3B_F16);
                 mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
                 if (tid < r1_ - r0_) {
@@ -1430,8 +1524,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 // publishes its slice of h already in Q8_0, which is fc2's
                 // input; the F16 path publishes h as floats
                 const int r0_ = mk_fc_r0(wi, GW, FUSE), r1_ = mk_fc_r0(wi + 1, GW, FUSE);
+                const int uj = (int) (k - 1u) & 1;   // buffer pair of this use (wstage)
                 MkPref<T> pf_;
-                mk_prefetch<T>(Ly.fc, D, r0_, r1_, pf_);
+                if (!wstage) mk_prefetch<T>(Ly.fc, D, r0_, r1_, pf_);
                 if (!OWN) mk_l2_prefetch_rows(Ly.fc2, mk_r0(D, wi, GW), mk_r0(D, wi + 1, GW));
                 const MkLn lp = mk_ln_prefetch(Ly.ln2g, Ly.ln2b);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc + r0_ + tid) : 0.0f;
@@ -1456,11 +1551,21 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     x0 = xm.x; x1 = xm.y;
                 }
                 *(float2 *) (xmid + 2 * tid) = make_float2(x0, x1);   // P5's residual (read after barriers)
-                MK_STAMP(l * 20 + 6);
+                MK_STAMP(l * MK_TLL + 6);
+                if (wstage && tid == 0) {   // this use's fc + fc2 rows (issued a layer ago)
+                    const bool ok = mk_mbar_wait(&mbar[4 + uj], ((k - 1u) >> 1) & 1u, a.spin);
+                    if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                    okf = ok;
+                }
                 if (r1_ > r0_) {   // CTA-uniform
                     mk_ln_quant(x0, x1, lp, a.eps, redd, act, T == T3B_F16);
-                    mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
-                    if (OWN) MK_STAMP(l * 20 + 10);   // fc dot done
+                    if (OWN && wstage) {
+                        if (!okf) MK_BAIL;
+                        mk_dot_q4_smem(wbuf + 2 * uj * MK_FW_BYTES, MK_QKVW_ROW, D, r1_ - r0_, act, part, rowsum);
+                    } else {
+                        mk_dot<T>(pf_, D, r0_, r1_, act, part, rowsum);
+                    }
+                    if (OWN) MK_STAMP(l * MK_TLL + 10);   // fc dot done
                     if (FUSE) {
                         // warp w: GELU of block w of this CTA's rows, then
                         // Q8_0 with the arithmetic of mk_quant_block
@@ -1502,18 +1607,24 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     } else if (tid < r1_ - r0_) {
                         bH[r0_ + tid] = gelu_ggml(__fadd_rn(rowsum[tid], bias));
                     }
+                    MK_STAMP(l * MK_TLL + 20);   // h slice stored
                 }
                 if (LLX) __syncthreads();
                 else mk_release(cH);
+                MK_STAMP(l * MK_TLL + 21);
+                if (wstage) {
+                    if (!okf) MK_BAIL;
+                    CP_DONE(4 + uj);
+                }
             }
             // ---------------- P5: fc2 + bias + residual ------------------------
             if (worker) {
                 const int r0_ = mk_r0(D, wi, GW), r1_ = mk_r0(D, wi + 1, GW);
                 MkPref<T> pf_;
-                mk_prefetch<T>(Ly.fc2, 4 * D, r0_, r1_, pf_);
+                if (!wstage) mk_prefetch<T>(Ly.fc2, 4 * D, r0_, r1_, pf_);
                 if (l + 1 < NL && !OWN) mk_l2_prefetch(a.layers[l + 1].qkv, 3 * D);
                 const float bias = tid < r1_ - r0_ ? __ldg(Ly.bfc2 + r0_ + tid) : 0.0f;
-                if (OWN) MK_STAMP(l * 20 + 3);   // fc2 weights issued
+                if (OWN) MK_STAMP(l * MK_TLL + 3);   // fc2 weights issued
                 if (FUSE) {
                     // h arrives in Q8_0: 4096 quants, 128 scales, 128 sums
                     if (LLX) {
@@ -1526,15 +1637,22 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                         else act.s[tid - 384] = __ldcg(bHS + tid - 384);
                         __syncthreads();
                     }
-                    MK_STAMP(l * 20 + 7);
+                    MK_STAMP(l * MK_TLL + 7);
                 } else {
                     if (!mk_wait_vec(cH, k * GW, bH, 4 * D, vec, a)) MK_BAIL;
-                    MK_STAMP(l * 20 + 7);
+                    MK_STAMP(l * MK_TLL + 7);
                     mk_quantize(act, 4 * D, true);
                 }
-                if (!OWN) MK_STAMP(l * 20 + 10);
-                mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
-                MK_STAMP(l * 20 + 11);
+                if (!OWN) MK_STAMP(l * MK_TLL + 10);
+                if (OWN && wstage) {
+                    mk_dot_q4_smem(wbuf + (2 * ((k - 1u) & 1u) + 1) * MK_FW_BYTES, 4 * MK_QKVW_ROW, 4 * D, r1_ - r0_, act,
+                                   part, rowsum);
+                    MK_STAMP(l * MK_TLL + 22);
+                    if ((int) k + 1 < n_uses) issue_w((int) k + 1);   // use k - 1 + 2 into the buffers just read
+                } else {
+                    mk_dot<T>(pf_, 4 * D, r0_, r1_, act, part, rowsum);
+                }
+                MK_STAMP(l * MK_TLL + 11);
                 if (tid < r1_ - r0_) {
                     const int n = r0_ + tid;
                     const float xo = __fadd_rn(__fadd_rn(rowsum[tid], bias), xmid[n]);
@@ -1544,11 +1662,11 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 }
                 if (LLX) __syncthreads();
                 else mk_release(cX);
-                MK_STAMP(l * 20 + 8);
+                MK_STAMP(l * MK_TLL + 8);
             }
         }
         // ---------------- head: LN_f + speech_head ------------------------------
-        MK_STAMP(480);
+        MK_STAMP(MK_TLH + 0);
         {
             bool ok;
             if (a.head.type == T3B_F16)
@@ -1563,18 +1681,18 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         }
         // OWN: layer 0 of the next step (K rows up to this step's position)
         if (OWN && att && step + 1 < a.n_steps) issue_kw((step + 1) * NL, 0, pos + 1);
-        MK_STAMP(481);
+        MK_STAMP(MK_TLH + 1);
         if (!a.sample) MK_BAIL;   // eval_step: logits only
         // ---------------- sampler (CTA 0) and token broadcast -------------------
         if (cta == 0) {
             if (!mk_acquire(cLOG, (unsigned) (step + 1) * G, a)) MK_BAIL;
             SampArgs sa = a.samp;
             sa.cond = bLOG; sa.cond_stride = 0; sa.uncond = nullptr;   // read through L2 by the sampler
-            sa.tl = (a.tl && step == a.tl_step) ? a.tl + 490 : nullptr;
+            sa.tl = (a.tl && step == a.tl_step) ? a.tl + MK_TLH + 10 : nullptr;
             sa.mt_resident = step > 0;   // this CTA's shared copy of the mt19937 words is current
-            MK_STAMP(482);
+            MK_STAMP(MK_TLH + 2);
             const int t = sample_row_block(sa, 0, smem);
-            MK_STAMP(483);
+            MK_STAMP(MK_TLH + 3);
             if (tid == 0) {
                 const int stop = (t == a.stop_token && !a.ignore_stop) || cancelled || t < 0;
                 *bTOK = (t & 0xffff) | (stop ? 0x10000 : 0);
@@ -1584,7 +1702,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
         }
         {
             if (!mk_acquire(cTOK, (unsigned) (step + 1), a)) MK_BAIL;
-            MK_STAMP(484);
+            MK_STAMP(MK_TLH + 4);
             if (tid == 0) tokv = __ldcg(bTOK);
             __syncthreads();
             const int tv = tokv;

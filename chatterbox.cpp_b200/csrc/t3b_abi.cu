@@ -1004,7 +1004,7 @@ int mega_decode(t3b_ctx * ctx, int slot, int p0, int max_steps, int ignore_stop,
     a.epoch = m.epoch;
     CK(cudaMemsetAsync(m.cnt, 0, sizeof(unsigned) * MK_CTL_WORDS, st));
     // debug: T3B_MK_TIMELINE=<file> stamps every phase boundary of step
-    // T3B_MK_TIMELINE_STEP (default 2) per CTA and writes [G][256] u64 ns
+    // T3B_MK_TIMELINE_STEP (default 2) per CTA and writes [G][MK_TL] u64 ns
     const char * tl_file = getenv("T3B_MK_TIMELINE");
     unsigned long long * tl = nullptr;
     if (tl_file) {
