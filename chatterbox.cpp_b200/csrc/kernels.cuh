@@ -481,6 +481,260 @@ __global__ __launch_bounds__(256) void gemv_f16_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Few-row matrix-vector product in ONE launch (M < 16): the activation prep
+// of prep_act_kernel (optional LayerNorm, then Q8_0 blocks or f16 rounding,
+// the same arithmetic in the same order) runs in every CTA over its MT rows
+// in shared memory, followed by the dot of gemv_q_kernel / gemv_f16_kernel
+// (same lane order, so the result is identical to the two-launch path).
+// Before it reads the activations, each thread issues the loads of the first
+// GP_PF weight blocks (Q4_0/Q8_0: 32 elements) or chunks (F16: 8 elements) of
+// its rows, so the weight stream from HBM overlaps the prep.
+// CTA = 8 warps, warp w owns RPW consecutive rows; grid = (ceil(N /
+// (8 RPW)), ceil(M / MT)); dynamic smem = gemv_prep_smem(WT, MT, K).
+// ---------------------------------------------------------------------------
+#define GP_PF 4
+__host__ __device__ constexpr size_t gemv_prep_smem(int wt, int mt, int K) {
+    return (size_t) mt * K * 4 + (wt == T3B_F16 ? (size_t) mt * K * 2 : (size_t) mt * K + (size_t) mt * (K / 32) * 8);
+}
+
+template <int WT, int MT, int RPW>
+__global__ __launch_bounds__(256) void gemv_prep_kernel(
+        const uint8_t * __restrict__ W, int N, int K, int rb, const float * __restrict__ x, int ldx,
+        const float * __restrict__ g, const float * __restrict__ b, float eps, int M, GemvEpi e) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    constexpr int NW = 8;                                       // warps
+    constexpr int QW = WT == T3B_Q8_0 ? 2 : 1;                  // 16-byte words per prefetched unit
+    constexpr int PF = WT == T3B_F16 ? 2 * GP_PF : GP_PF;       // units prefetched per row and lane
+    __shared__ double red[MT][NW];
+    const int nb = K / 32;
+    const int nu = WT == T3B_F16 ? K / 8 : nb;                  // units per row
+    float * rows = (float *) sm;                                // [MT][K] f32
+    int8_t * sq = (int8_t *) (rows + (size_t) MT * K);          // [MT][K]  (Q4_0 / Q8_0)
+    float * sd = (float *) (sq + (size_t) MT * K);              // [MT][nb]
+    int * ss = (int *) (sd + (size_t) MT * nb);                 // [MT][nb]
+    __half * sx = (__half *) (rows + (size_t) MT * K);          // [MT][K]  (F16)
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row0 = (blockIdx.x * NW + warp) * RPW;
+
+    // (1) weight prefetch
+    uint4 pw[RPW][PF][QW];
+    float pd[RPW][PF];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+#pragma unroll
+        for (int j = 0; j < PF; ++j) {
+            const int u = lane + 32 * j, r = row0 + i;
+            pd[i][j] = 0.0f;
+            if (r < N && u < nu) {
+                const uint8_t * wr = W + (size_t) r * rb;
+                if (WT == T3B_Q4_0) {
+                    pw[i][j][0] = __ldg((const uint4 *) (wr + u * 16));
+                    pd[i][j] = __half2float(__ldg((const __half *) (wr + K / 2 + u * 2)));
+                } else if (WT == T3B_Q8_0) {
+                    pw[i][j][0] = __ldg((const uint4 *) (wr + u * 32));
+                    pw[i][j][QW - 1] = __ldg((const uint4 *) (wr + u * 32 + 16));
+                    pd[i][j] = __half2float(__ldg((const __half *) (wr + K + u * 2)));
+                } else {
+                    pw[i][j][0] = __ldg((const uint4 *) (wr + u * 16));
+                }
+            }
+        }
+
+    // (2) activation prep of rows m0 .. m0 + mt - 1 (prep_act_kernel per row)
+    for (int m = 0; m < mt; ++m) {
+        const float * xr = x + (size_t) (m0 + m) * ldx;
+        for (int i = tid; i < K; i += blockDim.x) rows[(size_t) m * K + i] = xr[i];
+    }
+    __syncthreads();
+    if (g) {
+        double s[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            s[m] = 0.0;
+            if (m < mt)
+                for (int i = tid; i < K; i += blockDim.x) s[m] += (double) rows[(size_t) m * K + i];
+        }
+        // block_sum_d for every row at once (same order per row)
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s[m] += __shfl_xor_sync(0xffffffffu, s[m], o);
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) red[m][warp] = s[m];
+        __syncthreads();
+        float mean[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            double r = lane < NW ? red[m][lane] : 0.0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+            mean[m] = (float) (r / K);
+        }
+        __syncthreads();   // red is reused
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            s[m] = 0.0;
+            if (m < mt)
+                for (int i = tid; i < K; i += blockDim.x) {
+                    const float v = __fsub_rn(rows[(size_t) m * K + i], mean[m]);
+                    s[m] += (double) __fmul_rn(v, v);
+                }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s[m] += __shfl_xor_sync(0xffffffffu, s[m], o);
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) red[m][warp] = s[m];
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            double r = lane < NW ? red[m][lane] : 0.0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+            const float var = (float) (r / K);
+            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+            if (m < mt)
+                for (int i = tid; i < K; i += blockDim.x) {
+                    const float v = __fsub_rn(rows[(size_t) m * K + i], mean[m]);
+                    rows[(size_t) m * K + i] = __fadd_rn(__fmul_rn(__fmul_rn(v, scale), g[i]), b[i]);
+                }
+        }
+        __syncthreads();
+    }
+    if (WT != T3B_F16) {
+        // Q8_0 blocks, eight lanes per block (four elements each), every
+        // group of the CTA on its own block at once: the same maximum,
+        // scale, rounding and integer sum as prep_act_kernel's warp per block.
+        // K % 256 == 0 (the launcher's condition): mt * nb is a multiple of 8,
+        // so each warp's four groups are all in or all out of an iteration
+        // and every lane takes the full-mask shuffles.
+        const int grp = tid >> 3, sub = tid & 7;
+#pragma unroll 4
+        for (int q = grp; q < mt * nb; q += 32) {
+            const int m = q / nb, blk = q % nb;
+            const float4 v = *(const float4 *) (rows + (size_t) m * K + blk * 32 + sub * 4);
+            float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            const float d = __fdiv_rn(mx, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q0 = (int) roundf(__fmul_rn(v.x, id)), q1 = (int) roundf(__fmul_rn(v.y, id));
+            const int q2 = (int) roundf(__fmul_rn(v.z, id)), q3 = (int) roundf(__fmul_rn(v.w, id));
+            *(int *) (sq + (size_t) m * K + blk * 32 + sub * 4) =
+                (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
+            int sum = q0 + q1 + q2 + q3;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            if (sub == 0) {
+                sd[m * nb + blk] = __half2float(__float2half_rn(d));
+                ss[m * nb + blk] = sum;
+            }
+        }
+    } else {
+        for (int i = tid; i < mt * K; i += blockDim.x) sx[i] = __float2half_rn(rows[i]);
+    }
+    __syncthreads();
+
+    // (3) the dot, lanes striding the units in increasing order
+    float acc[RPW][MT];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[i][m] = 0.0f;
+    auto unit = [&](int i, int u, const uint4 (&w)[QW], float dw) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m >= mt) break;
+            if (WT == T3B_Q4_0) {
+                const int * xv = (const int *) (sq + (size_t) m * K + u * 32);
+                const uint4 qv = w[0];
+                int si = 0;
+                si = __dp4a((int) (qv.x & 0x0F0F0F0Fu), xv[0], si);
+                si = __dp4a((int) ((qv.x >> 4) & 0x0F0F0F0Fu), xv[4], si);
+                si = __dp4a((int) (qv.y & 0x0F0F0F0Fu), xv[1], si);
+                si = __dp4a((int) ((qv.y >> 4) & 0x0F0F0F0Fu), xv[5], si);
+                si = __dp4a((int) (qv.z & 0x0F0F0F0Fu), xv[2], si);
+                si = __dp4a((int) ((qv.z >> 4) & 0x0F0F0F0Fu), xv[6], si);
+                si = __dp4a((int) (qv.w & 0x0F0F0F0Fu), xv[3], si);
+                si = __dp4a((int) ((qv.w >> 4) & 0x0F0F0F0Fu), xv[7], si);
+                si -= 8 * ss[m * nb + u];
+                acc[i][m] = __fadd_rn(acc[i][m], __fmul_rn(__fmul_rn((float) si, dw), sd[m * nb + u]));
+            } else if (WT == T3B_Q8_0) {
+                const int * xv = (const int *) (sq + (size_t) m * K + u * 32);
+                const uint4 q0 = w[0], q1 = w[QW - 1];
+                int si = 0;
+                si = __dp4a((int) q0.x, xv[0], si);
+                si = __dp4a((int) q0.y, xv[1], si);
+                si = __dp4a((int) q0.z, xv[2], si);
+                si = __dp4a((int) q0.w, xv[3], si);
+                si = __dp4a((int) q1.x, xv[4], si);
+                si = __dp4a((int) q1.y, xv[5], si);
+                si = __dp4a((int) q1.z, xv[6], si);
+                si = __dp4a((int) q1.w, xv[7], si);
+                acc[i][m] = __fadd_rn(acc[i][m], __fmul_rn(__fmul_rn((float) si, dw), sd[m * nb + u]));
+            } else {
+                const __half2 * wp = (const __half2 *) &w[0];
+                const uint4 xw = *(const uint4 *) (sx + (size_t) m * K + u * 8);
+                const __half2 * xp = (const __half2 *) &xw;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 wf = __half22float2(wp[j]), xf = __half22float2(xp[j]);
+                    acc[i][m] = fmaf(wf.x, xf.x, acc[i][m]);
+                    acc[i][m] = fmaf(wf.y, xf.y, acc[i][m]);
+                }
+            }
+        }
+    };
+    // units lane + 32 j: the prefetched ones, then the rest from global memory
+    // (for each unit all rows, as in the two-launch kernels)
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+        const int u = lane + 32 * j;
+        if (u >= nu) break;
+#pragma unroll
+        for (int i = 0; i < RPW; ++i)
+            if (row0 + i < N) unit(i, u, pw[i][j], pd[i][j]);
+    }
+    for (int u = lane + 32 * PF; u < nu; u += 32) {
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            const int r = row0 + i;
+            if (r >= N) continue;
+            const uint8_t * wr = W + (size_t) r * rb;
+            uint4 w[QW];
+            float dw = 0.0f;
+            if (WT == T3B_Q4_0) {
+                w[0] = __ldg((const uint4 *) (wr + u * 16));
+                dw = __half2float(__ldg((const __half *) (wr + K / 2 + u * 2)));
+            } else if (WT == T3B_Q8_0) {
+                w[0] = __ldg((const uint4 *) (wr + u * 32));
+                w[QW - 1] = __ldg((const uint4 *) (wr + u * 32 + 16));
+                dw = __half2float(__ldg((const __half *) (wr + K + u * 2)));
+            } else {
+                w[0] = __ldg((const uint4 *) (wr + u * 16));
+            }
+            unit(i, u, w, dw);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int r = row0 + i;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float v = warp_sum(acc[i][m]);
+            if (lane == 0 && r < N && m < mt) epi_store(e, m0 + m, r, v);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // F16-weight GEMM on the 5th-generation tensor cores (tcgen05), M >= 16
 // activation rows (batched decode, prefill): Y = W . xh with f16 weights and
 // f16-rounded activations (ggml's F16 mul_mat arithmetic: every f16 x f16
@@ -1494,6 +1748,188 @@ __device__ __forceinline__ int samp_dbin(float v, float smin, float scale) {
     return SAMP_NBIN - 1 - b;
 }
 
+// The two 32-bit draws of the row's generator (block-wide: the mt19937
+// state is loaded and twisted by every thread).  The stream advances by two
+// words / one Philox counter, as in the reference's discrete_distribution.
+__device__ __forceinline__ void samp_rng_bits(const SampArgs & a, int slot, int rmode, uint32_t * mtx, uint32_t & x1,
+                                              uint32_t & x2) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    if (rmode == T3B_RNG_MT19937) {
+        uint32_t * st = a.mt + (size_t) slot * 625;
+        if (!a.mt_resident) {        // else mtx still holds this slot's state
+            for (int i = tid; i < 625; i += nth) mtx[i] = st[i];
+            __syncthreads();
+        }
+        int idx = (int) mtx[624];
+        bool tw = false;
+        if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
+        x1 = mt_temper(mtx[idx]); ++idx;
+        if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
+        x2 = mt_temper(mtx[idx]); ++idx;
+        __syncthreads();          // every thread has read the index word
+        if (tw) for (int i = tid; i < 624; i += nth) st[i] = mtx[i];
+        if (tid == 0) { st[624] = (uint32_t) idx; mtx[624] = (uint32_t) idx; }
+    } else {
+        const unsigned long long sd = a.ph_seed[slot];
+        const unsigned long long ct = a.ph_ctr[slot];
+        uint32_t c4[4] = {(uint32_t) ct, (uint32_t) (ct >> 32), (uint32_t) slot, 0u};
+        philox4x32_10(c4, (uint32_t) sd, (uint32_t) (sd >> 32));
+        x1 = c4[0]; x2 = c4[1];
+        __syncthreads();
+        if (tid == 0) a.ph_ctr[slot] = ct + 1ull;
+    }
+}
+
+// std::generate_canonical<double, 53> of two 32-bit draws
+__device__ __forceinline__ double samp_canonical(uint32_t x1, uint32_t x2) {
+    double sum = (double) x1;
+    sum += (double) x2 * 4294967296.0;
+    double u = sum / 18446744073709551616.0;
+    if (u >= 1.0) u = nextafter(1.0, 0.0);
+    return u;
+}
+
+// Ascending bitonic sort of one 64-bit key per lane.
+__device__ __forceinline__ unsigned long long warp_sort_u64(unsigned long long k) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, stride);
+            const bool keep_min = ((lane & size) == 0) == ((lane & stride) == 0);
+            k = keep_min ? (o < k ? o : k) : (o > k ? o : k);
+        }
+    return k;
+}
+
+// The row's outputs: token, next-step token, history append, stop flag.
+__device__ __forceinline__ int samp_finish(const SampArgs & a, int r, int slot, int hl, int tok) {
+    if (threadIdx.x == 0) {
+        if (a.tok_out) a.tok_out[r] = tok;
+        if (a.step_tok) a.step_tok[slot] = tok;
+        if (a.hist_append && a.hist && a.hist_len) {
+            if (hl < a.hist_stride) {
+                a.hist[(size_t) slot * a.hist_stride + hl] = tok;
+                a.hist_len[slot] = hl + 1;
+            }
+        }
+        if (a.done && tok == a.stop_token) a.done[slot] = 1;
+    }
+    __syncthreads();
+    return tok;
+}
+
+// Steps (2)-(5) of the row when at most 32 scores are finite (after min-p),
+// by one warp: lane j holds survivor j, lists are sorted with shuffles, and
+// each sequential float chain of the reference (top-p sum and running sum,
+// softmax sum) is walked in the reference's order by every lane over
+// shuffled operands.  sml: the finite scores' indices (any order); seen:
+// history bit set.  Writes the n survivors in index order to lst and their
+// probabilities to pr (0 for the ones dropped on the way); returns false
+// when every probability is 0 (the reference returns token 0 undrawn).
+__device__ bool samp_small_probs(const t3b_sample_params & P, int V, const float * s, const int * sml, int n,
+                                 const unsigned * seen, const ExpFix & fx, const unsigned long long * e2tab,
+                                 int * lst, float * pr) {
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int idx = (int) (warp_sort_u64(lane < n ? (unsigned long long) (unsigned) sml[lane] : ~0ull) & 0xffffffffu);
+    bool alive = lane < n;
+    float v = alive ? s[idx] : -INFINITY;
+    // (2) top-k: with n <= k the reference's threshold is -inf (no change);
+    // else the score at descending rank k, nudged by 1e-10f when fewer than
+    // k scores are above it, and every score <= it dropped
+    if (P.top_k > 0 && P.top_k < V && n > P.top_k) {
+        const unsigned long long kd = warp_sort_u64(alive ? ((unsigned long long) desc_key(v) << 32) | (unsigned) idx : ~0ull);
+        const float thr = desc_key_inv((uint32_t) (__shfl_sync(FULL, kd, P.top_k) >> 32));
+        const int above = __popc(__ballot_sync(FULL, alive && v > thr));
+        const float thr2 = above < P.top_k ? __fsub_rn(thr, 1e-10f) : thr;
+        alive = alive && v > thr2;
+    }
+    // (3) top-p: descending score (ties by index), e = exp(s - max),
+    // psum = sequential sum, keep up to the first j whose running sum of
+    // e / psum reaches top_p
+    if (P.top_p < 1.0f) {
+        const unsigned long long kd = warp_sort_u64(alive ? ((unsigned long long) desc_key(v) << 32) | (unsigned) idx : ~0ull);
+        const int c = __popc(__ballot_sync(FULL, alive));
+        if (c > 0) {
+            const float vj = desc_key_inv((uint32_t) (kd >> 32));
+            const float mx = __shfl_sync(FULL, vj, 0);
+            const float ej = lane < c ? t3_expf_dev(__fsub_rn(vj, mx), fx, e2tab) : 0.0f;
+            float psum = 0.0f;
+            for (int j = 0; j < c; ++j) psum = __fadd_rn(psum, __shfl_sync(FULL, ej, j));
+            const float qj = __fdiv_rn(ej, psum);
+            float cum = 0.0f;
+            int cut = c;
+            for (int j = 0; j < c; ++j) {
+                cum = __fadd_rn(cum, __shfl_sync(FULL, qj, j));
+                if (cum >= P.top_p) { cut = j + 1; break; }
+            }
+            // sorted position j survives iff j < cut: find this lane's index
+            const int ij = (int) (kd & 0xffffffffu);
+            bool keep = false;
+            for (int j = 0; j < cut; ++j) {   // every lane takes every shuffle
+                const int ix = __shfl_sync(FULL, ij, j);
+                keep |= ix == idx;
+            }
+            alive = alive && keep;
+        }
+    }
+    // (4) repetition penalty on surviving history ids (each id once)
+    if (P.repeat_penalty != 1.0f && alive && ((seen[idx >> 5] >> (idx & 31)) & 1u))
+        v = v > 0.0f ? __fdiv_rn(v, P.repeat_penalty) : __fmul_rn(v, P.repeat_penalty);
+    // (5) softmax over the survivors in index order (idx ascending by lane)
+    float mx = alive ? v : -INFINITY;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    const float pe = alive ? t3_expf_dev(__fsub_rn(v, mx), fx, e2tab) : 0.0f;
+    float psum = 0.0f;
+    for (int j = 0; j < n; ++j) psum = __fadd_rn(psum, __shfl_sync(FULL, pe, j));
+    if (lane < n) {
+        lst[lane] = idx;
+        pr[lane] = psum != 0.0f ? __fdiv_rn(pe, psum) : 0.0f;
+    }
+    return psum != 0.0f;
+}
+
+// Steps (6)/(7) over the list of samp_small_probs, by one warp: the first
+// maximum in index order (temp <= 0), or discrete_distribution's draw:
+// dsum = sequential double sum, running sum of p / dsum with the last index
+// (V - 1) forced to 1, first entry >= u.
+__device__ int samp_small_pick(const t3b_sample_params & P, int V, const int * lst, const float * pr, int n,
+                               uint32_t x1, uint32_t x2) {
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const float p = lane < n ? pr[lane] : 0.0f;
+    const int idx = lane < n ? lst[lane] : 0;
+    if (P.temp <= 0.0f) {
+        float bp = p;
+        int bl = lane < n ? lane : 32;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float op = __shfl_xor_sync(FULL, bp, o);
+            const int ol = __shfl_xor_sync(FULL, bl, o);
+            if (op > bp || (op == bp && ol < bl)) { bp = op; bl = ol; }
+        }
+        // the reference starts at index 0: with every p = 0 index 0 stays
+        const int ib = __shfl_sync(FULL, idx, bl < 32 ? bl : 0);
+        return bp > 0.0f ? ib : 0;
+    }
+    double dsum = 0.0;
+    for (int j = 0; j < n; ++j) dsum = __dadd_rn(dsum, (double) __shfl_sync(FULL, p, j));
+    const double u = samp_canonical(x1, x2);
+    if (u <= 0.0) return 0;
+    double cc = 0.0;
+    for (int j = 0; j < n; ++j) {
+        const float pj = __shfl_sync(FULL, p, j);
+        const int ix = __shfl_sync(FULL, idx, j);
+        cc = __dadd_rn(cc, (double) pj / dsum);
+        const double ci = ix == V - 1 ? 1.0 : cc;
+        if (ci >= u) return ix;
+    }
+    return V - 1;
+}
+
 // One row of sample_next_token_ex by the whole block (any blockDim.x that
 // is a multiple of 32 and >= 256).  smraw: T3B_SAMPLER_SMEM bytes of shared
 // memory.  Returns the token (every thread), or -1 for a finished stream.
@@ -1519,11 +1955,14 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     __shared__ float shf[4];
     __shared__ uint32_t mtx[625];
     __shared__ unsigned long long e2tab[32];   // t3_expf_core's table (first use is after several barriers)
+    __shared__ int sml[32];                    // indices kept by min-p while they are at most 32
+    __shared__ int sml_n;
 
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31;
     const int slot = a.slot_of ? a.slot_of[r] : r;
     if (a.done && a.done[slot]) return -1;
     if (tid < 32) e2tab[tid] = g_t3_exp2_tab[tid];
+    if (tid == 0) sml_n = 0;
     unsigned long long * tls = (a.tl && r == 0) ? a.tl : nullptr;
 #define SAMP_STAMP(i) do { if (tls && tid == 0) { unsigned long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); tls[i] = t_; } } while (0)
     SAMP_STAMP(0);
@@ -1544,23 +1983,39 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const float inv_t = use_t ? __fdiv_rn(1.0f, P.temp) : 1.0f;
     float lmx = -INFINITY, lmn = INFINITY;
     int lfin = 0;
-    for (int i0 = 0; i0 < V; i0 += 8 * nth) {
-        float cv[8], uv[8];
+    auto take = [&](int i, float v, float uv) {
+        if (cfg) v = __fadd_rn(v, __fmul_rn(P.cfg_weight, __fsub_rn(v, uv)));
+        if (use_t) v = __fmul_rn(v, inv_t);
+        s[i] = v;
+        if (v != -INFINITY) { lmx = fmaxf(lmx, v); lmn = fminf(lmn, v); ++lfin; }
+    };
+    if (!cfg) {   // one row: sixteen loads in flight per thread (one round trip for V <= 16 nth)
+        for (int i0 = 0; i0 < V; i0 += 16 * nth) {
+            float cv[16];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int i = i0 + q * nth + tid;
-            cv[q] = i < V ? __ldcg(cond + i) : 0.0f;
-            uv[q] = (cfg && i < V) ? __ldcg(unc + i) : 0.0f;
+            for (int q = 0; q < 16; ++q) {
+                const int i = i0 + q * nth + tid;
+                cv[q] = i < V ? __ldcg(cond + i) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                const int i = i0 + q * nth + tid;
+                if (i < V) take(i, cv[q], 0.0f);
+            }
         }
+    } else {
+        for (int i0 = 0; i0 < V; i0 += 8 * nth) {
+            float cv[8], uv[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int i = i0 + q * nth + tid;
-            if (i < V) {
-                float v = cv[q];
-                if (cfg) v = __fadd_rn(v, __fmul_rn(P.cfg_weight, __fsub_rn(v, uv[q])));
-                if (use_t) v = __fmul_rn(v, inv_t);
-                s[i] = v;
-                if (v != -INFINITY) { lmx = fmaxf(lmx, v); lmn = fminf(lmn, v); ++lfin; }
+            for (int q = 0; q < 8; ++q) {
+                const int i = i0 + q * nth + tid;
+                cv[q] = i < V ? __ldcg(cond + i) : 0.0f;
+                uv[q] = i < V ? __ldcg(unc + i) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int i = i0 + q * nth + tid;
+                if (i < V) take(i, cv[q], uv[q]);
             }
         }
     }
@@ -1585,18 +2040,64 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         const double lg = log((double) P.min_p);
         const double lo = lg - 1e-5, hi = lg + 1e-5;
         int kept = 0;
-        for (int i = tid; i < V; i += nth) {
-            const float v = s[i];
-            if (v == -INFINITY) continue;
-            const float d = __fsub_rn(v, smax);
-            bool drop;
-            if (fast && (double) d <= lo) drop = true;
-            else if (fast && (double) d >= hi) drop = false;
-            else drop = t3_expf_dev(d, a.fx, e2tab) < P.min_p;
-            if (drop) s[i] = -INFINITY;
-            else ++kept;
+        for (int i0 = 0; i0 < V; i0 += nth) {   // warp-uniform trip count (the ballot below)
+            const int i = i0 + tid;
+            bool keep = false;
+            if (i < V) {
+                const float v = s[i];
+                if (v != -INFINITY) {
+                    const float d = __fsub_rn(v, smax);
+                    bool drop;
+                    if (fast && (double) d <= lo) drop = true;
+                    else if (fast && (double) d >= hi) drop = false;
+                    else drop = t3_expf_dev(d, a.fx, e2tab) < P.min_p;
+                    if (drop) s[i] = -INFINITY;
+                    else { ++kept; keep = true; }
+                }
+            }
+            // the first 32 kept indices (any order), one atomic per warp
+            const unsigned bk = __ballot_sync(0xffffffffu, keep);
+            if (bk) {
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&sml_n, __popc(bk));
+                base = __shfl_sync(0xffffffffu, base, 0) + __popc(bk & ((1u << lane) - 1u));
+                if (keep && base < 32) sml[base] = i;
+            }
         }
         nfin = block_sum_i(kept, redi);
+        if (nfin > 0 && nfin <= 32) {
+            // Few survivors: steps (2)-(7) by one warp over the list
+            SAMP_STAMP(2);
+            const int nwords = (V + 31) / 32;
+            for (int i = tid; i < nwords; i += nth) seen[i] = 0u;
+            __syncthreads();
+            if (P.repeat_penalty != 1.0f)
+                for (int j = tid; j < hl; j += nth) {
+                    const int t = hist[j];
+                    if (t >= 0 && t < V) atomicOr(&seen[t >> 5], 1u << (t & 31));
+                }
+            __syncthreads();
+            if (tid < 32) {
+                const bool ok = samp_small_probs(P, V, s, sml, nfin, seen, a.fx, e2tab, lst, e);
+                if (lane == 0) shi[7] = ok;
+            }
+            __syncthreads();
+            SAMP_STAMP(12);
+            int tok = 0;
+            if (shi[7]) {
+                uint32_t x1 = 0u, x2 = 0u;
+                if (P.temp > 0.0f) samp_rng_bits(a, slot, rmode, mtx, x1, x2);
+                SAMP_STAMP(13);
+                if (tid < 32) {
+                    const int t = samp_small_pick(P, V, lst, e, nfin, x1, x2);
+                    if (lane == 0) shi[6] = t;
+                }
+                __syncthreads();
+                tok = shi[6];
+            }
+            SAMP_STAMP(15);
+            return samp_finish(a, r, slot, hl, tok);
+        }
     }
 
     SAMP_STAMP(2);
@@ -2070,37 +2571,10 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             tok = shi[5];
         } else {
             // (7) discrete_distribution draw
-            const int mode = rmode;
             uint32_t x1, x2;
-            if (mode == T3B_RNG_MT19937) {
-                uint32_t * st = a.mt + (size_t) slot * 625;
-                if (!a.mt_resident) {        // else mtx still holds this slot's state
-                    for (int i = tid; i < 625; i += nth) mtx[i] = st[i];
-                    __syncthreads();
-                }
-                int idx = (int) mtx[624];
-                bool tw = false;
-                if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
-                x1 = mt_temper(mtx[idx]); ++idx;
-                if (idx >= 624) { mt_twist(mtx); idx = 0; tw = true; }
-                x2 = mt_temper(mtx[idx]); ++idx;
-                __syncthreads();          // every thread has read the index word
-                if (tw) for (int i = tid; i < 624; i += nth) st[i] = mtx[i];
-                if (tid == 0) { st[624] = (uint32_t) idx; mtx[624] = (uint32_t) idx; }
-            } else {
-                const unsigned long long sd = a.ph_seed[slot];
-                const unsigned long long ct = a.ph_ctr[slot];
-                uint32_t c4[4] = {(uint32_t) ct, (uint32_t) (ct >> 32), (uint32_t) slot, 0u};
-                philox4x32_10(c4, (uint32_t) sd, (uint32_t) (sd >> 32));
-                x1 = c4[0]; x2 = c4[1];
-                __syncthreads();
-                if (tid == 0) a.ph_ctr[slot] = ct + 1ull;
-            }
+            samp_rng_bits(a, slot, rmode, mtx, x1, x2);
             SAMP_STAMP(13);
-            double sum = (double) x1;
-            sum += (double) x2 * 4294967296.0;
-            double u = sum / 18446744073709551616.0;
-            if (u >= 1.0) u = nextafter(1.0, 0.0);
+            const double u = samp_canonical(x1, x2);
             // dsum = sequential double sum of the p (std::accumulate).  When
             // every nonzero p >= 2^-29 all partial sums (< 2) are exact in
             // double, so any order gives the same value.
@@ -2149,19 +2623,7 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     }
     SAMP_STAMP(15);
 #undef SAMP_STAMP
-    if (tid == 0) {
-        if (a.tok_out) a.tok_out[r] = tok;
-        if (a.step_tok) a.step_tok[slot] = tok;
-        if (a.hist_append && a.hist && a.hist_len) {
-            if (hl < a.hist_stride) {
-                a.hist[(size_t) slot * a.hist_stride + hl] = tok;
-                a.hist_len[slot] = hl + 1;
-            }
-        }
-        if (a.done && tok == a.stop_token) a.done[slot] = 1;
-    }
-    __syncthreads();
-    return tok;
+    return samp_finish(a, r, slot, hl, tok);
 }
 
 __global__ __launch_bounds__(T3B_SAMPLER_THREADS, 1) void sampler_kernel(SampArgs a) {

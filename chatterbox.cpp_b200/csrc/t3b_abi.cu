@@ -372,6 +372,52 @@ void launch_gemv(const Mat & W, const int8_t * xq, const float * xd, const int *
     }
 }
 
+// Few rows (M < 16): activation prep and GEMV in one launch
+// (gemv_prep_kernel).  Returns false when the shape does not fit it; the
+// caller then runs prep_act_kernel + launch_gemv.
+#define GP_MAX_M 16
+#define GP_SMEM_MAX (200u * 1024u)   // dynamic bytes (the static arrays and the 227 KB opt-in limit leave room)
+template <int WT, int MT>
+bool launch_gemv_prep_t(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
+                        const GemvEpi & e, cudaStream_t st) {
+    constexpr int RPW = 2;
+    const size_t smem = gemv_prep_smem(WT, MT, W.K);
+    static std::mutex mu;
+    static bool ready[64] = {false};
+    int dev = 0;
+    if (smem > GP_SMEM_MAX || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    {   // the opt-in limit (the default 48 KB counts the static arrays too)
+        std::lock_guard<std::mutex> lk(mu);
+        if (!ready[dev]) {
+            if (cudaFuncSetAttribute(gemv_prep_kernel<WT, MT, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     GP_SMEM_MAX) != cudaSuccess) {
+                cudaGetLastError();   // not sticky: the caller falls back to two launches
+                return false;
+            }
+            ready[dev] = true;
+        }
+    }
+    dim3 grid((W.N + 8 * RPW - 1) / (8 * RPW), (M + MT - 1) / MT);
+    gemv_prep_kernel<WT, MT, RPW><<<grid, 256, smem, st>>>(W.p, W.N, W.K, W.rb, x, ldx, g, b, eps, M, e);
+    return true;
+}
+template <int WT>
+bool launch_gemv_prep_w(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
+                        const GemvEpi & e, cudaStream_t st) {
+    if (M <= 1) return launch_gemv_prep_t<WT, 1>(W, x, ldx, M, g, b, eps, e, st);
+    if (M <= 2) return launch_gemv_prep_t<WT, 2>(W, x, ldx, M, g, b, eps, e, st);
+    if (M <= 4) return launch_gemv_prep_t<WT, 4>(W, x, ldx, M, g, b, eps, e, st);
+    return launch_gemv_prep_t<WT, 8>(W, x, ldx, M, g, b, eps, e, st);
+}
+bool launch_gemv_prep(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
+                      const GemvEpi & e, cudaStream_t st) {
+    if (M <= 0 || M >= GP_MAX_M || W.K % 256 || W.K > 8192) return false;   // K % 256: see the kernel's quantisation
+    if (W.type == T3B_Q4_0) return launch_gemv_prep_w<T3B_Q4_0>(W, x, ldx, M, g, b, eps, e, st);
+    if (W.type == T3B_Q8_0) return launch_gemv_prep_w<T3B_Q8_0>(W, x, ldx, M, g, b, eps, e, st);
+    if (W.type == T3B_F16) return launch_gemv_prep_w<T3B_F16>(W, x, ldx, M, g, b, eps, e, st);
+    return false;
+}
+
 GemvEpi epi_plain(int kind, float * y, int ldy, const float * bias, const float * res, int ldres) {
     GemvEpi e{};
     e.kind = kind; e.y = y; e.ldy = ldy; e.bias = bias; e.res = res; e.ldres = ldres;
@@ -386,17 +432,20 @@ GemvEpi epi_plain(int kind, float * y, int ldy, const float * bias, const float 
 void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int head_first, int head_rows,
                 float * logits_out, const int * y_row, cudaStream_t st, float * htrace = nullptr, bool prompt = false) {
     const int D = ctx->hp.n_embd, H = ctx->hp.n_head;
+    const float eps = ctx->hp.eps;
     if (htrace) cudaMemcpyAsync(htrace, ctx->x, sizeof(float) * D, cudaMemcpyDeviceToDevice, st);
     for (int il = 0; il < ctx->hp.n_layer; ++il) {
         const Layer & Ly = ctx->L[il];
-        // LN1 + QKV + K/V append
-        launch_prep(ctx, ctx->x, D, M, D, Ly.ln1g, Ly.ln1b, Ly.attn.type, st);
+        // LN1 + QKV + K/V append (few rows: one launch)
         GemvEpi e = epi_plain(EPI_QKV, ctx->qkv, 3 * D, Ly.attn_b, nullptr, 0);
         e.kv = ctx->kv; e.row_elems = ctx->row_elems;
         e.layer_off = (size_t) il * 2 * H * ctx->max_ctx * T3B_HD;
         e.v_off = (size_t) H * ctx->max_ctx * T3B_HD;
         e.row_of = row_of; e.pos = pos; e.max_ctx = ctx->max_ctx; e.D = D; e.err = ctx->err_word;
-        launch_gemv(Ly.attn, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, e, st, &ctx->gws);
+        if (!launch_gemv_prep(Ly.attn, ctx->x, D, M, Ly.ln1g, Ly.ln1b, eps, e, st)) {
+            launch_prep(ctx, ctx->x, D, M, D, Ly.ln1g, Ly.ln1b, Ly.attn.type, st);
+            launch_gemv(Ly.attn, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, e, st, &ctx->gws);
+        }
         // attention
         AttnArgs a{};
         a.q = ctx->qkv; a.ldq = 3 * D;
@@ -411,28 +460,39 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
         else if (M >= T3B_ATTN_ROWS_MIN) attn_rows_kernel<<<dim3(H, M), 128, 0, st>>>(a);
         else attn_decode_kernel<<<dim3(H, M, ctx->s_max), T3B_ATTN_CHUNK, 0, st>>>(a);
         // proj + bias + residual
-        if (!q_attn) launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
-        launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, epi_plain(EPI_RESID, ctx->x, D, Ly.proj_b, ctx->x, D), st, &ctx->gws);
+        const GemvEpi ep = epi_plain(EPI_RESID, ctx->x, D, Ly.proj_b, ctx->x, D);
+        if (q_attn || !launch_gemv_prep(Ly.proj, ctx->attn, D, M, nullptr, nullptr, eps, ep, st)) {
+            if (!q_attn) launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
+            launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ep, st, &ctx->gws);
+        }
         // LN2 + fc + GELU; with the tensor-core GEMM (M >= 16) its epilogue
         // writes fc2's Q8_0 input (separate buffers: fc is still reading xq)
-        launch_prep(ctx, ctx->x, D, M, D, Ly.ln2g, Ly.ln2b, Ly.fc.type, st);
         GemvEpi ef = epi_plain(EPI_GELU, ctx->h, 4 * D, Ly.fc_b, nullptr, 0);
         const bool q_fc = M >= 16 && Ly.fc.type != T3B_F16 && Ly.fc2.type != T3B_F16 &&
                           Ly.fc.K % (32 * GQ_KB) == 0 && (4 * D) % GQ_BN == 0;
         if (q_fc) { ef.qx = ctx->xq2; ef.qd = ctx->xd2; ef.qs = ctx->xs2; ef.qK = 4 * D; }
-        launch_gemv(Ly.fc, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ef, st, &ctx->gws);
+        if (q_fc || !launch_gemv_prep(Ly.fc, ctx->x, D, M, Ly.ln2g, Ly.ln2b, eps, ef, st)) {
+            launch_prep(ctx, ctx->x, D, M, D, Ly.ln2g, Ly.ln2b, Ly.fc.type, st);
+            launch_gemv(Ly.fc, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ef, st, &ctx->gws);
+        }
         // fc2 + bias + residual
-        if (!q_fc) launch_prep(ctx, ctx->h, 4 * D, M, 4 * D, nullptr, nullptr, Ly.fc2.type, st);
-        launch_gemv(Ly.fc2, q_fc ? ctx->xq2 : ctx->xq, q_fc ? ctx->xd2 : ctx->xd, q_fc ? ctx->xs2 : ctx->xs, ctx->xh, M,
-                    epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D), st, &ctx->gws);
+        const GemvEpi e2 = epi_plain(EPI_RESID, ctx->x, D, Ly.fc2_b, ctx->x, D);
+        if (q_fc || !launch_gemv_prep(Ly.fc2, ctx->h, 4 * D, M, nullptr, nullptr, eps, e2, st)) {
+            if (!q_fc) launch_prep(ctx, ctx->h, 4 * D, M, 4 * D, nullptr, nullptr, Ly.fc2.type, st);
+            launch_gemv(Ly.fc2, q_fc ? ctx->xq2 : ctx->xq, q_fc ? ctx->xd2 : ctx->xd, q_fc ? ctx->xs2 : ctx->xs, ctx->xh,
+                        M, e2, st, &ctx->gws);
+        }
         if (htrace)
             cudaMemcpyAsync(htrace + (size_t) (il + 1) * D, ctx->x, sizeof(float) * D, cudaMemcpyDeviceToDevice, st);
     }
     if (head_rows > 0) {
-        launch_prep(ctx, ctx->x + (size_t) head_first * D, D, head_rows, D, ctx->lnf_g, ctx->lnf_b, ctx->head.type, st);
         GemvEpi e = epi_plain(EPI_BIAS, logits_out, ctx->hp.n_speech_vocab, ctx->head_b, nullptr, 0);
         e.y_row = y_row;
-        launch_gemv(ctx->head, ctx->xq, ctx->xd, ctx->xs, ctx->xh, head_rows, e, st, &ctx->gws);
+        const float * xh0 = ctx->x + (size_t) head_first * D;
+        if (!launch_gemv_prep(ctx->head, xh0, D, head_rows, ctx->lnf_g, ctx->lnf_b, eps, e, st)) {
+            launch_prep(ctx, xh0, D, head_rows, D, ctx->lnf_g, ctx->lnf_b, ctx->head.type, st);
+            launch_gemv(ctx->head, ctx->xq, ctx->xd, ctx->xs, ctx->xh, head_rows, e, st, &ctx->gws);
+        }
     }
 }
 
@@ -1356,11 +1416,14 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
             sc->gws.cap = wsn;
         }
     }
-    const int qmode = dtype == T3B_F16 ? 2 : 1;
-    prep_act_kernel<<<M, 256, K * sizeof(float), st>>>(x_dev, K, K, ln_g, ln_b, eps, qmode, sc->xq, sc->xd, sc->xs, sc->xh);
     Mat W; W.type = dtype; W.N = N; W.K = K; W.rb = (int) row_bytes(dtype, K); W.p = (uint8_t *) w_dev;
     const int kind = epilogue == 0 ? EPI_BIAS : (epilogue == 1 ? EPI_GELU : EPI_RESID);
-    launch_gemv(W, sc->xq, sc->xd, sc->xs, sc->xh, M, epi_plain(kind, y_dev, N, bias_dev, residual_dev, N), st, &sc->gws);
+    const GemvEpi ge = epi_plain(kind, y_dev, N, bias_dev, residual_dev, N);
+    if (!launch_gemv_prep(W, x_dev, K, M, ln_g, ln_b, eps, ge, st)) {   // M < 16: one launch
+        const int qmode = dtype == T3B_F16 ? 2 : 1;
+        prep_act_kernel<<<M, 256, K * sizeof(float), st>>>(x_dev, K, K, ln_g, ln_b, eps, qmode, sc->xq, sc->xd, sc->xs, sc->xh);
+        launch_gemv(W, sc->xq, sc->xd, sc->xs, sc->xh, M, ge, st, &sc->gws);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(nullptr, "t3b_op_gemv: %s", cudaGetErrorString(e)); return T3B_ERR_CUDA; }
     return T3B_OK;

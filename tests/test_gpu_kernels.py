@@ -229,6 +229,56 @@ def test_sampler_philox_matches_oracle(pkg, orc):
         assert checked > rows * 0.9
 
 
+@pytest.mark.parametrize("ties", [False, True])
+def test_sampler_few_survivors_matches_oracle(pkg, orc, ties):
+    """min-p leaves at most 32 scores: the one-warp path (top-k below the
+    survivor count, top-p cuts, penalty, greedy and drawn rows; with `ties`
+    the logits are rounded so equal scores meet the top-k threshold and the
+    top-p order): device tokens == oracle tokens."""
+    L = pkg.lib()
+    rows, V, HL = 128, 6563, 64
+    rng = np.random.default_rng(21 + ties)
+    cond = np.stack([synth_logits(900 + r, scale=3.0, kind="rounded" if ties else "normal") for r in range(rows)])
+    unc = np.zeros_like(cond)
+    hist = rng.integers(0, V, (rows, HL)).astype(np.int32)
+    hist[:, :8] = np.argsort(-cond, axis=1)[:, :8]          # the top scores are in the history
+    hlen = rng.integers(0, HL + 1, rows).astype(np.int32)
+    params = [dict(top_k=int(rng.choice([0, 1, 3, 8, 20, 1000])), top_p=float(rng.choice([0.3, 0.7, 0.95, 1.0])),
+                   temp=float(rng.choice([0.0, 0.5, 0.8, 1.0])), repeat_penalty=float(rng.choice([1.0, 1.3])),
+                   min_p=float(rng.choice([0.02, 0.05, 0.2])), cfg_weight=0.0) for _ in range(rows)]
+    seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
+    ctrs = rng.integers(0, 2 ** 40, rows, dtype=np.uint64)
+    P = (pkg.SampleParams * rows)(*[pkg.SampleParams.make(**p) for p in params])
+    pd = torch.frombuffer(bytearray(bytes(P)), dtype=torch.uint8).cuda()
+    cd, ud = torch.from_numpy(cond).cuda(), torch.from_numpy(unc).cuda()
+    hd, hld = torch.from_numpy(hist).cuda(), torch.from_numpy(hlen).cuda()
+    sd = torch.from_numpy(seeds.view(np.int64)).cuda()
+    ctd = torch.from_numpy(ctrs.view(np.int64)).cuda()
+    td = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    ctr0 = ctd.clone()
+    pkg.check(L.t3b_op_sample_philox(_p(cd), _p(ud), rows, V, _p(hd), _p(hld), HL, _p(pd), _p(sd), _p(ctd),
+                                     _p(td), _stream()))
+    torch.cuda.synchronize()
+    got = td.cpu().numpy()
+    drawn = (ctd - ctr0).cpu().numpy()
+    few = checked = 0
+    for r in range(rows):
+        x1, x2 = _philox_words(orc, int(seeds[r]), int(ctrs[r]), r)
+        t, aux = orc.sample(cond[r], params[r], x1, x2, uncond=unc[r], hist=hist[r, :hlen[r]])
+        # a row draws once, unless it is greedy or nothing survived (then
+        # the reference returns token 0 undrawn); the counter is the draw count
+        assert drawn[r] in (0, 1) and (drawn[r] == 0 or params[r]["temp"] > 0.0), r
+        if drawn[r] == 0 and params[r]["temp"] > 0.0:
+            assert t == 0 and got[r] == 0, r
+        if aux[2]:
+            continue
+        s = cond[r] / np.float32(params[r]["temp"]) if params[r]["temp"] not in (0.0, 1.0) else cond[r]
+        few += int(np.count_nonzero(np.exp(s.astype(np.float64) - s.max()) >= params[r]["min_p"]) <= 32)
+        assert got[r] == t, (r, params[r])
+        checked += 1
+    assert checked > rows * 0.8 and few > rows // 2, (checked, few)
+
+
 def test_attention_length_error_is_reported(pkg):
     """A row whose length is 0 is skipped by the kernel and reported by
     t3b_op_check as T3B_ERR_DEVICE; the word is cleared by the read."""
