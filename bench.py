@@ -598,8 +598,9 @@ def batched_kernels(pkg, torch, peak, reps=50):
 
 def gemv_sweep(pkg, torch, peak, reps=20):
     """the four T3 layer shapes x {Q4_0, Q8_0, F16} x
-    M in {1, 2, 8, 32, 128} through t3b_op_gemv (activation prep + GEMV for
-    M < 16; M >= 16: int8 mma.sync (Q4_0/Q8_0) or tcgen05 (F16) GEMM).
+    M in {1, 2, 8, 32, 128} through t3b_op_gemv (M <= 4: one launch of the
+    fused prep + GEMV kernel; 5 <= M < 16: activation prep + GEMV; M >= 16:
+    int8 mma.sync (Q4_0/Q8_0) or tcgen05 (F16) GEMM).
     Device time per call: `reps` calls on weights cycled over enough copies
     to exceed L2 are captured into a CUDA graph and replayed, so host launch
     overhead is not in the number.  Algorithmic bytes
@@ -652,8 +653,9 @@ def gemv_sweep(pkg, torch, peak, reps=20):
                 del g
             del wd
     return {"columns": ["type", "K", "N", "M", "us_per_call", "GB/s", "TOP/s"], "rows": out, "peak": peak,
-            "note": "t3b_op_gemv: activation prep (LN off) + GEMV (M < 16); M >= 16: int8 mma.sync GEMM (Q4_0/Q8_0), "
-                    "tcgen05 GEMM (F16); device time per call from CUDA-graph replay"}
+            "note": "t3b_op_gemv (LN off): M <= 4 gemv_prep_kernel (one launch); 5 <= M < 16 prep_act + GEMV; "
+                    "M >= 16 int8 mma.sync GEMM (Q4_0/Q8_0), tcgen05 GEMM (F16); device time per call from "
+                    "CUDA-graph replay"}
 
 
 def phase_timeline(pkg, step=5):
@@ -723,8 +725,9 @@ def measured_traffic():
 
 def gemv_roofline(pkg, torch, peak):
     """Average device time of the FC GEMV (1024 -> 4096, Q4_0, M = 1) through
-    t3b_op_gemv, CUDA events on the launching stream, weights > L2 by cycling
-    48 distinct weight copies (113 MB)."""
+    t3b_op_gemv (one launch of gemv_prep_kernel), weights > L2 by cycling 48
+    distinct weight copies (113 MB); 192 calls captured in a CUDA graph and
+    replayed, CUDA events on the replaying stream."""
     import ctypes as C
     import gguf
     L = pkg.lib()
@@ -738,22 +741,31 @@ def gemv_roofline(pkg, torch, peak):
     x = torch.randn(K, device="cuda")
     y = torch.empty(N, device="cuda")
     s = torch.cuda.current_stream()
-    sp = C.c_void_p(s.cuda_stream)
+
+    def call(i, stream):
+        return L.t3b_op_gemv(2, C.c_void_p(wd[i % copies].data_ptr()), N, K, C.c_void_p(x.data_ptr()), 1, None, None,
+                             1e-5, None, None, 0, C.c_void_p(y.data_ptr()), stream)
     for i in range(8):
-        pkg.check(L.t3b_op_gemv(2, C.c_void_p(wd[i].data_ptr()), N, K, C.c_void_p(x.data_ptr()), 1, None, None, 1e-5,
-                                None, None, 0, C.c_void_p(y.data_ptr()), sp))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pkg.check(call(i, C.c_void_p(s.cuda_stream)))
+    torch.cuda.synchronize()
     reps = copies * 4
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for i in range(reps):
+            call(i, cs)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
-    for i in range(reps):
-        pkg.check(L.t3b_op_gemv(2, C.c_void_p(wd[i % copies].data_ptr()), N, K, C.c_void_p(x.data_ptr()), 1, None,
-                                None, 1e-5, None, None, 0, C.c_void_p(y.data_ptr()), sp))
+    g.replay()
     e1.record(s)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / reps
+    del g
     byts = N * rb + K * 4 + N * 4
     ach = byts / (us * 1e-6) / 1e9
-    return {"kernel": "prep_act + gemv_q_kernel<Q4_0> (1024x4096, M=1)", "us_per_launch": us,
+    return {"kernel": "gemv_prep_kernel<Q4_0, 1, 2> (1024x4096, M=1, one launch)", "us_per_launch": us,
             "bytes": byts, "achieved": ach, "peak": peak, "frac": ach / peak}
 
 

@@ -481,7 +481,7 @@ __global__ __launch_bounds__(256) void gemv_f16_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Few-row matrix-vector product in ONE launch (M < 16): the activation prep
+// Few-row matrix-vector product in ONE launch (M <= 4): the activation prep
 // of prep_act_kernel (optional LayerNorm, then Q8_0 blocks or f16 rounding,
 // the same arithmetic in the same order) runs in every CTA over its MT rows
 // in shared memory, followed by the dot of gemv_q_kernel / gemv_f16_kernel

@@ -372,10 +372,10 @@ void launch_gemv(const Mat & W, const int8_t * xq, const float * xd, const int *
     }
 }
 
-// Few rows (M < 16): activation prep and GEMV in one launch
+// Few rows (M <= 4): activation prep and GEMV in one launch
 // (gemv_prep_kernel).  Returns false when the shape does not fit it; the
 // caller then runs prep_act_kernel + launch_gemv.
-#define GP_MAX_M 16
+#define GP_MAX_M 5   // from 5 rows the per-CTA prep of every row costs more than the second launch (measured)
 #define GP_SMEM_MAX (200u * 1024u)   // dynamic bytes (the static arrays and the 227 KB opt-in limit leave room)
 template <int WT, int MT>
 bool launch_gemv_prep_t(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
@@ -406,8 +406,7 @@ bool launch_gemv_prep_w(const Mat & W, const float * x, int ldx, int M, const fl
                         const GemvEpi & e, cudaStream_t st) {
     if (M <= 1) return launch_gemv_prep_t<WT, 1>(W, x, ldx, M, g, b, eps, e, st);
     if (M <= 2) return launch_gemv_prep_t<WT, 2>(W, x, ldx, M, g, b, eps, e, st);
-    if (M <= 4) return launch_gemv_prep_t<WT, 4>(W, x, ldx, M, g, b, eps, e, st);
-    return launch_gemv_prep_t<WT, 8>(W, x, ldx, M, g, b, eps, e, st);
+    return launch_gemv_prep_t<WT, 4>(W, x, ldx, M, g, b, eps, e, st);
 }
 bool launch_gemv_prep(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
                       const GemvEpi & e, cudaStream_t st) {
@@ -1419,7 +1418,7 @@ int t3b_op_gemv(int dtype, const void * w_dev, int N, int K, const float * x_dev
     Mat W; W.type = dtype; W.N = N; W.K = K; W.rb = (int) row_bytes(dtype, K); W.p = (uint8_t *) w_dev;
     const int kind = epilogue == 0 ? EPI_BIAS : (epilogue == 1 ? EPI_GELU : EPI_RESID);
     const GemvEpi ge = epi_plain(kind, y_dev, N, bias_dev, residual_dev, N);
-    if (!launch_gemv_prep(W, x_dev, K, M, ln_g, ln_b, eps, ge, st)) {   // M < 16: one launch
+    if (!launch_gemv_prep(W, x_dev, K, M, ln_g, ln_b, eps, ge, st)) {   // M <= 4: one launch
         const int qmode = dtype == T3B_F16 ? 2 : 1;
         prep_act_kernel<<<M, 256, K * sizeof(float), st>>>(x_dev, K, K, ln_g, ln_b, eps, qmode, sc->xq, sc->xd, sc->xs, sc->xh);
         launch_gemv(W, sc->xq, sc->xd, sc->xs, sc->xh, M, ge, st, &sc->gws);
