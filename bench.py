@@ -411,8 +411,9 @@ def serving(pkg, torch, peak, which, dist, ws, rank, local, quant=None, steps=No
 def sampler_microbench(pkg, torch, peak, reps=200):
     """128 rows x 6563, cond/uncond ~N(0, 3^2), CFG 0.5,
     256-token histories, penalty 1.2, temp 0.8, min_p 0.05, top_k 1000,
-    top_p 0.95, one Philox stream per row.  Device time per call (CUDA events
-    on the launching stream), median over `reps` calls."""
+    top_p 0.95, one Philox stream per row.  Device time per call: `reps`
+    calls captured in a CUDA graph and replayed (CUDA events on the replaying
+    stream; host launch cost excluded), median over 5 replays."""
     import ctypes as C
     L = pkg.lib()
     rows, V, HL = 128, 6563, 256
@@ -433,15 +434,24 @@ def sampler_microbench(pkg, torch, peak, reps=200):
             C.c_void_p(tok.data_ptr()), C.c_void_p(s.cuda_stream))
     for _ in range(5):
         pkg.check(L.t3b_op_sample_philox(*args))
-    times = []
-    for _ in range(reps):
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gargs = args[:-1] + (C.c_void_p(torch.cuda.current_stream().cuda_stream),)
+        for _ in range(reps):
+            L.t3b_op_sample_philox(*gargs)
+    g.replay()
+    torch.cuda.synchronize()
+    us = []
+    for _ in range(5):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
-        pkg.check(L.t3b_op_sample_philox(*args))
+        g.replay()
         e1.record(s)
-        times.append((e0, e1))
-    torch.cuda.synchronize()
-    us = sorted(e0.elapsed_time(e1) * 1000.0 for e0, e1 in times)
+        torch.cuda.synchronize()
+        us.append(e0.elapsed_time(e1) * 1000.0 / reps)
+    del g
+    us.sort()
     med = us[len(us) // 2]
     byts = 2 * rows * V * 4 + rows * HL * 4 + rows * 4
     return {"config": "configs[1]: 128x6563, CFG 0.5, min_p 0.05, top_k 1000, top_p 0.95, penalty 1.2, temp 0.8, "

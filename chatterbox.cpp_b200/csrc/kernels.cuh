@@ -1820,20 +1820,34 @@ __device__ __forceinline__ int samp_finish(const SampArgs & a, int r, int slot, 
     return tok;
 }
 
+// Warp scratch of the few-survivor path (shared memory)
+struct SampWarpBuf { float f[32]; float q[32]; double d[32]; int i[32]; };
+
 // Steps (2)-(5) of the row when at most 32 scores are finite (after min-p),
-// by one warp: lane j holds survivor j, lists are sorted with shuffles, and
-// each sequential float chain of the reference (top-p sum and running sum,
-// softmax sum) is walked in the reference's order by every lane over
-// shuffled operands.  sml: the finite scores' indices (any order); seen:
-// history bit set.  Writes the n survivors in index order to lst and their
+// by one warp: lane j holds survivor j.  Orders come from ranks (each lane
+// counts the lanes ahead of it over 32 shuffles) and a pass through shared
+// memory; each sequential float chain of the reference (top-p sum and
+// running sum, softmax sum) is walked in the reference's order by every lane
+// over values read back from shared memory, whose loads do not wait on the
+// chain.  sml: the finite scores' indices (any order); seen: history bit
+// set.  Writes the n survivors in index order to lst and their
 // probabilities to pr (0 for the ones dropped on the way); returns false
 // when every probability is 0 (the reference returns token 0 undrawn).
 __device__ bool samp_small_probs(const t3b_sample_params & P, int V, const float * s, const int * sml, int n,
                                  const unsigned * seen, const ExpFix & fx, const unsigned long long * e2tab,
-                                 int * lst, float * pr) {
+                                 int * lst, float * pr, SampWarpBuf * wb, unsigned long long * tls) {
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
-    const int idx = (int) (warp_sort_u64(lane < n ? (unsigned long long) (unsigned) sml[lane] : ~0ull) & 0xffffffffu);
+    // survivors in index order: rank of each index among the n (distinct)
+    {
+        const int raw = lane < n ? sml[lane] : 0x7fffffff;
+        int rk = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rk += __shfl_sync(FULL, raw, j) < raw ? 1 : 0;
+        if (lane < n) wb->i[rk] = raw;
+        __syncwarp();
+    }
+    const int idx = lane < n ? wb->i[lane] : -1;
     bool alive = lane < n;
     float v = alive ? s[idx] : -INFINITY;
     // (2) top-k: with n <= k the reference's threshold is -inf (no change);
@@ -1846,49 +1860,60 @@ __device__ bool samp_small_probs(const t3b_sample_params & P, int V, const float
         const float thr2 = above < P.top_k ? __fsub_rn(thr, 1e-10f) : thr;
         alive = alive && v > thr2;
     }
-    // (3) top-p: descending score (ties by index), e = exp(s - max),
-    // psum = sequential sum, keep up to the first j whose running sum of
-    // e / psum reaches top_p
+    // (3) top-p: descending score (ties by index: lanes are in index
+    // order), e = exp(s - max), psum = sequential sum, keep up to the first
+    // rank whose running sum of e / psum reaches top_p
     if (P.top_p < 1.0f) {
-        const unsigned long long kd = warp_sort_u64(alive ? ((unsigned long long) desc_key(v) << 32) | (unsigned) idx : ~0ull);
         const int c = __popc(__ballot_sync(FULL, alive));
         if (c > 0) {
-            const float vj = desc_key_inv((uint32_t) (kd >> 32));
-            const float mx = __shfl_sync(FULL, vj, 0);
-            const float ej = lane < c ? t3_expf_dev(__fsub_rn(vj, mx), fx, e2tab) : 0.0f;
+            const float vv = alive ? v : -INFINITY;
+            int rk = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float o = __shfl_sync(FULL, vv, j);
+                rk += (o > vv || (o == vv && j < lane)) ? 1 : 0;
+            }
+            float mx = vv;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+            const float ej = alive ? t3_expf_dev(__fsub_rn(vv, mx), fx, e2tab) : 0.0f;
+            if (alive) wb->f[rk] = ej;
+            __syncwarp();
             float psum = 0.0f;
-            for (int j = 0; j < c; ++j) psum = __fadd_rn(psum, __shfl_sync(FULL, ej, j));
-            const float qj = __fdiv_rn(ej, psum);
+#pragma unroll 4
+            for (int r = 0; r < c; ++r) psum = __fadd_rn(psum, wb->f[r]);
+            if (alive) wb->q[rk] = __fdiv_rn(ej, psum);
+            __syncwarp();
             float cum = 0.0f;
             int cut = c;
-            for (int j = 0; j < c; ++j) {
-                cum = __fadd_rn(cum, __shfl_sync(FULL, qj, j));
-                if (cum >= P.top_p) { cut = j + 1; break; }
+#pragma unroll 4
+            for (int r = 0; r < c; ++r) {
+                cum = __fadd_rn(cum, wb->q[r]);
+                if (cum >= P.top_p) { cut = r + 1; break; }
             }
-            // sorted position j survives iff j < cut: find this lane's index
-            const int ij = (int) (kd & 0xffffffffu);
-            bool keep = false;
-            for (int j = 0; j < cut; ++j) {   // every lane takes every shuffle
-                const int ix = __shfl_sync(FULL, ij, j);
-                keep |= ix == idx;
-            }
-            alive = alive && keep;
+            alive = alive && rk < cut;
+            __syncwarp();
         }
     }
+    if (tls && lane == 0) { unsigned long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); tls[8] = t_; }
     // (4) repetition penalty on surviving history ids (each id once)
     if (P.repeat_penalty != 1.0f && alive && ((seen[idx >> 5] >> (idx & 31)) & 1u))
         v = v > 0.0f ? __fdiv_rn(v, P.repeat_penalty) : __fmul_rn(v, P.repeat_penalty);
-    // (5) softmax over the survivors in index order (idx ascending by lane)
+    // (5) softmax over the survivors in index order (lane order)
     float mx = alive ? v : -INFINITY;
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
     const float pe = alive ? t3_expf_dev(__fsub_rn(v, mx), fx, e2tab) : 0.0f;
+    wb->f[lane] = pe;
+    __syncwarp();
     float psum = 0.0f;
-    for (int j = 0; j < n; ++j) psum = __fadd_rn(psum, __shfl_sync(FULL, pe, j));
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) psum = __fadd_rn(psum, wb->f[j]);
     if (lane < n) {
         lst[lane] = idx;
         pr[lane] = psum != 0.0f ? __fdiv_rn(pe, psum) : 0.0f;
     }
+    __syncwarp();
     return psum != 0.0f;
 }
 
@@ -1897,7 +1922,7 @@ __device__ bool samp_small_probs(const t3b_sample_params & P, int V, const float
 // dsum = sequential double sum, running sum of p / dsum with the last index
 // (V - 1) forced to 1, first entry >= u.
 __device__ int samp_small_pick(const t3b_sample_params & P, int V, const int * lst, const float * pr, int n,
-                               uint32_t x1, uint32_t x2) {
+                               uint32_t x1, uint32_t x2, SampWarpBuf * wb) {
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const float p = lane < n ? pr[lane] : 0.0f;
@@ -1916,18 +1941,23 @@ __device__ int samp_small_pick(const t3b_sample_params & P, int V, const int * l
         return bp > 0.0f ? ib : 0;
     }
     double dsum = 0.0;
-    for (int j = 0; j < n; ++j) dsum = __dadd_rn(dsum, (double) __shfl_sync(FULL, p, j));
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) dsum = __dadd_rn(dsum, (double) pr[j]);
     const double u = samp_canonical(x1, x2);
     if (u <= 0.0) return 0;
+    wb->d[lane] = (double) p / dsum;   // each term divided once, in parallel
+    __syncwarp();
+    // running sum: every lane walks the chain in the reference's order
     double cc = 0.0;
+    int pick = V - 1;
+#pragma unroll 4
     for (int j = 0; j < n; ++j) {
-        const float pj = __shfl_sync(FULL, p, j);
-        const int ix = __shfl_sync(FULL, idx, j);
-        cc = __dadd_rn(cc, (double) pj / dsum);
-        const double ci = ix == V - 1 ? 1.0 : cc;
-        if (ci >= u) return ix;
+        cc = __dadd_rn(cc, wb->d[j]);
+        const double ci = lst[j] == V - 1 ? 1.0 : cc;
+        if (ci >= u) { pick = lst[j]; break; }
     }
-    return V - 1;
+    __syncwarp();
+    return pick;
 }
 
 // One row of sample_next_token_ex by the whole block (any blockDim.x that
@@ -1957,14 +1987,18 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     __shared__ unsigned long long e2tab[32];   // t3_expf_core's table (first use is after several barriers)
     __shared__ int sml[32];                    // indices kept by min-p while they are at most 32
     __shared__ int sml_n;
+    __shared__ SampWarpBuf swb;                // few-survivor path scratch
 
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31;
+    unsigned long long t_entry = 0;   // debug: the row's first instruction
+    if (a.tl && tid == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_entry));
     const int slot = a.slot_of ? a.slot_of[r] : r;
     if (a.done && a.done[slot]) return -1;
     if (tid < 32) e2tab[tid] = g_t3_exp2_tab[tid];
     if (tid == 0) sml_n = 0;
     unsigned long long * tls = (a.tl && r == 0) ? a.tl : nullptr;
 #define SAMP_STAMP(i) do { if (tls && tid == 0) { unsigned long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); tls[i] = t_; } } while (0)
+    if (tls && tid == 0) tls[T3B_SAMPLER_TL - 2] = t_entry;
     SAMP_STAMP(0);
     const t3b_sample_params P = a.params[a.params_per_row ? r : 0];
     const int V = a.V;
@@ -1973,6 +2007,8 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     const int hl = a.hist_len ? min(a.hist_len[slot], a.hist_stride) : 0;
     const int rmode = a.rng_mode ? a.rng_mode[slot] : T3B_RNG_PHILOX;   // loaded early: used at the draw
     const int * hist = a.hist ? a.hist + (size_t) slot * a.hist_stride : nullptr;
+    // first history id of this thread, loaded now: the min-p stage needs it
+    const int hist0 = (P.repeat_penalty != 1.0f && tid < hl) ? __ldg(hist + tid) : -1;
 
     // (0) CFG mix, (1) temperature  (main.cpp:735-738).  Each thread issues
     // its loads eight at a time (through L2: the persistent kernel passes
@@ -1989,21 +2025,36 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         s[i] = v;
         if (v != -INFINITY) { lmx = fmaxf(lmx, v); lmn = fminf(lmn, v); ++lfin; }
     };
-    if (!cfg) {   // one row: sixteen loads in flight per thread (one round trip for V <= 16 nth)
-        for (int i0 = 0; i0 < V; i0 += 16 * nth) {
-            float cv[16];
+    const int mis = (int) (((uintptr_t) cond >> 2) & 3u);
+    const bool vec = !cfg || mis == (int) (((uintptr_t) unc >> 2) & 3u);
+    if (vec) {
+        // 16-byte loads over the aligned body (both rows share the alignment),
+        // the first `head` and the last few elements one by one; two 16-byte
+        // loads per row and thread in flight (one round trip for V <= 8 nth)
+        const int head = min((4 - mis) & 3, V), nq = (V - head) >> 2, tail0 = head + 4 * nq;
+        const float4 * c4 = (const float4 *) (cond + head);
+        const float4 * u4 = cfg ? (const float4 *) (unc + head) : nullptr;
+        if (tid < head) take(tid, __ldcg(cond + tid), cfg ? __ldcg(unc + tid) : 0.0f);
+        if (tid < V - tail0) take(tail0 + tid, __ldcg(cond + tail0 + tid), cfg ? __ldcg(unc + tail0 + tid) : 0.0f);
+        for (int q0 = 0; q0 < nq; q0 += 2 * nth) {
+            float4 cv[2], uv[2];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const int i = i0 + q * nth + tid;
-                cv[q] = i < V ? __ldcg(cond + i) : 0.0f;
+            for (int k = 0; k < 2; ++k) {
+                const int q = q0 + k * nth + tid;
+                cv[k] = q < nq ? __ldcg(c4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                uv[k] = (cfg && q < nq) ? __ldcg(u4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const int i = i0 + q * nth + tid;
-                if (i < V) take(i, cv[q], 0.0f);
+            for (int k = 0; k < 2; ++k) {
+                const int q = q0 + k * nth + tid;
+                if (q < nq) {
+                    const int i = head + 4 * q;
+                    take(i, cv[k].x, uv[k].x); take(i + 1, cv[k].y, uv[k].y);
+                    take(i + 2, cv[k].z, uv[k].z); take(i + 3, cv[k].w, uv[k].w);
+                }
             }
         }
-    } else {
+    } else {   // CFG rows of different alignment: eight loads per row and thread in flight
         for (int i0 = 0; i0 < V; i0 += 8 * nth) {
             float cv[8], uv[8];
 #pragma unroll
@@ -2019,8 +2070,19 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
             }
         }
     }
-    // count, max and min in one exchange
+    // count, max and min in one exchange; before its barrier, one thread
+    // evaluates log(min_p) for the min-p stage (a double log in every thread
+    // costs microseconds of FP64 issue) and the history bit set is cleared
     const int nw = nth >> 5, w = tid >> 5;
+    const int nwords0 = (V + 31) / 32;
+    if (tid == 0 && P.min_p > 0.0f) {
+        // (double) d <= lg - 1e-5  <=>  d <= largest float not above it;
+        // (double) d >= lg + 1e-5  <=>  d >= smallest float not below it
+        const double lg = log((double) P.min_p);
+        shf[2] = __double2float_rd(lg - 1e-5);
+        shf[3] = __double2float_ru(lg + 1e-5);
+    }
+    for (int i = tid; i < nwords0; i += nth) seen[i] = 0u;
     lfin = warp_sum_i(lfin);
     lmx = warp_max(lmx);
     lmn = -warp_max(-lmn);
@@ -2037,9 +2099,15 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
     // exp, far above one ulp); only that window evaluates expf exactly.
     if (P.min_p > 0.0f && nfin > 0) {
         const bool fast = P.min_p >= 1e-30f;
-        const double lg = log((double) P.min_p);
-        const double lo = lg - 1e-5, hi = lg + 1e-5;
+        const float flo = shf[2], fhi = shf[3];
         int kept = 0;
+        // history ids into the bit set (published by the count's barrier):
+        // the few-survivor path below uses it as is
+        if (P.repeat_penalty != 1.0f)
+            for (int j = tid; j < hl; j += nth) {
+                const int t = j == tid ? hist0 : hist[j];
+                if (t >= 0 && t < V) atomicOr(&seen[t >> 5], 1u << (t & 31));
+            }
         for (int i0 = 0; i0 < V; i0 += nth) {   // warp-uniform trip count (the ballot below)
             const int i = i0 + tid;
             bool keep = false;
@@ -2048,8 +2116,8 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
                 if (v != -INFINITY) {
                     const float d = __fsub_rn(v, smax);
                     bool drop;
-                    if (fast && (double) d <= lo) drop = true;
-                    else if (fast && (double) d >= hi) drop = false;
+                    if (fast && d <= flo) drop = true;
+                    else if (fast && d >= fhi) drop = false;
                     else drop = t3_expf_dev(d, a.fx, e2tab) < P.min_p;
                     if (drop) s[i] = -INFINITY;
                     else { ++kept; keep = true; }
@@ -2066,37 +2134,51 @@ __device__ __noinline__ int sample_row_block(const SampArgs & a, int r, unsigned
         }
         nfin = block_sum_i(kept, redi);
         if (nfin > 0 && nfin <= 32) {
-            // Few survivors: steps (2)-(7) by one warp over the list
+            // Few survivors: steps (2)-(7) by one warp over the list (the
+            // history bit set is complete: block_sum_i's barrier)
             SAMP_STAMP(2);
-            const int nwords = (V + 31) / 32;
-            for (int i = tid; i < nwords; i += nth) seen[i] = 0u;
-            __syncthreads();
-            if (P.repeat_penalty != 1.0f)
-                for (int j = tid; j < hl; j += nth) {
-                    const int t = hist[j];
-                    if (t >= 0 && t < V) atomicOr(&seen[t >> 5], 1u << (t & 31));
-                }
-            __syncthreads();
-            if (tid < 32) {
-                const bool ok = samp_small_probs(P, V, s, sml, nfin, seen, a.fx, e2tab, lst, e);
-                if (lane == 0) shi[7] = ok;
-            }
-            __syncthreads();
-            SAMP_STAMP(12);
             int tok = 0;
-            if (shi[7]) {
-                uint32_t x1 = 0u, x2 = 0u;
-                if (P.temp > 0.0f) samp_rng_bits(a, slot, rmode, mtx, x1, x2);
-                SAMP_STAMP(13);
+            if (rmode != T3B_RNG_MT19937) {
+                // Philox: the draw is computed by the warp itself, no barrier
                 if (tid < 32) {
-                    const int t = samp_small_pick(P, V, lst, e, nfin, x1, x2);
+                    const bool ok = samp_small_probs(P, V, s, sml, nfin, seen, a.fx, e2tab, lst, e, &swb, tls);
+                    uint32_t x1 = 0u, x2 = 0u;
+                    if (ok && P.temp > 0.0f) {
+                        const unsigned long long sd = a.ph_seed[slot];
+                        const unsigned long long ct = a.ph_ctr[slot];
+                        uint32_t c4[4] = {(uint32_t) ct, (uint32_t) (ct >> 32), (uint32_t) slot, 0u};
+                        philox4x32_10(c4, (uint32_t) sd, (uint32_t) (sd >> 32));
+                        x1 = c4[0]; x2 = c4[1];
+                        if (lane == 0) a.ph_ctr[slot] = ct + 1ull;
+                    }
+                    const int t = ok ? samp_small_pick(P, V, lst, e, nfin, x1, x2, &swb) : 0;
                     if (lane == 0) shi[6] = t;
                 }
                 __syncthreads();
                 tok = shi[6];
+            } else {
+                if (tid < 32) {
+                    const bool ok = samp_small_probs(P, V, s, sml, nfin, seen, a.fx, e2tab, lst, e, &swb, tls);
+                    if (lane == 0) shi[7] = ok;
+                }
+                __syncthreads();
+                SAMP_STAMP(12);
+                if (shi[7]) {
+                    uint32_t x1 = 0u, x2 = 0u;
+                    if (P.temp > 0.0f) samp_rng_bits(a, slot, rmode, mtx, x1, x2);
+                    SAMP_STAMP(13);
+                    if (tid < 32) {
+                        const int t = samp_small_pick(P, V, lst, e, nfin, x1, x2, &swb);
+                        if (lane == 0) shi[6] = t;
+                    }
+                    __syncthreads();
+                    tok = shi[6];
+                }
             }
             SAMP_STAMP(15);
-            return samp_finish(a, r, slot, hl, tok);
+            const int tk = samp_finish(a, r, slot, hl, tok);
+            SAMP_STAMP(T3B_SAMPLER_TL - 1);
+            return tk;
         }
     }
 
