@@ -415,17 +415,24 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         }
         return;
     }
+    // plain epilogue through the same tile: each warp then stores 32
+    // consecutive columns of a row (coalesced), with one copy of the
+    // epilogue's code instead of sixteen unrolled ones
+    float (*Tt)[GQ_BN + 1] = (float (*)[GQ_BN + 1]) & As[0][0][0];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            const int m = m0 + wm * 32 + mt * 16 + g;
-            const int n = n0 + wn * 16 + nt * 8 + 2 * t;
-            if (m < M && n < N) epi_store(e, m, n, acc[mt][nt][0]);
-            if (m < M && n + 1 < N) epi_store(e, m, n + 1, acc[mt][nt][1]);
-            if (m + 8 < M && n < N) epi_store(e, m + 8, n, acc[mt][nt][2]);
-            if (m + 8 < M && n + 1 < N) epi_store(e, m + 8, n + 1, acc[mt][nt][3]);
-        }
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                Tt[wm * 32 + mt * 16 + g + (i >> 1) * 8][wn * 16 + nt * 8 + 2 * t + (i & 1)] = acc[mt][nt][i];
+    __syncthreads();
+    const int rows = min(GQ_BM, M - m0);
+#pragma unroll 1
+    for (int q = threadIdx.x; q < rows * GQ_BN; q += blockDim.x) {
+        const int r = q / GQ_BN, c = q % GQ_BN;
+        if (n0 + c < N) epi_store(e, m0 + r, n0 + c, Tt[r][c]);
+    }
 }
 
 // F16 weights x f16-rounded activations, f32 accumulation (each f16*f16
@@ -940,10 +947,22 @@ __global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_consta
         }
         if (tid == 0) p.cnt[tile] = 0u;
     }
-    if (!mrow) return;
+    // epilogue through shared memory (the ring is free): row m's 64 values
+    // into a padded tile, then each warp stores 32 consecutive columns of a
+    // row at a time (coalesced), with one copy of the epilogue's code rather
+    // than 64 unrolled ones, which the CTA would fetch cold exactly once
+    // (the MMAs that read the ring completed before the accumulator was read)
+    if (!tf_ok) return;              // CTA-uniform
+    float * tile_s = (float *) As;   // [TF_BM][TF_BN + 1]
 #pragma unroll
-    for (int j = 0; j < TF_BN; ++j)
-        if (n0 + j < p.N) epi_store(p.e, m, n0 + j, v[j]);
+    for (int j = 0; j < TF_BN; ++j) tile_s[tid * (TF_BN + 1) + j] = v[j];
+    __syncthreads();
+    const int rows = min(TF_BM, p.M - m0);
+#pragma unroll 1
+    for (int q = tid; q < rows * TF_BN; q += TF_BM) {
+        const int r = q / TF_BN, c = q % TF_BN;
+        if (n0 + c < p.N) epi_store(p.e, m0 + r, n0 + c, tile_s[r * (TF_BN + 1) + c]);
+    }
 }
 
 // Plain f32 matvec for the speaker projection (cond_spkr: K = 256).

@@ -349,7 +349,9 @@ bool launch_gemm_f16_tc(const Mat & W, const __half * xh, int M, const GemvEpi &
     const int nkb = W.K / TF_BK;
     int splits = 1;
     if (gw && gw->ws && gw->cnt && tiles <= gw->ccap && tiles < 120) {
-        splits = std::min(std::max(1, 148 / tiles), 8);
+        // at least 4 K-steps (256 columns) per split: below that the split
+        // partials' write and in-order sum cost more than the idle SMs
+        splits = std::min(std::min(std::max(1, 148 / tiles), 8), std::max(1, nkb / 4));
         const size_t ldw = (size_t) tx * TF_BN;
         while (splits > 1 && (nkb % splits != 0 || (size_t) splits * M * ldw > gw->cap)) --splits;
     }
