@@ -201,7 +201,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="leave out the batched CFG run (profiling commands)")
-    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels", "sweep", "serve3", "serve4"],
+    ap.add_argument("--only", choices=["sampler", "gemv", "timeline", "batched", "kernels", "sweep", "serve3", "serve4",
+                                       "refdefault"],
                     default=None,
                     help="run one kernel micro-benchmark alone (ncu captures), or the megakernel phase timeline")
     args = ap.parse_args()
@@ -225,6 +226,9 @@ def main():
         elif args.only == "sweep":
             import torch
             r = gemv_sweep(pkg, torch, peak)
+        elif args.only == "refdefault":
+            hp, t = make_model(pkg, seed=0)
+            r = reference_default_decode(pkg, hp, t, pkg.SampleParams.make(**PARAMS), model_weight_bytes(t), peak)
         else:
             r = sampler_microbench(pkg, torch, peak, reps=20) if args.only == "sampler" else gemv_roofline(pkg, torch, peak)
         print(json.dumps(r), flush=True)
@@ -318,6 +322,7 @@ def main():
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
             "sampler": sampler_microbench(pkg, torch, peak),
+            "batch1_reference_default": reference_default_decode(pkg, hp, t, params, wbytes, peak),
             "serving_configs3": serving(pkg, torch, peak, 3, dist, ws, rank, local) if not args.no_batched else None,
             "serving_configs4": ({q: serving(pkg, torch, peak, 4, dist, ws, rank, local, quant=q) for q in ("q4_0", "f16")}
                                  if ws == 8 and not args.no_batched else None),
@@ -406,6 +411,43 @@ def serving(pkg, torch, peak, which, dist, ws, rank, local, quant=None, steps=No
             "rank0_streams": len(mine), "rank0_achieved_gbs": ach, "rank0_frac": ach / peak, "peak": peak,
             "path": "t3b_serve_run: admit (prefill + first sample) into free slots, one batched step + sampler "
                     "per iteration over all admitted streams, retire at stop / n_predict"}
+
+
+def reference_default_decode(pkg, hp, t, params, wbytes, peak, steps=1000):
+    """Batch 1 at the reference's defaults: the builtin cond prompt of 375
+    speech tokens (src/chatterbox_cli.cpp:707) + 86 text ids (prompt 463) and
+    n_predict = 1000 (include/tts-cpp/chatterbox/engine.h:84), stop ignored:
+    positions 463 .. 1462, past the 640 that fit the persistent kernel's
+    K/V stage at once (the long-context instantiation streams K/V in tiles).
+    Same weights as configs[0] with a 375-token cond prompt."""
+    rng = np.random.default_rng(7)
+    hp2 = dict(hp, cond_prompt_len=375)
+    t2 = dict(t)
+    ty, _ = t["chatterbox/builtin/cond_prompt_speech_tokens"]
+    t2["chatterbox/builtin/cond_prompt_speech_tokens"] = (
+        ty, rng.integers(0, hp["start_speech_token"], 375).astype(np.int32))
+    m = pkg.T3Model(hp2, t2)
+    try:
+        m.alloc_streams(1, 1536)
+        text = rng.integers(0, 50257, PROMPT_TEXT).astype(np.int32)
+        m.prefill(0, text)
+        m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
+        m.decode([params], 8, ignore_stop=True)          # warm-up
+        P, _ = m.prefill(0, text)
+        m.set_rng(0, pkg.T3B_RNG_MT19937, 0, 0)
+        n0 = m.launch_count()
+        m.decode([params], steps, ignore_stop=True)
+        ms = m.last_device_ms()
+        launches = m.launch_count() - n0
+    finally:
+        m.close()
+    L_mean = P + (steps + 1) / 2.0
+    byts = algorithmic_bytes_per_step(hp, L_mean, wbytes)
+    ach = byts / (ms / steps / 1000.0) / 1e9
+    return {"config": "batch-1 Q4_0, builtin cond prompt 375 + 86 text ids, 1000 decode steps (stop ignored)",
+            "positions": [int(P), int(P + steps - 1)], "value": steps / (ms / 1000.0), "unit": UNIT,
+            "ms_per_step": ms / steps, "gpu_launches": launches,
+            "roofline": {"achieved_gbs": ach, "peak": peak, "frac": ach / peak, "bytes_per_step": byts, "mean_L": L_mean}}
 
 
 def sampler_microbench(pkg, torch, peak, reps=200):
