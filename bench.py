@@ -322,7 +322,7 @@ def main():
                          "bytes_per_step": step_bytes, "mean_L": L_mean},
             "gemv_roofline": gemv,
             "sampler": sampler_microbench(pkg, torch, peak),
-            "batch1_reference_default": reference_default_decode(pkg, hp, t, params, wbytes, peak),
+            "batch1_reference_default": reference_default_decode(pkg, hp, t, params, wbytes, peak, device=local),
             "serving_configs3": serving(pkg, torch, peak, 3, dist, ws, rank, local) if not args.no_batched else None,
             "serving_configs4": ({q: serving(pkg, torch, peak, 4, dist, ws, rank, local, quant=q) for q in ("q4_0", "f16")}
                                  if ws == 8 and not args.no_batched else None),
@@ -413,7 +413,7 @@ def serving(pkg, torch, peak, which, dist, ws, rank, local, quant=None, steps=No
                     "per iteration over all admitted streams, retire at stop / n_predict"}
 
 
-def reference_default_decode(pkg, hp, t, params, wbytes, peak, steps=1000):
+def reference_default_decode(pkg, hp, t, params, wbytes, peak, steps=1000, device=0):
     """Batch 1 at the reference's defaults: the builtin cond prompt of 375
     speech tokens (src/chatterbox_cli.cpp:707) + 86 text ids (prompt 463) and
     n_predict = 1000 (include/tts-cpp/chatterbox/engine.h:84), stop ignored:
@@ -426,7 +426,7 @@ def reference_default_decode(pkg, hp, t, params, wbytes, peak, steps=1000):
     ty, _ = t["chatterbox/builtin/cond_prompt_speech_tokens"]
     t2["chatterbox/builtin/cond_prompt_speech_tokens"] = (
         ty, rng.integers(0, hp["start_speech_token"], 375).astype(np.int32))
-    m = pkg.T3Model(hp2, t2)
+    m = pkg.T3Model(hp2, t2, device=device)
     try:
         m.alloc_streams(1, 1536)
         text = rng.integers(0, 50257, PROMPT_TEXT).astype(np.int32)
