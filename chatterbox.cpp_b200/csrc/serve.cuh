@@ -183,6 +183,7 @@ int t3b_serve_run(t3b_ctx * ctx, int max_iters, int32_t * n_active, int32_t * n_
             }
             CK(cudaMemcpyAsync(ctx->pos, pos.data(), sizeof(int) * pos.size(), cudaMemcpyHostToDevice, st));
             CK(cudaMemcpyAsync(ctx->params, prm.data(), sizeof(t3b_sample_params) * n, cudaMemcpyHostToDevice, st));
+            ctx->params_last.clear();
             if (S.tok_cap < ctx->S) {
                 if (S.tok_pin) CK(cudaFreeHost(S.tok_pin));
                 CK(cudaHostAlloc((void **) &S.tok_pin, sizeof(int) * ctx->S, cudaHostAllocDefault));

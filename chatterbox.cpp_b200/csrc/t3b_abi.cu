@@ -167,6 +167,10 @@ struct t3b_ctx {
     ExpFix fx{};
     unsigned * err_word = nullptr;
     unsigned * err_pin = nullptr;   // pinned host copy of err_word (read in the same synchronize as results)
+    // pinned staging of the per-step calls' host buffers (logits in/out, tokens): a pageable copy of
+    // 26 KB costs a synchronous staging pass of its own
+    float * io_pin = nullptr; size_t io_pin_cap = 0;
+    std::vector<t3b_sample_params> params_last;   // what t3b_sample last uploaded to params (empty: unknown)
     volatile int cancel = 0;
     float last_ms = 0.0f;
     unsigned wait_limit = 0;            // persistent-kernel wait limit in polls (0: MK_SPIN)
@@ -643,6 +647,7 @@ void t3b_destroy(t3b_ctx * ctx) {
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
     if (ctx->err_pin) cudaFreeHost(ctx->err_pin);
+    if (ctx->io_pin) cudaFreeHost(ctx->io_pin);
     if (ctx->st) cudaStreamDestroy(ctx->st);
     delete ctx;
 }
@@ -718,6 +723,7 @@ int t3b_stream_alloc(t3b_ctx * ctx, int n_streams, int max_ctx, int cfg) {
     free_streams(ctx);
     const int D = ctx->hp.n_embd, H = ctx->hp.n_head, V = ctx->hp.n_speech_vocab;
     ctx->S = n_streams; ctx->rps = cfg ? 2 : 1; ctx->max_ctx = max_ctx;
+    ctx->params_last.clear();
     ctx->hist_cap = max_ctx;
     ctx->s_max = (max_ctx + T3B_ATTN_CHUNK - 1) / T3B_ATTN_CHUNK;
     const int rows = n_streams * ctx->rps;
@@ -884,6 +890,21 @@ namespace {
 // graph reads its row maps (row_slot, row_of, slot_list), tokens and
 // positions from device buffers, so one graph serves any n streams;
 // upload_maps() fills the maps before a launch.
+// Pinned staging area of at least `floats` floats (nullptr if it cannot be had: the caller copies directly).
+float * io_pinned(t3b_ctx * ctx, size_t floats) {
+    if (ctx->io_pin_cap < floats) {
+        if (ctx->io_pin) cudaFreeHost(ctx->io_pin);
+        ctx->io_pin = nullptr; ctx->io_pin_cap = 0;
+        if (cudaHostAlloc((void **) &ctx->io_pin, floats * sizeof(float), cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            ctx->io_pin = nullptr;
+            return nullptr;
+        }
+        ctx->io_pin_cap = floats;
+    }
+    return ctx->io_pin;
+}
+
 int upload_maps(t3b_ctx * ctx, const std::vector<int> & slots) {
     if (!ctx->maps_slots.empty() && ctx->maps_slots == slots) return T3B_OK;   // already on the device
     const int n = (int) slots.size(), M = n * ctx->rps;
@@ -1135,9 +1156,11 @@ int t3b_step(t3b_ctx * ctx, int n, const int32_t * streams, const int32_t * toke
         rc = mega_decode(ctx, slots[0], p_first, 1, 1, nullptr, dst, tokens[0]);
         if (rc != T3B_OK) return rc;
         CK(cudaEventRecord(ctx->ev1, st));
-        if (logits_out) CK(cudaMemcpyAsync(logits_out, dst, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
+        float * pin = logits_out ? io_pinned(ctx, (size_t) V) : nullptr;
+        if (logits_out) CK(cudaMemcpyAsync(pin ? pin : logits_out, dst, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
         CK(cudaMemcpyAsync(ctx->err_pin, ctx->err_word, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
+        if (pin) std::memcpy(logits_out, pin, sizeof(float) * V);
         cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1);
         ctx->pos_host[slots[0]] = p_first + 1;
         return *ctx->err_pin ? check_dev_err(ctx) : T3B_OK;
@@ -1180,21 +1203,37 @@ int t3b_sample(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     CK(cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->st;
     const int V = ctx->hp.n_speech_vocab;
-    if (logits)
+    // pinned staging: [host logits n * rps * V][tokens n]
+    const size_t nl = logits ? (size_t) n * ctx->rps * V : 0;
+    float * pin = io_pinned(ctx, nl + (size_t) n);
+    if (logits) {
+        if (pin) std::memcpy(pin, logits, sizeof(float) * nl);
+        const float * srcl = pin ? pin : logits;
         for (int i = 0; i < n; ++i)
-            CK(cudaMemcpyAsync(ctx->logits + (size_t) slots[i] * ctx->rps * V, logits + (size_t) i * ctx->rps * V,
+            CK(cudaMemcpyAsync(ctx->logits + (size_t) slots[i] * ctx->rps * V, srcl + (size_t) i * ctx->rps * V,
                                sizeof(float) * ctx->rps * V, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(ctx->params, params, sizeof(t3b_sample_params) * n, cudaMemcpyHostToDevice, st));
-    ctx->maps_slots.clear();
-    CK(cudaMemcpyAsync(ctx->slot_list, slots.data(), sizeof(int) * n, cudaMemcpyHostToDevice, st));
+    }
+    // parameters and slot list: uploaded only when they differ from what the device holds
+    if ((int) ctx->params_last.size() != n ||
+        std::memcmp(ctx->params_last.data(), params, sizeof(t3b_sample_params) * n) != 0) {
+        // (a pageable source is staged before the call returns)
+        CK(cudaMemcpyAsync(ctx->params, params, sizeof(t3b_sample_params) * n, cudaMemcpyHostToDevice, st));
+        ctx->params_last.assign(params, params + n);
+    }
+    if (ctx->maps_slots != slots) {
+        ctx->maps_slots.clear();
+        CK(cudaMemcpyAsync(ctx->slot_list, slots.data(), sizeof(int) * n, cudaMemcpyHostToDevice, st));
+    }
     SampArgs a = sampler_args(ctx, false);
     CK(cudaEventRecord(ctx->ev0, st));
     sampler_kernel<<<n, T3B_SAMPLER_THREADS, T3B_SAMPLER_SMEM, st>>>(a);
     CK(cudaGetLastError());
     ctx->launches += 1;
     CK(cudaEventRecord(ctx->ev1, st));
-    CK(cudaMemcpyAsync(tokens_out, ctx->tok_out, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
+    int * tpin = pin ? (int *) (pin + nl) : nullptr;
+    CK(cudaMemcpyAsync(tpin ? tpin : tokens_out, ctx->tok_out, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+    if (tpin) std::memcpy(tokens_out, tpin, sizeof(int) * n);
     cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1);
     return T3B_OK;
 }
@@ -1229,6 +1268,7 @@ int t3b_decode(t3b_ctx * ctx, int n, const int32_t * streams, const t3b_sample_p
     rc = upload_maps(ctx, slots);
     if (rc != T3B_OK) return rc;
     CK(cudaMemcpyAsync(ctx->params, params, sizeof(t3b_sample_params) * n, cudaMemcpyHostToDevice, st));
+    ctx->params_last.clear();
     CK(cudaMemcpyAsync(ctx->pos, pos.data(), sizeof(int) * M, cudaMemcpyHostToDevice, st));
     std::vector<int> zeros(ctx->S, 0);
     CK(cudaMemcpyAsync(ctx->done, zeros.data(), sizeof(int) * ctx->S, cudaMemcpyHostToDevice, st));
