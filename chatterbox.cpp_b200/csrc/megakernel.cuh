@@ -57,7 +57,11 @@
 #define MK_B_HS (MK_B_HD + 128)             //   block sums [128]
 #define MK_B_XT (MK_B_HS + 128)             // Q4_0 layout: x as tagged words [1024] u64 (2048 floats)
 #define MK_B_HT (MK_B_XT + 2048)            // Q4_0 layout: h in Q8_0 as tagged words [1280] u64
-#define MK_B_TOTAL (MK_B_HT + 2560)
+#define MK_HPH 7                            // long contexts: helper workers per head (worker CTAs 1..112)
+#define MK_HR_WORDS 66                      //   one helper's result: max, sum, o[64]
+#define MK_HMAX 2048                        //   helped up to this many positions (slices of <= 256)
+#define MK_B_HR (MK_B_HT + 2560)            // the helpers' results as tagged words [16][MK_HPH][66] u64
+#define MK_B_TOTAL (MK_B_HR + 2 * 16 * MK_HPH * MK_HR_WORDS)
 enum { MK_C_QKV, MK_C_ATT, MK_C_XM, MK_C_H, MK_C_X, MK_C_LOG, MK_C_TOK, MK_C_N };
 #define MK_C_STRIDE 32   // counters 128 bytes apart
 #define MK_CTL_WORDS ((MK_C_N + 2) * MK_C_STRIDE)   // counters, abort flag, steps done
@@ -831,9 +835,10 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
 // Bulk-copy bookkeeping of a CTA, one register (every thread holds the same
 // value): per mbarrier i (0: K rows + q/k/v weights, 1: V rows / tile
 // buffer B, 2: head rows, 3: tile buffer A, 4 and 5: a worker's fc + fc2
-// rows of even and odd layer uses) bit 2i = a phase was issued and not yet
-// waited for, bit 2i+1 = that phase's parity; bits 12 and 13 = the parity
-// of the next phase of mbarriers 1 and 3.
+// rows of even and odd layer uses, 6: a helper's q rows and K/V slice) bit
+// 2i = a phase was issued and not yet waited for, bit 2i+1 = that phase's
+// parity; bits 16, 17 and 18 = the parity of the next phase of mbarriers 1,
+// 3 and 6.
 #define CP_OUT(i) ((cp >> (2 * (i))) & 1u)
 #define CP_PAR(i) ((cp >> (2 * (i) + 1)) & 1u)
 #define CP_ISSUE(i, par) (cp = (cp & ~(3u << (2 * (i)))) | ((1u | (((unsigned) (par) & 1u) << 1)) << (2 * (i))))
@@ -842,8 +847,8 @@ __device__ __forceinline__ int mk_fc_r0(int c, int G, bool blocks) {
 #define CP_ISSUE_NEXT(i, nb) do { CP_ISSUE(i, (cp >> (nb)) & 1u); cp ^= 1u << (nb); } while (0)
 
 // waits (bounded, MK_SPIN polls each) for every copy phase still in flight
-#define MK_NMBAR 6
-#define CP_PENDING 0xfffu   // bits 0..11: phases issued per mbarrier
+#define MK_NMBAR 7
+#define CP_PENDING 0x3fffu   // bits 0..13: phases issued per mbarrier
 __device__ __noinline__ void mk_drain(unsigned long long * mbar, unsigned cp) {
 #pragma unroll 1
     for (int i = 0; i < MK_NMBAR; ++i)
@@ -881,8 +886,8 @@ __device__ __noinline__ unsigned mk_issue_tile(unsigned cp, int i, int npos, con
             mk_bulk_g2s(dst + (size_t) MK_TP * T3B_HD, kb + v_off + (size_t) t0 * T3B_HD, rb, mb);
         }
     }
-    if (inB) CP_ISSUE_NEXT(1, 12);
-    else CP_ISSUE_NEXT(3, 13);
+    if (inB) CP_ISSUE_NEXT(1, 16);
+    else CP_ISSUE_NEXT(3, 17);
     return cp;
 }
 
@@ -978,6 +983,167 @@ __device__ __noinline__ float mk_attend_tiled(unsigned * cpp, bool tile0_ready, 
     return warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
 }
 
+// ---------------------------------------------------------------------------
+// Contexts of MK_MAX_POS < L <= MK_HMAX positions (Q4_0 layout): each head's
+// positions split over its attention CTA and MK_HPH idle worker CTAs.  A
+// slice is C = ceil(L / (MK_HPH + 1)) positions; helper j takes positions
+// [j C, (j + 1) C), the attention CTA the rest (with the current position).
+// A helper computes the head's q itself (LN1 of x, its 64 q rows bulk-copied
+// with its K/V slice), attends its slice and publishes (max, sum, o[64]) as
+// tagged words; the attention CTA merges them with its own slice in helper
+// order.  One K/V stream of a long head is then 8 SMs' work instead of one's.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int mk_hslice(int L) { return (L + MK_HPH) / (MK_HPH + 1); }
+
+// Attention of one slice by the CTA: keys j < n (<= MK_THREADS), K row j at
+// ks + 64 j, V row j at vs + 64 j (shared memory), query q[64] (shared).
+// Writes the per-warp outputs og[16][64]; returns {max score, sum of p}.
+__device__ float2 mk_attend_slice(int n, const float * q, const __half * ks, const __half * vs, float * pw, float * rf,
+                                  float * og) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    float sc = -INFINITY;
+    if (tid < n) {
+        const uint4 * kp = (const uint4 *) (ks + (size_t) tid * T3B_HD);
+        float dot = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const int c = (cc + tid) & 7;
+            const uint4 uu = kp[c];
+            const float4 qa = *(const float4 *) (q + c * 8), qb = *(const float4 *) (q + c * 8 + 4);
+            const __half2 * hp = (const __half2 *) &uu;
+            const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
+            const float2 f2 = __half22float2(hp[2]), f3 = __half22float2(hp[3]);
+            dot = fmaf(qa.x, f0.x, dot); dot = fmaf(qa.y, f0.y, dot);
+            dot = fmaf(qa.z, f1.x, dot); dot = fmaf(qa.w, f1.y, dot);
+            dot = fmaf(qb.x, f2.x, dot); dot = fmaf(qb.y, f2.y, dot);
+            dot = fmaf(qb.z, f3.x, dot); dot = fmaf(qb.w, f3.y, dot);
+        }
+        sc = dot * 0.125f;
+    }
+    const float lm = warp_max(sc);
+    if (lane == 0) rf[w] = lm;
+    __syncthreads();
+    const float mx = warp_max(rf[lane & 15]);
+    const float p = tid < n ? expf(sc - mx) : 0.0f;
+    if (tid < n) pw[tid] = p;
+    const float ls = warp_sum(p);
+    if (lane == 0) rf[32 + w] = ls;
+    __syncthreads();
+    const float l = warp_sum(lane < 16 ? rf[32 + lane] : 0.0f);
+    float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
+    int j = w;
+    for (; j + 16 < n; j += 32) {
+        const float2 v0 = __half22float2(*(const __half2 *) (vs + (size_t) j * T3B_HD + 2 * lane));
+        const float2 v1 = __half22float2(*(const __half2 *) (vs + (size_t) (j + 16) * T3B_HD + 2 * lane));
+        const float p0 = pw[j], p1 = pw[j + 16];
+        o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+        o1.x = fmaf(p1, v1.x, o1.x); o1.y = fmaf(p1, v1.y, o1.y);
+    }
+    if (j < n) {
+        const float2 v0 = __half22float2(*(const __half2 *) (vs + (size_t) j * T3B_HD + 2 * lane));
+        const float p0 = pw[j];
+        o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
+    }
+    og[w * 64 + 2 * lane] = o0.x + o1.x;
+    og[w * 64 + 2 * lane + 1] = o0.y + o1.y;
+    __syncthreads();
+    return make_float2(mx, l);
+}
+
+// A helper's slice: q = its head's 64 q rows (staged Q4_0, the attention
+// CTA's lane layout and bias order, so q is the same bits) on the prepared
+// LN1 activation, the slice's attention, then {max, sum, o[64]} as tagged
+// words at dst.
+__device__ __noinline__ void mk_help(const unsigned char * qw, const MkAct & act, const float * bq, int n,
+                                     const __half * ks, const __half * vs, float * att_s, float * rf,
+                                     unsigned long long * dst, unsigned tag) {
+    const int tid = threadIdx.x;
+    float * q = att_s;              // [64]
+    float * pw = att_s + 256;       // [n]
+    float * og = att_s + 256 + MK_MAX_POS;   // [16][64]
+    mk_rows_q4_smem(qw, T3B_HD, act, att_s + 64);
+    __syncthreads();
+    if (tid < T3B_HD) q[tid] = __fadd_rn(__fadd_rn(0.0f, att_s[64 + tid]), __ldg(bq + tid));
+    __syncthreads();
+    const float2 ml = mk_attend_slice(n, q, ks, vs, pw, rf, og);
+    if (tid < T3B_HD) {
+        float o = 0.0f;
+#pragma unroll
+        for (int gg = 0; gg < 16; ++gg) o += og[gg * 64 + tid];
+        mk_st_x(dst + 2 + tid, tag, o);
+    }
+    if (tid == 0) { mk_st_x(dst, tag, ml.x); mk_st_x(dst + 1, tag, ml.y); }
+    __syncthreads();
+}
+
+// The attention CTA's side: its own slice (L_own keys, K rows at kst, V rows
+// at kst + 64 L_own), then the merge with the MK_HPH helpers' results for
+// this head (src: [MK_HPH][66] tagged words, polled by warp 0): the combined
+// output goes to og[0][*] (og[1..15][*] zeroed) and the combined sum is
+// returned, so the caller's sum over og / denominator gives the attention.
+// Negative (every thread) when the wait gave up.
+__device__ __noinline__ float mk_attend_helped(int L_own, const float * qkvh, const __half * kst, float * pw, float * rf,
+                                               float * og, float * hr, const unsigned long long * src, unsigned tag,
+                                               unsigned spin, unsigned * err, int * abort_flag, int * okf) {
+    const int tid = threadIdx.x;
+    const float2 ml = mk_attend_slice(L_own, qkvh, kst, kst + (size_t) L_own * T3B_HD, pw, rf, og);
+    constexpr int NW = MK_HPH * MK_HR_WORDS, NQ = (NW + 31) / 32;
+    if (tid < 32) {
+        const int lane = tid;
+        unsigned long long wv[NQ];
+        int ok = 1;
+        for (unsigned spins = 0;; ++spins) {
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) {
+                const int i = q * 32 + lane;
+                if (i < NW) asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(wv[q]) : "l"(src + i) : "memory");
+                else wv[q] = (unsigned long long) tag << 32;
+            }
+            bool all = true;
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) all = all && (unsigned) (wv[q] >> 32) == tag;
+            if (__all_sync(0xffffffffu, all)) break;
+            int stop = 0;
+            if (lane == 0 && (spins > spin || ((spins & 255u) == 0 && *(volatile int *) abort_flag))) {
+                if (spins > spin) { atomicOr(err, T3B_DEVERR_TIMEOUT); atomicExch(abort_flag, 1); }
+                stop = 1;
+            }
+            if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
+            __nanosleep(20);
+        }
+        if (ok) {
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) {
+                const int i = q * 32 + lane;
+                if (i < NW) hr[i] = __uint_as_float((unsigned) wv[q]);
+            }
+        }
+        if (lane == 0) *okf = ok;
+    }
+    __syncthreads();
+    if (!*okf) return -1.0f;
+    // merge in order: own slice, helpers 0 .. MK_HPH - 1
+    float M = ml.x;
+#pragma unroll
+    for (int jh = 0; jh < MK_HPH; ++jh) M = fmaxf(M, hr[jh * MK_HR_WORDS]);
+    const float so = expf(ml.x - M);
+    float lt = ml.y * so;
+#pragma unroll
+    for (int jh = 0; jh < MK_HPH; ++jh) lt = fmaf(hr[jh * MK_HR_WORDS + 1], expf(hr[jh * MK_HR_WORDS] - M), lt);
+    float o = 0.0f;
+    if (tid < T3B_HD) {
+#pragma unroll
+        for (int gg = 0; gg < 16; ++gg) o += og[gg * 64 + tid];
+        o *= so;
+#pragma unroll
+        for (int jh = 0; jh < MK_HPH; ++jh) o = fmaf(hr[jh * MK_HR_WORDS + 2 + tid], expf(hr[jh * MK_HR_WORDS] - M), o);
+    }
+    __syncthreads();   // every read of og is done
+    for (int i = tid; i < 16 * T3B_HD; i += MK_THREADS) og[i] = i < T3B_HD ? o : 0.0f;
+    __syncthreads();
+    return lt;
+}
+
 // LONG: the instantiation that can stream K/V in tiles past MK_MAX_POS
 // positions.  The host launches it only when a decode will pass that many
 // positions; the common instantiation carries none of that code, which
@@ -1038,6 +1204,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     const bool worker = !OWN || !att;
     const int GW = OWN ? G - Hn : G;
     const int wi = OWN ? (cta == 0 ? 0 : cta - Hn) : cta;
+    // long contexts (LONG, Q4_0): workers 1 .. 16 MK_HPH help head (wi - 1) / MK_HPH with slice (wi - 1) % MK_HPH
+    const bool helper = LONG && OWN && worker && wi >= 1 && wi <= 16 * MK_HPH;
+    const int hh_h = helper ? (wi - 1) / MK_HPH : 0, hj_h = helper ? (wi - 1) % MK_HPH : 0;
     // OWN staging: mbar[0] = a use's K rows + q/k/v weights (use u = step *
     // n_layer + layer completes phase u), plus its V rows when K and V of
     // positions [0, pos] fit the K stage together ("packed": V at row pos+1);
@@ -1077,18 +1246,23 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
     // warp's first thread (not the hand-off poller)
     auto packed = [](int p) { return 2 * (p + 1) <= MK_MAX_POS; };
     auto tiled = [](int p) { return LONG && p + 1 > MK_MAX_POS; };
+    auto helped = [](int p) { return LONG && OWN && p + 1 > MK_MAX_POS && p + 1 <= MK_HMAX; };
     auto issue_kw = [&](int u, int nl, int npos) {
         if (tid == MK_THREADS - 32) {
-            const bool tl = tiled(npos);
+            const bool hp = helped(npos);
+            const bool tl = tiled(npos) && !hp;
             const bool pk = packed(npos);
-            const int nk = tl ? MK_TP : npos;
+            // helped: the own slice, positions [c0, npos), K at row 0, V at row npos + 1 - c0
+            const int c0 = hp ? MK_HPH * mk_hslice(npos + 1) : 0;
+            const int nk = hp ? npos - c0 : (tl ? MK_TP : npos);
             const unsigned rb = (unsigned) nk * T3B_HD * 2;
-            const __half * kb = a.kv + (size_t) nl * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
+            const __half * kb = a.kv + (size_t) nl * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD + (size_t) c0 * T3B_HD;
             mk_fence_proxy_async();   // K/V rows this CTA stored (generic proxy) are read by the bulk copy
-            mk_mbar_expect(&mbar[0], (pk || tl ? 2u : 1u) * rb + MK_QKVW_BYTES);
+            mk_mbar_expect(&mbar[0], (pk || tl || hp ? 2u : 1u) * rb + MK_QKVW_BYTES);
             if (nk > 0) {
                 mk_bulk_g2s(kst, kb, rb, &mbar[0]);
-                if (tl) mk_bulk_g2s(kst + (size_t) MK_TP * T3B_HD, kb + a.v_off, rb, &mbar[0]);
+                if (hp) mk_bulk_g2s(kst + (size_t) (nk + 1) * T3B_HD, kb + a.v_off, rb, &mbar[0]);
+                else if (tl) mk_bulk_g2s(kst + (size_t) MK_TP * T3B_HD, kb + a.v_off, rb, &mbar[0]);
                 else if (pk) mk_bulk_g2s(kst + (size_t) (npos + 1) * T3B_HD, kb + a.v_off, rb, &mbar[0]);
             }
             mk_bulk_qkvw(qkvw, a.layers[nl].qkv, hh_, &mbar[0]);
@@ -1188,6 +1362,25 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                 // rows from the staged weights, then append K/V at pos
                 const MkLn lp = mk_ln_prefetch(Ly.ln1g, Ly.ln1b);
                 const float bq = att && tid < 3 * T3B_HD ? __ldg(Ly.bqkv + (tid >> 6) * D + hh_ * T3B_HD + (tid & 63)) : 0.0f;
+                const bool hwork = helper && helped(pos);
+                const int hC = hwork ? mk_hslice(pos + 1) : 0;
+                const int hn = hC;   // a helper's slice is full: MK_HPH C < pos
+                if (hwork) {
+                    // this layer's q rows of the head and the slice's K/V rows
+                    // (positions [j C, (j + 1) C), all cached) into the free
+                    // stages: K rows at kst, V rows after them, q rows at vst
+                    if (tid == MK_THREADS - 32) {
+                        const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) hh_h * a.max_ctx * T3B_HD +
+                                            (size_t) hj_h * hC * T3B_HD;
+                        const unsigned rb = (unsigned) hn * T3B_HD * 2;
+                        mk_fence_proxy_async();   // the stages were last read by generic loads
+                        mk_mbar_expect(&mbar[6], 2u * rb + (unsigned) MK_QKVW_SEC);
+                        mk_bulk_g2s(kst, kb, rb, &mbar[6]);
+                        mk_bulk_g2s(kst + (size_t) hn * T3B_HD, kb + a.v_off, rb, &mbar[6]);
+                        mk_bulk_g2s_w(qkvw, Ly.qkv.w + (size_t) hh_h * T3B_HD * MK_QKVW_ROW, (unsigned) MK_QKVW_SEC, &mbar[6]);
+                    }
+                    CP_ISSUE_NEXT(6, 18);
+                }
                 MK_STAMP(l * MK_TLL + 0);
                 float2 xv;
                 if (l > 0 && LLX) {
@@ -1201,6 +1394,20 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     xv = *(const float2 *) (xres + 2 * tid);
                 }
                 MK_STAMP(l * MK_TLL + 1);
+                if (hwork) {
+                    mk_ln_quant(xv.x, xv.y, lp, a.eps, redd, act, false);
+                    if (tid == 0) {
+                        const bool ok = mk_mbar_wait(&mbar[6], CP_PAR(6), a.spin);
+                        if (!ok) { atomicOr(a.err, T3B_DEVERR_TIMEOUT); atomicExch(a.abort_flag, 1); }
+                        okf = ok;
+                    }
+                    __syncthreads();
+                    if (!okf) MK_BAIL;
+                    CP_DONE(6);
+                    mk_help(qkvw, act, Ly.bqkv + hh_h * T3B_HD, hn, kst, kst + (size_t) hn * T3B_HD, att_s, (float *) redd,
+                            (unsigned long long *) (a.buf + MK_B_HR) + (size_t) (hh_h * MK_HPH + hj_h) * MK_HR_WORDS,
+                            mk_xtag(a.epoch, k));
+                }
                 if (att) {
                     float * qkvh = att_s;   // [192]
                     const __half * kb = a.kv + (size_t) l * a.layer_stride + (size_t) hh_ * a.max_ctx * T3B_HD;
@@ -1220,7 +1427,9 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                     MK_STAMP(l * MK_TLL + 15);
                     const bool pk = packed(pos);
                     __half * vrow = pk ? kst + (size_t) (pos + 1) * T3B_HD : vst;
-                    if (tiled(pos)) {
+                    if (helped(pos)) {
+                        // the own slice (and its V rows) came with the weights
+                    } else if (tiled(pos)) {
                         // tile 0 came with the weights; tile 1 replaces them
                         cp = mk_issue_tile(cp, 1, pos, kb, a.v_off, true, kst, vst, mbar);
                     } else if (!pk) {
@@ -1231,7 +1440,7 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             mk_mbar_expect(&mbar[1], (unsigned) pos * T3B_HD * 2);
                             if (pos > 0) mk_bulk_g2s(vst, kb + a.v_off, (unsigned) pos * T3B_HD * 2, &mbar[1]);
                         }
-                        CP_ISSUE_NEXT(1, 12);
+                        CP_ISSUE_NEXT(1, 16);
                     }
                     MK_STAMP(l * MK_TLL + 16);
                     if (tid < 3 * T3B_HD) {
@@ -1242,6 +1451,10 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             const __half hv = __float2half_rn(v);
                             (vv ? (__half *) (kb + a.v_off) : (__half *) kb)[(size_t) pos * T3B_HD + c] = hv;
                             if (!tiled(pos)) (vv ? vrow : kst)[(size_t) pos * T3B_HD + c] = hv;
+                            else if (helped(pos)) {
+                                const int c0 = MK_HPH * mk_hslice(pos + 1), lo = pos + 1 - c0;
+                                kst[(size_t) ((vv ? lo : 0) + pos - c0) * T3B_HD + c] = hv;
+                            }
                         }
                     }
                     __syncthreads();
@@ -1395,6 +1608,15 @@ __global__ __launch_bounds__(MK_THREADS, 1) void t3_decode_megakernel(MegaArgs a
                             o0.x = fmaf(p0, v0.x, o0.x); o0.y = fmaf(p0, v0.y, o0.y);
                         }
                     }
+                } else if (helped(pos)) {
+                    // own slice + the helpers' results (out of line)
+                    const int c0 = MK_HPH * mk_hslice(pos + 1);
+                    lsum = mk_attend_helped(pos + 1 - c0, qkvh, kst, pw, rf, att_s + 256 + MK_MAX_POS,
+                                            (float *) (smem + MK_ATT_BYTES),
+                                            (const unsigned long long *) (a.buf + MK_B_HR) + (size_t) h * MK_HPH * MK_HR_WORDS,
+                                            mk_xtag(a.epoch, k), a.spin, a.err, a.abort_flag, &okf);
+                    if (lsum < 0.0f) MK_BAIL;
+                    MK_STAMP(l * MK_TLL + 9);
                 } else {
                     // L > MK_MAX_POS: K/V streamed in tiles (out of line)
                     lsum = mk_attend_tiled(&cp, OWN, pos, kb, a.v_off, qkvh, kst, vst, pw, rf, att_s + 256 + MK_MAX_POS,
