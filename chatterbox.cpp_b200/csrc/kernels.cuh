@@ -262,36 +262,38 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], const int (&a)[4], int b0, i
                      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-template <int WT>
+template <int WT, int BM>
 __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         const uint8_t * __restrict__ W, int N, int K, int rb,
         const int8_t * __restrict__ xq, const float * __restrict__ xd, const int * __restrict__ xs,
         int M, GemvEpi e) {
     constexpr int QB = WT == T3B_Q4_0 ? 16 : 32;          // weight bytes per block
-    __shared__ __align__(16) int8_t As[2][GQ_BM][GQ_AROW];
-    __shared__ __align__(16) uint8_t Bs[2][GQ_BN][GQ_BROW];
-    __shared__ __align__(16) float Ds[2][GQ_BM][GQ_KB];   // activation block scales
-    __shared__ __align__(16) int Ss[2][GQ_BM][GQ_KB];     // activation block sums (Q4_0)
-    __shared__ __align__(16) __half Dw[2][GQ_BN][GQ_KB];  // weight block scales
+    constexpr int MT = BM / 32;                           // 16-row MMA tiles per warp (warps 2 x 2)
+    constexpr int NS = BM == 32 ? 4 : 3;                  // cp.async stages in flight (static smem <= 48 KB)
+    __shared__ __align__(16) int8_t As[NS][BM][GQ_AROW];
+    __shared__ __align__(16) uint8_t Bs[NS][GQ_BN][GQ_BROW];
+    __shared__ __align__(16) float Ds[NS][BM][GQ_KB];   // activation block scales
+    __shared__ __align__(16) int Ss[NS][BM][GQ_KB];     // activation block sums (Q4_0)
+    __shared__ __align__(16) __half Dw[NS][GQ_BN][GQ_KB];  // weight block scales
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int wm = warp >> 1, wn = warp & 1;
-    const int m0 = blockIdx.y * GQ_BM, n0 = blockIdx.x * GQ_BN;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * GQ_BN;
     const int nb = K / 32;
     const int nstage = nb / GQ_KB;
 
     auto load_stage = [&](int s, int st) {
         const int kb = st * GQ_KB;                         // first block of the stage
-        // activations: 64 rows x 128 bytes = 512 chunks of 16 bytes
+        // activations: BM rows x 128 bytes = 8 BM chunks of 16 bytes
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < BM / 16; ++u) {
             const int c = tid + u * 128;
             const int r = c >> 3, q = c & 7;
             const bool ok = m0 + r < M;
             cp_async16(&As[s][r][q * 16], xq + (size_t) (ok ? m0 + r : 0) * K + kb * 32 + q * 16, ok);
         }
-        // activation scales and sums: 64 rows x 16 bytes each
-        if (tid < 64) {
+        // activation scales and sums: BM rows x 16 bytes each
+        if (tid < BM) {
             const bool ok = m0 + tid < M;
             const size_t o = (size_t) (ok ? m0 + tid : 0) * nb + kb;
             cp_async16(&Ds[s][tid][0], xd + o, ok);
@@ -316,30 +318,35 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    float acc[2][2][4];
+    float acc[MT][2][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < MT; ++i)
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
             for (int k = 0; k < 4; ++k) acc[i][j][k] = 0.0f;
 
-    load_stage(0, 0);
+    // NS - 1 stages in flight ahead of the one being consumed; every
+    // iteration commits one group (empty at the tail), so "all but the
+    // newest NS - 1 groups" is always the current stage
+#pragma unroll
+    for (int p = 0; p < NS - 1; ++p) {
+        if (p < nstage) load_stage(p, p);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     for (int st = 0; st < nstage; ++st) {
-        const int s = st & 1;
-        if (st + 1 < nstage) {
-            load_stage(s ^ 1, st + 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
+        const int s = st % NS;
+        if (st + NS - 1 < nstage) load_stage((st + NS - 1) % NS, st + NS - 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        if (NS == 4) asm volatile("cp.async.wait_group 3;" ::: "memory");
+        else asm volatile("cp.async.wait_group 2;" ::: "memory");
         __syncthreads();
 #pragma unroll
         for (int bb = 0; bb < GQ_KB; ++bb) {
-            int a[2][4];
+            int a[MT][4];
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const int r = wm * 32 + mt * 16 + g;
+            for (int mt = 0; mt < MT; ++mt) {
+                const int r = wm * (16 * MT) + mt * 16 + g;
                 a[mt][0] = *(const int *) &As[s][r][bb * 32 + t * 4];
                 a[mt][1] = *(const int *) &As[s][r + 8][bb * 32 + t * 4];
                 a[mt][2] = *(const int *) &As[s][r][bb * 32 + 16 + t * 4];
@@ -360,8 +367,8 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
                 }
             }
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const int r0 = wm * 32 + mt * 16 + g;
+            for (int mt = 0; mt < MT; ++mt) {
+                const int r0 = wm * (16 * MT) + mt * 16 + g;
                 const float dx0 = Ds[s][r0][bb], dx1 = Ds[s][r0 + 8][bb];
                 int sx0 = 0, sx1 = 0;
                 if (WT == T3B_Q4_0) { sx0 = 8 * Ss[s][r0][bb]; sx1 = 8 * Ss[s][r0 + 8][bb]; }
@@ -384,21 +391,21 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
     if (e.qx) {
         // bias + GELU, then Q8_0 of each row's 32-wide block (this CTA's
         // columns are exactly one block): the tile goes through shared memory
-        float (*Tt)[GQ_BN + 1] = (float (*)[GQ_BN + 1]) & As[0][0][0];   // 64 x 33 floats fit in As[0]
+        float (*Tt)[GQ_BN + 1] = (float (*)[GQ_BN + 1]) & As[0][0][0];   // BM x 33 floats fit in As[0]
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const int ml = wm * 32 + mt * 16 + g + (i >> 1) * 8;
+                    const int ml = wm * (16 * MT) + mt * 16 + g + (i >> 1) * 8;
                     const int nl = wn * 16 + nt * 8 + 2 * t + (i & 1);
                     const float b = e.bias ? e.bias[n0 + nl] : 0.0f;
                     Tt[ml][nl] = gelu_ggml(e.bias ? __fadd_rn(acc[mt][nt][i], b) : acc[mt][nt][i]);
                 }
         __syncthreads();
         const int nbk = e.qK / 32;
-        for (int ml = warp * 16; ml < warp * 16 + 16; ++ml) {
+        for (int ml = warp * (BM / 4); ml < warp * (BM / 4) + BM / 4; ++ml) {
             const int m = m0 + ml;
             if (m >= M) break;   // uniform over the warp
             const float v = Tt[ml][lane];
@@ -420,14 +427,14 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
     // epilogue's code instead of sixteen unrolled ones
     float (*Tt)[GQ_BN + 1] = (float (*)[GQ_BN + 1]) & As[0][0][0];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                Tt[wm * 32 + mt * 16 + g + (i >> 1) * 8][wn * 16 + nt * 8 + 2 * t + (i & 1)] = acc[mt][nt][i];
+                Tt[wm * (16 * MT) + mt * 16 + g + (i >> 1) * 8][wn * 16 + nt * 8 + 2 * t + (i & 1)] = acc[mt][nt][i];
     __syncthreads();
-    const int rows = min(GQ_BM, M - m0);
+    const int rows = min(BM, M - m0);
 #pragma unroll 1
     for (int q = threadIdx.x; q < rows * GQ_BN; q += blockDim.x) {
         const int r = q / GQ_BN, c = q % GQ_BN;

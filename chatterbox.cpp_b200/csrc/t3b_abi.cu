@@ -289,8 +289,14 @@ template <int WT>
 void launch_gemv_q(const Mat & W, const int8_t * xq, const float * xd, const int * xs, int M, const GemvEpi & e,
                    cudaStream_t st) {
     if (M >= 16 && W.K % (32 * GQ_KB) == 0) {   // many rows: int8 tensor-core GEMM
-        dim3 grid((W.N + GQ_BN - 1) / GQ_BN, (M + GQ_BM - 1) / GQ_BM);
-        gemm_q_mma_kernel<WT><<<grid, 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd, xs, M, e);
+        // 32-row tiles when 64-row ones would leave SMs idle (N = 1024: 64 CTAs at M = 128)
+        const int tx = (W.N + GQ_BN - 1) / GQ_BN;
+        if (tx * ((M + GQ_BM - 1) / GQ_BM) < 148) {
+            gemm_q_mma_kernel<WT, 32><<<dim3(tx, (M + 31) / 32), 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd, xs, M, e);
+        } else {
+            gemm_q_mma_kernel<WT, GQ_BM><<<dim3(tx, (M + GQ_BM - 1) / GQ_BM), 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd,
+                                                                                       xs, M, e);
+        }
         return;
     }
     if (M <= 1) launch_gemv_q_t<WT, 1>(W, xq, xd, xs, M, e, st);
