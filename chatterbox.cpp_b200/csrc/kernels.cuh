@@ -556,6 +556,13 @@ __global__ __launch_bounds__(256) void gemv_prep_kernel(
             }
         }
 
+    // launched with programmatic stream serialization: the weight loads above
+    // overlap the previous kernel's tail; everything it writes (x, the
+    // residual, the caches) is read only after this wait.  The next kernel
+    // may start its own prologue now.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
     // (2) activation prep of rows m0 .. m0 + mt - 1 (prep_act_kernel per row)
     for (int m = 0; m < mt; ++m) {
         const float * xr = x + (size_t) (m0 + m) * ldx;

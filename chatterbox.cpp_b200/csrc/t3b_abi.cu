@@ -409,8 +409,22 @@ bool launch_gemv_prep_t(const Mat & W, const float * x, int ldx, int M, const fl
             ready[dev] = true;
         }
     }
-    dim3 grid((W.N + 8 * RPW - 1) / (8 * RPW), (M + MT - 1) / MT);
-    gemv_prep_kernel<WT, MT, RPW><<<grid, 256, smem, st>>>(W.p, W.N, W.K, W.rb, x, ldx, g, b, eps, M, e);
+    // programmatic stream serialization: the kernel waits for its predecessor
+    // (griddepcontrol.wait) only after issuing its weight loads
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((W.N + 8 * RPW - 1) / (8 * RPW), (M + MT - 1) / MT);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gemv_prep_kernel<WT, MT, RPW>, W.p, W.N, W.K, W.rb, x, ldx, g, b, eps, M, e) != cudaSuccess) {
+        cudaGetLastError();
+        gemv_prep_kernel<WT, MT, RPW><<<cfg.gridDim, 256, smem, st>>>(W.p, W.N, W.K, W.rb, x, ldx, g, b, eps, M, e);
+    }
     return true;
 }
 template <int WT>
