@@ -285,10 +285,15 @@ void launch_gemv_h_t(const Mat & W, const __half * xh, int M, const GemvEpi & e,
     const size_t smem = (size_t) MT * W.K * 2;
     gemv_f16_kernel<MT, RPW><<<grid, 256, smem, st>>>((const __half *) W.p, W.N, W.K, xh, M, e);
 }
+// activation rows from which quantised weights go through gemm_q_mma_kernel
+// (M <= 4 run the one-launch GEMV): at M = 8 the GEMM with 32-row tiles takes
+// about half the time of gemv_q_kernel, and it adds the per-block terms in
+// block order, as ggml's dot does
+#define GQ_MIN_M 5
 template <int WT>
 void launch_gemv_q(const Mat & W, const int8_t * xq, const float * xd, const int * xs, int M, const GemvEpi & e,
                    cudaStream_t st) {
-    if (M >= 16 && W.K % (32 * GQ_KB) == 0) {   // many rows: int8 tensor-core GEMM
+    if (M >= GQ_MIN_M && W.K % (32 * GQ_KB) == 0) {   // several rows: int8 tensor-core GEMM
         // 32-row tiles when 64-row ones would leave SMs idle (N = 1024: 64 CTAs at M = 128)
         const int tx = (W.N + GQ_BN - 1) / GQ_BN;
         if (tx * ((M + GQ_BM - 1) / GQ_BM) < 148) {
@@ -389,10 +394,9 @@ void launch_gemv(const Mat & W, const int8_t * xq, const float * xd, const int *
 // caller then runs prep_act_kernel + launch_gemv.
 #define GP_MAX_M 5   // from 5 rows the per-CTA prep of every row costs more than the second launch (measured)
 #define GP_SMEM_MAX (200u * 1024u)   // dynamic bytes (the static arrays and the 227 KB opt-in limit leave room)
-template <int WT, int MT>
+template <int WT, int MT, int RPW>
 bool launch_gemv_prep_t(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
                         const GemvEpi & e, cudaStream_t st) {
-    constexpr int RPW = 2;
     const size_t smem = gemv_prep_smem(WT, MT, W.K);
     static std::mutex mu;
     static bool ready[64] = {false};
@@ -427,12 +431,19 @@ bool launch_gemv_prep_t(const Mat & W, const float * x, int ldx, int M, const fl
     }
     return true;
 }
+template <int WT, int MT>
+bool launch_gemv_prep_r(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
+                        const GemvEpi & e, cudaStream_t st) {
+    // one row per warp when two would leave SMs idle (N = 1024: 128 CTAs, not 64)
+    if ((W.N + 15) / 16 < 148) return launch_gemv_prep_t<WT, MT, 1>(W, x, ldx, M, g, b, eps, e, st);
+    return launch_gemv_prep_t<WT, MT, 2>(W, x, ldx, M, g, b, eps, e, st);
+}
 template <int WT>
 bool launch_gemv_prep_w(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
                         const GemvEpi & e, cudaStream_t st) {
-    if (M <= 1) return launch_gemv_prep_t<WT, 1>(W, x, ldx, M, g, b, eps, e, st);
-    if (M <= 2) return launch_gemv_prep_t<WT, 2>(W, x, ldx, M, g, b, eps, e, st);
-    return launch_gemv_prep_t<WT, 4>(W, x, ldx, M, g, b, eps, e, st);
+    if (M <= 1) return launch_gemv_prep_r<WT, 1>(W, x, ldx, M, g, b, eps, e, st);
+    if (M <= 2) return launch_gemv_prep_r<WT, 2>(W, x, ldx, M, g, b, eps, e, st);
+    return launch_gemv_prep_r<WT, 4>(W, x, ldx, M, g, b, eps, e, st);
 }
 bool launch_gemv_prep(const Mat & W, const float * x, int ldx, int M, const float * g, const float * b, float eps,
                       const GemvEpi & e, cudaStream_t st) {
@@ -490,10 +501,11 @@ void run_layers(t3b_ctx * ctx, int M, const int * row_of, const int * pos, int h
             if (!q_attn) launch_prep(ctx, ctx->attn, D, M, D, nullptr, nullptr, Ly.proj.type, st);
             launch_gemv(Ly.proj, ctx->xq, ctx->xd, ctx->xs, ctx->xh, M, ep, st, &ctx->gws);
         }
-        // LN2 + fc + GELU; with the tensor-core GEMM (M >= 16) its epilogue
-        // writes fc2's Q8_0 input (separate buffers: fc is still reading xq)
+        // LN2 + fc + GELU; with the tensor-core GEMM (M >= GQ_MIN_M) its
+        // epilogue writes fc2's Q8_0 input (separate buffers: fc is still
+        // reading xq)
         GemvEpi ef = epi_plain(EPI_GELU, ctx->h, 4 * D, Ly.fc_b, nullptr, 0);
-        const bool q_fc = M >= 16 && Ly.fc.type != T3B_F16 && Ly.fc2.type != T3B_F16 &&
+        const bool q_fc = M >= GQ_MIN_M && Ly.fc.type != T3B_F16 && Ly.fc2.type != T3B_F16 &&
                           Ly.fc.K % (32 * GQ_KB) == 0 && (4 * D) % GQ_BN == 0;
         if (q_fc) { ef.qx = ctx->xq2; ef.qd = ctx->xd2; ef.qs = ctx->xs2; ef.qK = 4 * D; }
         if (q_fc || !launch_gemv_prep(Ly.fc, ctx->x, D, M, Ly.ln2g, Ly.ln2b, eps, ef, st)) {

@@ -102,8 +102,8 @@ def test_gemv_matches_oracle(pkg, orc, ty, KN, M):
         # oracle's can land on the neighbouring f16 (2^-11 relative)
         tol = 1e-3 if epi == 1 else 2e-4
         assert rel_err(y, ref) < tol, (ty, K, N, M, epi)
-        if ty != 1 and M >= 16 and epi == 0:
-            # the tensor-core GEMM (M >= 16) adds the per-block terms in block
+        if ty != 1 and M >= 5 and epi == 0:
+            # the tensor-core GEMM (M >= 5) adds the per-block terms in block
             # order, as the oracle's restatement of ggml's dot does: identical
             assert np.array_equal(y, ref), (ty, K, N, M, float(np.abs(y - ref).max()))
 
