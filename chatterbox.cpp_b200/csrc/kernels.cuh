@@ -462,6 +462,9 @@ __global__ __launch_bounds__(256) void gemv_f16_kernel(
     for (int i = 0; i < RPW; ++i)
 #pragma unroll
         for (int m = 0; m < MT; ++m) acc[i][m] = 0.0f;
+    // unrolled: the weight loads of four chunks per row are in flight at once
+    // (K = 4096 is 16 chunks per lane; one at a time they were 16 round trips)
+#pragma unroll 4
     for (int c = lane; c < K / 8; c += 32) {
 #pragma unroll
         for (int i = 0; i < RPW; ++i) {

@@ -278,12 +278,17 @@ void launch_gemv_q_t(const Mat & W, const int8_t * xq, const float * xd, const i
     const size_t smem = (size_t) MT * W.K + (size_t) MT * (W.K / 32) * 8;
     gemv_q_kernel<WT, MT, RPW><<<grid, 256, smem, st>>>(W.p, W.N, W.K, W.rb, xq, xd, xs, M, e);
 }
-template <int MT>
-void launch_gemv_h_t(const Mat & W, const __half * xh, int M, const GemvEpi & e, cudaStream_t st) {
-    constexpr int RPW = 2;
+template <int MT, int RPW>
+void launch_gemv_h_r(const Mat & W, const __half * xh, int M, const GemvEpi & e, cudaStream_t st) {
     dim3 grid((W.N + 8 * RPW - 1) / (8 * RPW), (M + MT - 1) / MT);
     const size_t smem = (size_t) MT * W.K * 2;
     gemv_f16_kernel<MT, RPW><<<grid, 256, smem, st>>>((const __half *) W.p, W.N, W.K, xh, M, e);
+}
+template <int MT>
+void launch_gemv_h_t(const Mat & W, const __half * xh, int M, const GemvEpi & e, cudaStream_t st) {
+    // one row per warp when two would leave SMs idle
+    if ((W.N + 15) / 16 * ((M + MT - 1) / MT) < 148) launch_gemv_h_r<MT, 1>(W, xh, M, e, st);
+    else launch_gemv_h_r<MT, 2>(W, xh, M, e, st);
 }
 // activation rows from which quantised weights go through gemm_q_mma_kernel
 // (M <= 4 run the one-launch GEMV): at M = 8 the GEMM with 32-row tiles takes
