@@ -61,6 +61,46 @@ __device__ __forceinline__ void epi_store(const GemvEpi & e, int m, int n, float
 // backend does to src1 before a quantised / f16 mul_mat.
 // One CTA of 256 threads per row; dynamic smem = K floats.
 // ---------------------------------------------------------------------------
+// rows x n floats from global memory (row stride ld) into shared memory
+// (row stride n), by the whole block, with four loads per thread in flight
+// (16-byte ones when every row start is 16-byte aligned): one memory round
+// trip for up to 4 * blockDim.x loads, where a plain strided loop waits on
+// each of its K / blockDim.x iterations in turn.
+__device__ __forceinline__ void rows_to_smem(float * dst, const float * __restrict__ src, int ld, int rows, int n) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    if (((((uintptr_t) src) | ((uintptr_t) dst)) & 15) == 0 && (n & 3) == 0 && (ld & 3) == 0) {
+        const int n4 = n >> 2, tot = rows * n4;
+        for (int q0 = tid; q0 < tot; q0 += 4 * nth) {
+            float4 t[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * nth;
+                if (q < tot) t[u] = *(const float4 *) (src + (size_t) (q / n4) * ld + 4 * (q % n4));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * nth;
+                if (q < tot) ((float4 *) dst)[q] = t[u];
+            }
+        }
+    } else {
+        const int tot = rows * n;
+        for (int q0 = tid; q0 < tot; q0 += 4 * nth) {
+            float t[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * nth;
+                if (q < tot) t[u] = src[(size_t) (q / n) * ld + q % n];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * nth;
+                if (q < tot) dst[q] = t[u];
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ double block_sum_d(double v, double * red) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
@@ -79,11 +119,10 @@ __global__ __launch_bounds__(256) void prep_act_kernel(
         const float * __restrict__ b, float eps, int qmode,
         int8_t * __restrict__ xq, float * __restrict__ xd, int * __restrict__ xs,
         __half * __restrict__ xh) {
-    extern __shared__ float row[];
+    extern __shared__ __align__(16) float row[];
     __shared__ double redd[32];
     const int m = blockIdx.x, tid = threadIdx.x;
-    const float * xr = x + (size_t) m * ldx;
-    for (int i = tid; i < K; i += blockDim.x) row[i] = xr[i];
+    rows_to_smem(row, x + (size_t) m * ldx, ldx, 1, K);
     __syncthreads();
     if (g) {
         double s = 0.0;
@@ -98,7 +137,8 @@ __global__ __launch_bounds__(256) void prep_act_kernel(
         s2 = block_sum_d(s2, redd);
         const float var = (float) (s2 / K);
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        for (int i = tid; i < K; i += blockDim.x) {
+#pragma unroll 4
+        for (int i = tid; i < K; i += blockDim.x) {   // unrolled: the g / b loads of 4 iterations in flight
             const float v = __fsub_rn(row[i], mean);
             row[i] = __fadd_rn(__fmul_rn(__fmul_rn(v, scale), g[i]), b[i]);
         }
@@ -567,10 +607,7 @@ __global__ __launch_bounds__(256) void gemv_prep_kernel(
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // (2) activation prep of rows m0 .. m0 + mt - 1 (prep_act_kernel per row)
-    for (int m = 0; m < mt; ++m) {
-        const float * xr = x + (size_t) (m0 + m) * ldx;
-        for (int i = tid; i < K; i += blockDim.x) rows[(size_t) m * K + i] = xr[i];
-    }
+    rows_to_smem(rows, x + (size_t) m0 * ldx, ldx, mt, K);
     __syncthreads();
     if (g) {
         double s[MT];
@@ -602,7 +639,8 @@ __global__ __launch_bounds__(256) void gemv_prep_kernel(
         for (int m = 0; m < MT; ++m) {
             s[m] = 0.0;
             if (m < mt)
-                for (int i = tid; i < K; i += blockDim.x) {
+#pragma unroll 4
+                for (int i = tid; i < K; i += blockDim.x) {   // the g / b loads of 4 iterations in flight
                     const float v = __fsub_rn(rows[(size_t) m * K + i], mean[m]);
                     s[m] += (double) __fmul_rn(v, v);
                 }
@@ -929,16 +967,31 @@ __global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_consta
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"((unsigned) TF_BN) : "memory");
     }
-    const int m = m0 + tid;
-    const bool mrow = m < p.M && tf_ok;
+    // the accumulator row of this thread goes into a padded shared tile (the
+    // ring is free: the MMAs that read it completed before the accumulator
+    // was read); the split partials and the epilogue are then written and
+    // read from it in coalesced order
+    const int rows = min(TF_BM, p.M - m0);
+    float * tile_s = (float *) As;   // [TF_BM][TF_BN + 1]
+#pragma unroll
+    for (int j = 0; j < TF_BN; ++j) tile_s[tid * (TF_BN + 1) + j] = v[j];
+    __syncthreads();
     if (p.splits > 1) {
         // partial tile of this split: [split][M][ldw] with the row padded to
-        // a multiple of TF_BN columns, written and read as float4
+        // a multiple of TF_BN columns; a warp moves two rows of 64 columns
+        // per float4 instruction (256 contiguous bytes each)
+        constexpr int C4 = TF_BN / 4;                       // float4 per tile row
+        constexpr int PT = TF_BM * C4 / TF_BM;              // float4 per thread (16)
         const int ldw = (p.N + TF_BN - 1) / TF_BN * TF_BN;
-        if (mrow) {
-            float4 * w = (float4 *) (p.ws + ((size_t) split * p.M + m) * ldw + n0);
+        if (tf_ok) {
 #pragma unroll
-            for (int j = 0; j < TF_BN / 4; ++j) w[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < PT; ++j) {
+                const int q = tid + j * TF_BM, r = q / C4, c = (q % C4) * 4;
+                if (r < rows) {
+                    const float * t = tile_s + r * (TF_BN + 1) + c;
+                    *(float4 *) (p.ws + ((size_t) split * p.M + m0 + r) * ldw + n0 + c) = make_float4(t[0], t[1], t[2], t[3]);
+                }
+            }
         }
         __threadfence();
         __syncthreads();
@@ -947,34 +1000,37 @@ __global__ __launch_bounds__(128, 1) void gemm_f16_tc_kernel(const __grid_consta
         __syncthreads();
         if (!tf_last) return;
         __threadfence();
-        if (mrow) {
-            // splits added in split order; every column of a split in flight at once
+        // splits added in split order (0 + s0 + s1 + ...), each thread's 16
+        // float4 of a split in flight at once
+        float4 a4[PT];
 #pragma unroll
-            for (int j = 0; j < TF_BN; ++j) v[j] = 0.0f;
-            for (int sp = 0; sp < p.splits; ++sp) {
-                const float4 * w = (const float4 *) (p.ws + ((size_t) sp * p.M + m) * ldw + n0);
-                float4 t[TF_BN / 4];
+        for (int j = 0; j < PT; ++j) a4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < p.splits; ++sp) {
+            float4 t4[PT];
 #pragma unroll
-                for (int j = 0; j < TF_BN / 4; ++j) t[j] = __ldcg(w + j);
+            for (int j = 0; j < PT; ++j) {
+                const int q = tid + j * TF_BM, r = q / C4, c = (q % C4) * 4;
+                t4[j] = r < rows ? __ldcg((const float4 *) (p.ws + ((size_t) sp * p.M + m0 + r) * ldw + n0 + c))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-                for (int j = 0; j < TF_BN / 4; ++j) {
-                    v[4 * j] += t[j].x; v[4 * j + 1] += t[j].y; v[4 * j + 2] += t[j].z; v[4 * j + 3] += t[j].w;
-                }
+            for (int j = 0; j < PT; ++j) {
+                a4[j].x += t4[j].x; a4[j].y += t4[j].y; a4[j].z += t4[j].z; a4[j].w += t4[j].w;
             }
         }
         if (tid == 0) p.cnt[tile] = 0u;
-    }
-    // epilogue through shared memory (the ring is free): row m's 64 values
-    // into a padded tile, then each warp stores 32 consecutive columns of a
-    // row at a time (coalesced), with one copy of the epilogue's code rather
-    // than 64 unrolled ones, which the CTA would fetch cold exactly once
-    // (the MMAs that read the ring completed before the accumulator was read)
-    if (!tf_ok) return;              // CTA-uniform
-    float * tile_s = (float *) As;   // [TF_BM][TF_BN + 1]
 #pragma unroll
-    for (int j = 0; j < TF_BN; ++j) tile_s[tid * (TF_BN + 1) + j] = v[j];
-    __syncthreads();
-    const int rows = min(TF_BM, p.M - m0);
+        for (int j = 0; j < PT; ++j) {
+            const int q = tid + j * TF_BM, r = q / C4, c = (q % C4) * 4;
+            float * t = tile_s + r * (TF_BN + 1) + c;
+            t[0] = a4[j].x; t[1] = a4[j].y; t[2] = a4[j].z; t[3] = a4[j].w;
+        }
+        __syncthreads();
+    }
+    // epilogue: each warp stores 32 consecutive columns of a row at a time,
+    // with one copy of the epilogue's code rather than 64 unrolled ones,
+    // which the CTA would fetch cold exactly once
+    if (!tf_ok) return;              // CTA-uniform
 #pragma unroll 1
     for (int q = tid; q < rows * TF_BN; q += TF_BM) {
         const int r = q / TF_BN, c = q % TF_BN;
