@@ -1266,20 +1266,27 @@ __global__ __launch_bounds__(128) void attn_rows_kernel(AttnArgs a) {
     for (int i = 0; i < 8; ++i) o[i] = 0.0f;
     // the loop bound is uniform over the warp (every lane reaches every
     // shuffle); a group whose key is past L contributes nothing.  Each group
-    // takes keys j, j+16, j+32, j+48: eight 16-byte loads in flight per lane.
+    // takes keys j, j+16, j+32, j+48: eight 16-byte loads per lane, and the
+    // next iteration's eight are issued before this one's arithmetic, so the
+    // memory latency overlaps the dots, the softmax and the P.V update.
     constexpr int U = 4;
-    for (int jb = w * 4; jb < L; jb += 16 * U) {
-        const int j = jb + grp;
-        uint4 kk[U], vv[U];
+    uint4 kk[U], vv[U];
+    auto fetch = [&](int jn, uint4 (&kd)[U], uint4 (&vd)[U]) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            kk[u] = make_uint4(0u, 0u, 0u, 0u);
-            vv[u] = kk[u];
-            if (j + 16 * u < L) {
-                kk[u] = __ldg((const uint4 *) (kb + (size_t) (j + 16 * u) * T3B_HD));
-                vv[u] = __ldg((const uint4 *) (vb + (size_t) (j + 16 * u) * T3B_HD));
+            kd[u] = make_uint4(0u, 0u, 0u, 0u);
+            vd[u] = kd[u];
+            if (jn + 16 * u < L) {
+                kd[u] = __ldg((const uint4 *) (kb + (size_t) (jn + 16 * u) * T3B_HD));
+                vd[u] = __ldg((const uint4 *) (vb + (size_t) (jn + 16 * u) * T3B_HD));
             }
         }
+    };
+    fetch(w * 4 + grp, kk, vv);
+    for (int jb = w * 4; jb < L; jb += 16 * U) {
+        const int j = jb + grp;
+        uint4 kn[U], vn[U];
+        fetch(j + 16 * U, kn, vn);
         float d[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -1324,6 +1331,8 @@ __global__ __launch_bounds__(128) void attn_rows_kernel(AttnArgs a) {
             }
         }
         mx = nm;
+#pragma unroll
+        for (int u = 0; u < U; ++u) { kk[u] = kn[u]; vv[u] = vn[u]; }
     }
     // merge the four groups of the warp (lanes c, c+8, c+16, c+24 hold the same dims)
 #pragma unroll
