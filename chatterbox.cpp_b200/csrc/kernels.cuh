@@ -265,11 +265,13 @@ __global__ __launch_bounds__(256) void gemv_q_kernel(
 // accumulated in registers in block order.  Per-32 f16 scales force a
 // rescale after every K = 32 step, which is why the accumulators live in
 // registers rather than in tensor memory.
-// CTA = 4 warps (2 x 2), CTA tile 64 activation rows x 32 weight rows, warp
-// tile 32 x 16 (2 x 2 MMA tiles).  K is staged four blocks (128 elements)
-// at a time in two cp.async buffers; smem rows are padded by 16 bytes so
-// the fragment loads of a warp hit 32 distinct banks.
-// grid = (ceil(N / 32), ceil(M / 64)).
+// CTA tile BM (64 or 32) activation rows x 32 weight rows; WARPS warps, two
+// along M and WARPS / 2 along N: 4 warps with 32 x 16 / 16 x 16 warp tiles,
+// or 8 warps with 16 x 8 ones (one MMA tile each, for the 32-row tile when
+// one CTA per SM would leave the schedulers idle).  K is staged four blocks
+// (128 elements) at a time in NS cp.async buffers; smem rows are padded by
+// 16 bytes so the fragment loads of a warp hit 32 distinct banks.
+// grid = (ceil(N / 32), ceil(M / BM)).
 // ---------------------------------------------------------------------------
 #define GQ_BM 64
 #define GQ_BN 32
@@ -302,13 +304,16 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], const int (&a)[4], int b0, i
                      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-template <int WT, int BM>
-__global__ __launch_bounds__(128) void gemm_q_mma_kernel(
+template <int WT, int BM, int WARPS>
+__global__ __launch_bounds__(32 * WARPS) void gemm_q_mma_kernel(
         const uint8_t * __restrict__ W, int N, int K, int rb,
         const int8_t * __restrict__ xq, const float * __restrict__ xd, const int * __restrict__ xs,
         int M, GemvEpi e) {
     constexpr int QB = WT == T3B_Q4_0 ? 16 : 32;          // weight bytes per block
-    constexpr int MT = BM / 32;                           // 16-row MMA tiles per warp (warps 2 x 2)
+    constexpr int MT = BM / 32;                           // 16-row MMA tiles per warp (2 warps along M)
+    constexpr int WN = WARPS / 2;                         // warps along N
+    constexpr int NT = GQ_BN / (8 * WN);                  // 8-column MMA tiles per warp
+    constexpr int NTHR = 32 * WARPS;
     constexpr int NS = BM == 32 ? 4 : 3;                  // cp.async stages in flight (static smem <= 48 KB)
     __shared__ __align__(16) int8_t As[NS][BM][GQ_AROW];
     __shared__ __align__(16) uint8_t Bs[NS][GQ_BN][GQ_BROW];
@@ -317,7 +322,7 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
     __shared__ __align__(16) __half Dw[NS][GQ_BN][GQ_KB];  // weight block scales
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int wm = warp >> 1, wn = warp & 1;
+    const int wm = warp / WN, wn = warp % WN;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * GQ_BN;
     const int nb = K / 32;
     const int nstage = nb / GQ_KB;
@@ -326,11 +331,13 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         const int kb = st * GQ_KB;                         // first block of the stage
         // activations: BM rows x 128 bytes = 8 BM chunks of 16 bytes
 #pragma unroll
-        for (int u = 0; u < BM / 16; ++u) {
-            const int c = tid + u * 128;
-            const int r = c >> 3, q = c & 7;
-            const bool ok = m0 + r < M;
-            cp_async16(&As[s][r][q * 16], xq + (size_t) (ok ? m0 + r : 0) * K + kb * 32 + q * 16, ok);
+        for (int u = 0; u < (8 * BM + NTHR - 1) / NTHR; ++u) {
+            const int c = tid + u * NTHR;
+            if (c < 8 * BM) {
+                const int r = c >> 3, q = c & 7;
+                const bool ok = m0 + r < M;
+                cp_async16(&As[s][r][q * 16], xq + (size_t) (ok ? m0 + r : 0) * K + kb * 32 + q * 16, ok);
+            }
         }
         // activation scales and sums: BM rows x 16 bytes each
         if (tid < BM) {
@@ -342,8 +349,8 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         // weights: 32 rows x (4 * QB) bytes
         constexpr int CPR = GQ_KB * QB / 16;              // chunks per row
 #pragma unroll
-        for (int u = 0; u < (GQ_BN * CPR + 127) / 128; ++u) {
-            const int c = tid + u * 128;
+        for (int u = 0; u < (GQ_BN * CPR + NTHR - 1) / NTHR; ++u) {
+            const int c = tid + u * NTHR;
             if (c < GQ_BN * CPR) {
                 const int r = c / CPR, q = c % CPR;
                 const bool ok = n0 + r < N;
@@ -358,11 +365,11 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    float acc[MT][2][4];
+    float acc[MT][NT][4];
 #pragma unroll
     for (int i = 0; i < MT; ++i)
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+        for (int j = 0; j < NT; ++j)
 #pragma unroll
             for (int k = 0; k < 4; ++k) acc[i][j][k] = 0.0f;
 
@@ -392,10 +399,10 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
                 a[mt][2] = *(const int *) &As[s][r][bb * 32 + 16 + t * 4];
                 a[mt][3] = *(const int *) &As[s][r + 8][bb * 32 + 16 + t * 4];
             }
-            int b[2][2];
+            int b[NT][2];
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                const int r = wn * 16 + nt * 8 + g;
+            for (int nt = 0; nt < NT; ++nt) {
+                const int r = wn * (8 * NT) + nt * 8 + g;
                 if (WT == T3B_Q4_0) {
                     // block byte j holds elements j (low nibble) and j + 16 (high)
                     const unsigned wv = *(const unsigned *) &Bs[s][r][bb * 16 + t * 4];
@@ -413,10 +420,10 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
                 int sx0 = 0, sx1 = 0;
                 if (WT == T3B_Q4_0) { sx0 = 8 * Ss[s][r0][bb]; sx1 = 8 * Ss[s][r0 + 8][bb]; }
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
+                for (int nt = 0; nt < NT; ++nt) {
                     int c[4];
                     mma_s8<WT>(c, a[mt], b[nt][0], b[nt][1]);
-                    const int cn = wn * 16 + nt * 8 + 2 * t;
+                    const int cn = wn * (8 * NT) + nt * 8 + 2 * t;
                     const float dw0 = __half2float(Dw[s][cn][bb]), dw1 = __half2float(Dw[s][cn + 1][bb]);
                     // c0, c1: row g, columns 2t, 2t+1; c2, c3: row g + 8
                     acc[mt][nt][0] = __fadd_rn(acc[mt][nt][0], __fmul_rn(__fmul_rn((float) (c[0] - sx0), dw0), dx0));
@@ -435,17 +442,17 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
+            for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int ml = wm * (16 * MT) + mt * 16 + g + (i >> 1) * 8;
-                    const int nl = wn * 16 + nt * 8 + 2 * t + (i & 1);
+                    const int nl = wn * (8 * NT) + nt * 8 + 2 * t + (i & 1);
                     const float b = e.bias ? e.bias[n0 + nl] : 0.0f;
                     Tt[ml][nl] = gelu_ggml(e.bias ? __fadd_rn(acc[mt][nt][i], b) : acc[mt][nt][i]);
                 }
         __syncthreads();
         const int nbk = e.qK / 32;
-        for (int ml = warp * (BM / 4); ml < warp * (BM / 4) + BM / 4; ++ml) {
+        for (int ml = warp * (BM / WARPS); ml < warp * (BM / WARPS) + BM / WARPS; ++ml) {
             const int m = m0 + ml;
             if (m >= M) break;   // uniform over the warp
             const float v = Tt[ml][lane];
@@ -469,10 +476,10 @@ __global__ __launch_bounds__(128) void gemm_q_mma_kernel(
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                Tt[wm * (16 * MT) + mt * 16 + g + (i >> 1) * 8][wn * 16 + nt * 8 + 2 * t + (i & 1)] = acc[mt][nt][i];
+                Tt[wm * (16 * MT) + mt * 16 + g + (i >> 1) * 8][wn * (8 * NT) + nt * 8 + 2 * t + (i & 1)] = acc[mt][nt][i];
     __syncthreads();
     const int rows = min(BM, M - m0);
 #pragma unroll 1

@@ -302,9 +302,11 @@ void launch_gemv_q(const Mat & W, const int8_t * xq, const float * xd, const int
         // 32-row tiles when 64-row ones would leave SMs idle (N = 1024: 64 CTAs at M = 128)
         const int tx = (W.N + GQ_BN - 1) / GQ_BN;
         if (tx * ((M + GQ_BM - 1) / GQ_BM) < 148) {
-            gemm_q_mma_kernel<WT, 32><<<dim3(tx, (M + 31) / 32), 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd, xs, M, e);
+            // eight warps (one 16 x 8 MMA tile each): with one CTA per SM,
+            // four warps left the schedulers idle between dependent steps
+            gemm_q_mma_kernel<WT, 32, 8><<<dim3(tx, (M + 31) / 32), 256, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd, xs, M, e);
         } else {
-            gemm_q_mma_kernel<WT, GQ_BM><<<dim3(tx, (M + GQ_BM - 1) / GQ_BM), 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd,
+            gemm_q_mma_kernel<WT, GQ_BM, 4><<<dim3(tx, (M + GQ_BM - 1) / GQ_BM), 128, 0, st>>>(W.p, W.N, W.K, W.rb, xq, xd,
                                                                                        xs, M, e);
         }
         return;
